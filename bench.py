@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""Benchmark: one causal RACE layer, forward + backward, tokens/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2|cfg3|cfg1]
+
+Workload (default cfg2 = BASELINE config 2, the metric's configuration):
+B=2, H=16, T=1,048,576 tokens per GPU, head_dim 64, L=16 tables x P=4
+hyperplanes (S=256 buckets), bf16 activations with fp32 state, inputs
+N(0,1)/8, planes from seed 0, eps 1e-6, logit scale 1/sqrt(64).  A step is one
+forward + backward of the layer through the public autograd op.  With N>1
+GPUs (torchrun), the ranks hold consecutive 1M-token slices of one
+N x 1M-token sequence (weak scaling, sequence-sharded with the NCCL
+prefix/suffix exchange).  Inputs (4.3 GB per tensor) exceed the 126 MB L2, so
+no flush is needed between steps.
+
+--impl reference times the reference's own CPU implementation of the path
+(its compiled OpenMP kernel kernels/cpu/race_pref.cpp + RaceCausalCPUFn glue +
+soft_hash_probs) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (B, H, T per rank, D, L, P, dtype, input scale)
+    "cfg1": (1, 8, 4096, 64, 8, 4, torch.float32, 1.0),
+    "cfg2": (2, 16, 1 << 20, 64, 16, 4, torch.bfloat16, 1.0 / 8.0),
+    "cfg3": (1, 8, 12582912, 64, 8, 4, torch.bfloat16, 1.0),
+}
+METRIC = "RACE layer fwd+bwd tokens/s (T=1M per GPU)"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock / throttle reasons via NVML during the timed region (read-only)."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown", 0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown", 0x0000000000000004: "sw_power_cap",
+    }
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.1)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def make_inputs(cfg, device, seed):
+    B, H, T, D, L, P, dtype, scale = cfg
+    g = torch.Generator(device=device).manual_seed(seed)
+    xs = []
+    for i in range(4):  # Q, K, V, dO
+        x = torch.randn(B, H, T, D, generator=g, device=device, dtype=torch.float32)
+        if i < 3:
+            x.mul_(scale)
+        xs.append(x.to(dtype))
+        del x
+    return xs
+
+
+def cpu_reference_sample(cfg, steps, warmup):
+    """Reference CPU path on a bounded sample of cfg: all heads, T_s tokens.
+
+    Returns (tok_per_s, meta).  One step = forward + backward of the sample."""
+    from oracle import ref_cpu
+    import race_attention_b200.race_common as rc
+    B, H, T, D, L, P, dtype, scale = cfg
+    torch.set_num_threads(os.cpu_count() or 1)
+    Ts = 1024 if L * (1 << P) >= 256 else 2048
+    g = torch.Generator().manual_seed(0)
+    Q, K, V, dO = (torch.randn(1, H, Ts, D, generator=g) for _ in range(4))
+    Q, K, V = Q * scale, K * scale, V * scale
+    planes, protos = rc.build_planes_protos(D, P, L, 1, device="cpu", seed=0)
+    kind = "reference" if ref_cpu.available() else "port"
+    if kind == "reference":
+        def step():
+            ref_cpu.layer_fwd_bwd(Q, K, V, dO, planes, protos, L, P)
+    else:
+        from oracle import oracle as O
+
+        def step():
+            O.race_qkv_fwd(Q, K, V, planes, L, P)
+            O.race_qkv_bwd(Q, K, V, dO, planes, L, P)
+    for _ in range(warmup):
+        step()
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        ts.append(time.perf_counter() - t0)
+    med = statistics.median(ts)
+    cores = torch.get_num_threads() if kind == "reference" else 1
+    meta = {"kind": kind, "cores": cores,
+            "sample": f"B=1 H={H} T={Ts} D={D} L={L} P={P} fp32 fwd+bwd (1/{B * T // Ts} of the tokens; "
+                      f"path is linear in T), median of {steps} after {warmup} warm-up, "
+                      f"{os.cpu_count()} host threads available",
+            "sec_per_step": med}
+    return Ts / med, meta
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    steps = max(1, min(args.steps, 5))
+    warm = 1
+    tps, meta = cpu_reference_sample(cfg, steps, warm)
+    line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warm, "ms_per_step": meta["sec_per_step"] * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": config_dict(args, cfg),
+            "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": meta["cores"], "kind": meta["kind"],
+                             "sample": meta["sample"]},
+            "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(args, cfg):
+    B, H, T, D, L, P, dtype, scale = cfg
+    return {"workload": f"{args.config}: single causal RACE layer fwd+bwd", "batch": B, "heads": H,
+            "tokens_per_gpu": T, "total_tokens": T * args.gpus, "head_dim": D, "tables_L": L, "planes_P": P,
+            "buckets_S": L << P, "dtype": str(dtype).replace("torch.", ""), "input_scale": scale,
+            "parallelism": f"seq{args.gpus}" if args.gpus > 1 else "single",
+            "l2_flush": "inputs larger than L2 (no flush)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (not a headline number)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    cfg = list(CONFIGS[args.config])
+    if args.config == "cfg3":
+        cfg[2] = cfg[2] // max(1, args.gpus)
+    if args.tokens:
+        cfg[2] = args.tokens
+    cfg = tuple(cfg)
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    return run_ours(args, cfg)
+
+
+def run_ours(args, cfg):
+    import torch.distributed as dist
+    import race_attention_b200 as rb
+    from race_attention_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    B, H, T, D, L, P, dtype, scale = cfg
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device=dev, seed=0)
+    Q, K, V, dO = make_inputs(cfg, dev, seed=1234 + rank)
+    qv, kv, vv = (x.detach().requires_grad_(True) for x in (Q, K, V))
+
+    def layer(q, k, v):
+        if world > 1:
+            return rb.race_causal_sharded(q, k, v, planes, L, P)
+        return rb.race_causal(q, k, v, planes, L, P)
+
+    ev_fwd = []
+    ev_bwd = []
+
+    def step(record=False):
+        for t in (qv, kv, vv):
+            t.grad = None
+        e0 = torch.cuda.Event(enable_timing=True) if record else None
+        e1 = torch.cuda.Event(enable_timing=True) if record else None
+        e2 = torch.cuda.Event(enable_timing=True) if record else None
+        if record:
+            e0.record()
+        out = layer(qv, kv, vv)
+        if record:
+            e1.record()
+        out.backward(dO)
+        if record:
+            e2.record()
+            ev_fwd.append((e0, e1))
+            ev_bwd.append((e1, e2))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    n0 = rb._lib.load().race_launch_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(record=True)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = (rb._lib.load().race_launch_counter() - n0) // args.steps
+    ms = start.elapsed_time(end) / args.steps
+    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_fwd)
+    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_bwd)
+    if world > 1:
+        t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, fwd_ms, bwd_ms = (float(x) for x in t.tolist())
+    tokens = B * T * world
+    value = tokens / (ms / 1e3)
+
+    # roofline of the dominant call (the fused backward, race_bwd_qkv): algorithmic bytes =
+    # read Q,K,V,dO + write dQ,dK,dV = 7*D*e per token-head
+    e = 2 if dtype == torch.bfloat16 else 4
+    hbm, tc, src = _peaks()
+    bwd_bytes = 7 * D * e * B * H * T
+    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
+    layer_bytes = 11 * D * e * B * H * T
+    roof = {"bound": "hbm", "kernel": "race_bwd_qkv (fused backward call)", "achieved": achieved, "peak": hbm,
+            "unit": "GB/s", "frac": achieved / hbm, "traffic": None, "peak_source": src,
+            "step_achieved": layer_bytes / (ms / 1e3) / 1e9, "step_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms}
+
+    # e2e: same step through the public API with host (pinned) buffers, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(layer, cfg, dev, world, barrier, args, planes)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tps, meta = cpu_reference_sample(cfg, 3, 1)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": meta["cores"], "kind": meta["kind"],
+               "sample": meta["sample"]}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
+                "data": "synthetic (seeded randn, BASELINE shapes)", "config": config_dict(args, cfg),
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(layer, cfg, dev, world, barrier, args, planes):
+    B, H, T, D, L, P, dtype, scale = cfg
+    steps = max(1, min(3, args.steps))
+    host_in = [torch.empty((B, H, T, D), dtype=dtype, pin_memory=True) for _ in range(4)]
+    host_out = [torch.empty((B, H, T, D), dtype=dtype, pin_memory=True) for _ in range(4)]
+    g = torch.Generator().manual_seed(7)
+    for h in host_in:
+        h.copy_(torch.randn(B, H, T, D, generator=g).mul_(scale).to(dtype))
+    nbytes = host_in[0].numel() * host_in[0].element_size()
+
+    def step():
+        q, k, v, do = (h.to(dev, non_blocking=True) for h in host_in)
+        for t in (q, k, v):
+            t.requires_grad_(True)
+        out = layer(q, k, v)
+        out.backward(do)
+        for src, dst in zip((out, q.grad, k.grad, v.grad), host_out):
+            dst.copy_(src.detach(), non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * nbytes,
+            "d2h_bytes_per_step": 4 * nbytes, "ms_per_step": ms, "steps": steps,
+            "api": "race_attention_b200.race_causal (autograd) from pinned host tensors"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,193 @@
+/*
+ * race_b200.h -- C ABI of the B200-native causal RACE attention operator.
+ *
+ * Plain pointers, sizes and an explicit cudaStream_t (passed as void*); no
+ * torch types.  Every entry point returns a status code (RACE_OK == 0) and
+ * never allocates: callers size the workspace with race_workspace_bytes().
+ * Launches go on the given stream and use the calling thread's current CUDA
+ * device (the library links the shared CUDA runtime, so a caller's
+ * cudaSetDevice / torch device guard applies).
+ *
+ * Notation: N independent streams (batch x heads), T tokens, D head_dim,
+ * L hash tables, P hyperplanes per table, R = 2^P corners, S = L*R buckets.
+ * Tensors are dense, row-major:
+ *   Q, K, V, out, dO, dQ, dK, dV : [N, T, D]           (dtype: RACE_F32/RACE_BF16)
+ *   probsK, probsQ, gradients    : [N, T, S]  float32  (bucket s = l*R + r)
+ *   planes_T                     : [D, L*P]   float32  (column l*P + p)
+ *   state A / B                  : [N, S] / [N, S, D] float32
+ * Bucket/corner order and plane layout are the reference's
+ * (scaling/race_common.py:14-33).  The math of every entry point is
+ *   out_t = sum_s pq[t,s] * B_t[s,:] / (A_t[s] + eps),
+ *   A_t = A0 + sum_{tau<=t} pk[tau,s],  B_t = B0 + sum_{tau<=t} pk[tau,s] V[tau,:]
+ * (scaling/race_common.py:76-90), with pq/pk the soft hash of Q/K
+ * (scaling/race_common.py:36-73): softmax over the R corners of
+ * sum_p tanh(x . planes_T[:, l*P+p]) * logit_scale * (+-1).
+ */
+#ifndef RACE_B200_H
+#define RACE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define RACE_OK 0
+#define RACE_ERR_ARG 1          /* NULL pointer or invalid scalar argument   */
+#define RACE_ERR_SHAPE 2        /* dimensions out of range / inconsistent    */
+#define RACE_ERR_DTYPE 3        /* dtype enum not supported                  */
+#define RACE_ERR_ALIGN 4        /* pointer alignment not met                 */
+#define RACE_ERR_WORKSPACE 5    /* workspace NULL or smaller than required   */
+#define RACE_ERR_CUDA 6         /* CUDA runtime / launch error               */
+#define RACE_ERR_TIMEOUT 7      /* a bounded device-side wait expired        */
+#define RACE_ERR_UNSUPPORTED 8  /* configuration has no kernel               */
+
+/* ---- dtypes of the [N,T,D] activations ------------------------------------ */
+#define RACE_F32 0
+#define RACE_BF16 1
+
+/* ---- operation ids for race_workspace_bytes ------------------------------ */
+#define RACE_OP_FWD_PROBS 0
+#define RACE_OP_BWD_PROBS 1
+#define RACE_OP_FWD_QKV 2
+#define RACE_OP_BWD_QKV 3
+#define RACE_OP_STATE 4
+#define RACE_OP_BWD_TOTALS 5
+
+/* Library ABI version (bumped on any signature change). */
+int race_abi_version(void);
+
+/* Human-readable text of a status code; race_last_error() gives the detail of
+ * the most recent failure on the calling thread (empty if none). */
+const char *race_status_string(int status);
+const char *race_last_error(void);
+
+/* Diagnostic: number of kernel launches this library has issued in this
+ * process (host-side counter; used to report launches per benchmark step). */
+unsigned long long race_launch_counter(void);
+
+/* Bytes of device workspace `op` needs for these sizes (pure host function).
+ * chunk <= 0 selects the library default. */
+int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D,
+                         int64_t L, int64_t P, int dtype, int64_t chunk,
+                         size_t *bytes);
+
+/* ---- probability-level operator -----------------------------------------
+ * Replaces race_fused_fwd (kernels/gpu/forward_kernel.cu:110-137), bound by
+ * pybind at kernels/gpu/race_cuda_binding.cpp:12-17.  out[N,T,D] fp32 is fully
+ * written (no pre-zeroing needed).  A_final/B_final may be NULL; otherwise they
+ * receive the state after the last token (race_prefix_ref's A_final/B_final,
+ * scaling/race_common.py:88-90). */
+int race_fwd_probs(const float *probsK, const float *probsQ, const float *V2,
+                   float *out, float *A_final, float *B_final,
+                   int64_t N, int64_t T, int64_t S, int64_t D,
+                   float eps, int64_t chunk,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/* Replaces race_backward (kernels/gpu/backward_kernels.cu:174-215), bound at
+ * kernels/gpu/race_cuda_binding.cpp:18-21: exact gradients w.r.t. probsK,
+ * probsQ and V2 for upstream grad_out. */
+int race_bwd_probs(const float *probsK, const float *probsQ, const float *V2,
+                   const float *grad_out,
+                   float *grad_probsK, float *grad_probsQ, float *grad_V2,
+                   int64_t N, int64_t T, int64_t S, int64_t D,
+                   float eps, int64_t chunk,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---- soft hash -------------------------------------------------------------
+ * Replaces the probability half of soft_hash_probs
+ * (scaling/race_common.py:36-73, share_planes layout): probs[N,T,S] fp32 of X. */
+int race_soft_hash(const void *X, int dtype, const float *planes_T, float *probs,
+                   int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                   float logit_scale, void *stream);
+
+/* Gradient of soft_hash_probs w.r.t. X (autograd of
+ * scaling/race_common.py:56-72): dX[N,T,D] (dtype) from dprobs[N,T,S] fp32. */
+int race_soft_hash_bwd(const void *X, int dtype, const float *planes_T,
+                       const float *dprobs, void *dX,
+                       int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                       float logit_scale, void *stream);
+
+/* ---- fused layer (soft hash + causal scan + readout) ---------------------
+ * Replaces RaceCausalCuda.forward (scaling/race_causal_cuda.py:94-102), i.e.
+ * soft_hash_probs + RaceCausalFn.forward without materialising the [N,T,S]
+ * probabilities.  A0/B0 (may be NULL = zero) is a carried-in state: the prefix
+ * of earlier sequence shards, or a decode cache.  A_final/B_final may be NULL. */
+int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype,
+                 const float *planes_T, void *out,
+                 const float *A0, const float *B0,
+                 float *A_final, float *B_final,
+                 int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                 float eps, float logit_scale,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/* Replaces RaceCausalFn.backward (scaling/race_causal_cuda.py:64-69) composed
+ * with the autograd of soft_hash_probs.  gA_in/gB_in (may be NULL) is the
+ * gradient reaching the final state from later sequence shards; dA0/dB0 (may
+ * be NULL) receive the gradient w.r.t. the carried-in state A0/B0. */
+int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO,
+                 int dtype, const float *planes_T,
+                 void *dQ, void *dK, void *dV,
+                 const float *A0, const float *B0,
+                 const float *gA_in, const float *gB_in,
+                 float *dA0, float *dB0,
+                 int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                 float eps, float logit_scale,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---- state / decode (no reference counterpart: the reference's KV-cache
+ * branch raises NotImplementedError, chat/nanochat/gpt.py:143-146) ---------- */
+
+/* Prefill -> decode-state handoff, and phase A of the sequence-sharded forward:
+ * A_out[N,S] = A0 + sum_t pk_t,  B_out[N,S,D] = B0 + sum_t pk_t V_t
+ * (race_prefix_ref's A_final/B_final, scaling/race_common.py:88-90).
+ * A0/B0 may be NULL. */
+int race_state_from_prefill(const void *K, const void *V, int dtype,
+                            const float *planes_T,
+                            const float *A0, const float *B0,
+                            float *A_out, float *B_out,
+                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                            float logit_scale,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
+/* One fused decode step for a batch of single tokens with grouped-query
+ * sharing: q[Nq,D], k/v[Nkv,D] (Nq = Nkv*group, q head i reads kv stream
+ * i/group).  Updates the persistent state A[Nkv,S], B[Nkv,S,D] in place with
+ * this token's key, then writes out[Nq,D] = row t of the layer output. */
+int race_decode_step(const void *q, const void *k, const void *v, int dtype,
+                     const float *planes_T, float *A, float *B, void *out,
+                     int64_t Nq, int64_t Nkv, int64_t D, int64_t L, int64_t P,
+                     float eps, float logit_scale, void *stream);
+
+/* ---- sequence-sharded phases (one rank's contiguous slice of T) ---------- */
+
+/* Forward phase A: this shard's state totals (== race_state_from_prefill with
+ * A0 = B0 = NULL).  Forward phase B is race_fwd_qkv with A0/B0 = the sum of
+ * the totals of all earlier shards. */
+int race_fwd_sharded_phaseA(const void *K, const void *V, int dtype,
+                            const float *planes_T, float *A_tot, float *B_tot,
+                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                            float logit_scale,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
+/* Backward phase A: this shard's gradient totals for its final state
+ *   gA_tot[N,S]   = sum_t -pq[t,s] * G_t[s] / (A_t[s] + eps)^2,
+ *                   G_t[s] = dO_t . B_t[s,:]
+ *   gB_tot[N,S,D] = sum_t pq[t,s] * dO_t / (A_t[s] + eps)
+ * given the carried-in forward prefix A0/B0.  Backward phase B is
+ * race_bwd_qkv with gA_in/gB_in = the sum of the totals of all later shards. */
+int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V,
+                            const void *dO, int dtype, const float *planes_T,
+                            const float *A0, const float *B0,
+                            float *gA_tot, float *gB_tot,
+                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                            float eps, float logit_scale,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RACE_B200_H */

@@ -1,0 +1,599 @@
+// race_api.cu -- extern "C" entry points of librace_b200.so (see include/race_b200.h).
+//
+// Host code only: argument validation, workspace carving and kernel dispatch.
+// Nothing here allocates device memory; launches go on the caller's stream.
+#include "race_b200.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <atomic>
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "decode.cuh"
+#include "generic.cuh"
+
+using race::align_up;
+namespace gen = race::gen;
+
+namespace {
+
+thread_local char g_err[512] = {0};
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = 0;
+  return RACE_OK;
+}
+
+std::atomic<unsigned long long> g_launches{0};
+
+int check_launch(const char *what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+constexpr int64_t kMaxN = 65535;
+constexpr int64_t kMaxS = 1024;
+constexpr int64_t kMaxT = (int64_t(1) << 31) - 1;
+
+int check_nts(int64_t N, int64_t T, int64_t S, int64_t D) {
+  if (N < 1 || N > kMaxN) return fail(RACE_ERR_SHAPE, "N=%lld out of range [1,%lld]", (long long)N, (long long)kMaxN);
+  if (T < 1 || T > kMaxT) return fail(RACE_ERR_SHAPE, "T=%lld out of range [1,2^31)", (long long)T);
+  if (S < 1 || S > kMaxS) return fail(RACE_ERR_SHAPE, "S=%lld out of range [1,%lld]", (long long)S, (long long)kMaxS);
+  if (D < 1 || D > gen::MAX_D) return fail(RACE_ERR_SHAPE, "D=%lld out of range [1,%d]", (long long)D, gen::MAX_D);
+  return RACE_OK;
+}
+
+int check_lp(int64_t L, int64_t P, int64_t *S) {
+  if (P < 1 || P > 10) return fail(RACE_ERR_SHAPE, "P=%lld out of range [1,10]", (long long)P);
+  if (L < 1 || (L << P) > kMaxS)
+    return fail(RACE_ERR_SHAPE, "L=%lld, P=%lld gives S=L*2^P outside [1,%lld]", (long long)L, (long long)P,
+                (long long)kMaxS);
+  *S = L << P;
+  return RACE_OK;
+}
+
+int check_dtype(int dtype) {
+  if (dtype != RACE_F32 && dtype != RACE_BF16) return fail(RACE_ERR_DTYPE, "dtype %d not supported", dtype);
+  return RACE_OK;
+}
+
+#define RACE_TRY(...)                 \
+  do {                                \
+    int _rc = (__VA_ARGS__);          \
+    if (_rc != RACE_OK) return _rc;   \
+  } while (0)
+
+#define RACE_NONNULL(p) \
+  if ((p) == nullptr) return fail(RACE_ERR_ARG, "%s must not be NULL", #p)
+
+// ---- workspace layout of the generic path ---------------------------------
+// Streams are processed in groups of `grp` so the workspace stays bounded
+// (kGroupBudget per group, at least one stream per group).
+struct Layout {
+  size_t pk = 0, pq = 0, dpk = 0, dpq = 0, st = 0, st2 = 0, total = 0;
+  int64_t grp = 1;
+};
+
+constexpr size_t kAlign = 256;
+constexpr size_t kGroupBudget = size_t(4) << 30;
+
+Layout layout_for(int op, int64_t n, int64_t T, int64_t S, int64_t D) {
+  const int64_t G = (T + gen::GC - 1) / gen::GC;
+  const size_t probs = sizeof(float) * (size_t)n * T * S;
+  const size_t states = sizeof(float) * (size_t)n * G * gen::state_elems((int)S, (int)D);
+  Layout w;
+  w.grp = n;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align_up(off + bytes, kAlign);
+    return at;
+  };
+  const bool qkv = op == RACE_OP_FWD_QKV || op == RACE_OP_BWD_QKV || op == RACE_OP_STATE || op == RACE_OP_BWD_TOTALS;
+  if (qkv) w.pk = take(probs);
+  if (op == RACE_OP_FWD_QKV || op == RACE_OP_BWD_QKV || op == RACE_OP_BWD_TOTALS) w.pq = take(probs);
+  if (op == RACE_OP_BWD_QKV) {
+    w.dpk = take(probs);
+    w.dpq = take(probs);
+  }
+  w.st = take(states);
+  if (op == RACE_OP_BWD_PROBS || op == RACE_OP_BWD_QKV || op == RACE_OP_BWD_TOTALS) w.st2 = take(states);
+  w.total = off;
+  return w;
+}
+
+Layout generic_layout(int op, int64_t N, int64_t T, int64_t S, int64_t D) {
+  const size_t per_stream = layout_for(op, 1, T, S, D).total;
+  int64_t grp = (int64_t)(kGroupBudget / (per_stream ? per_stream : 1));
+  if (grp < 1) grp = 1;
+  if (grp > N) grp = N;
+  return layout_for(op, grp, T, S, D);
+}
+
+int check_ws(void *ws, size_t have, size_t need) {
+  if (need == 0) return RACE_OK;
+  if (ws == nullptr) return fail(RACE_ERR_WORKSPACE, "workspace is NULL but %zu bytes are required", need);
+  if (have < need) return fail(RACE_ERR_WORKSPACE, "workspace has %zu bytes, %zu required", have, need);
+  if (reinterpret_cast<uintptr_t>(ws) % kAlign) return fail(RACE_ERR_ALIGN, "workspace must be %zu-byte aligned", kAlign);
+  return RACE_OK;
+}
+
+template <typename T>
+T *at(void *ws, size_t off) {
+  return reinterpret_cast<T *>(static_cast<char *>(ws) + off);
+}
+
+template <typename K>
+int set_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaFuncSetAttribute(%zu B smem): %s", bytes, cudaGetErrorString(e));
+  }
+  return RACE_OK;
+}
+
+gen::Dims make_dims(int64_t N, int64_t T, int64_t S, int64_t D, float eps) {
+  gen::Dims p;
+  p.N = (int)N;
+  p.T = (int)T;
+  p.S = (int)S;
+  p.D = (int)D;
+  p.G = (int)((T + gen::GC - 1) / gen::GC);
+  p.eps = eps;
+  return p;
+}
+
+// ---- generic building blocks ------------------------------------------------
+template <typename VT>
+int launch_totals(const float *pk, const VT *V, float *St, const gen::Dims &p, cudaStream_t s) {
+  const size_t sm = sizeof(float) * ((size_t)gen::GC * p.D + gen::GC * gen::GST);
+  RACE_TRY(set_smem(gen::fwd_totals<VT>, sm));
+  gen::fwd_totals<VT><<<dim3(p.G, p.N), gen::NT, sm, s>>>(pk, V, St, p);
+  return check_launch("fwd_totals");
+}
+
+int launch_scan(float *St, const float *initA, const float *initB, float *finA, float *finB, const gen::Dims &p,
+                int reverse, cudaStream_t s) {
+  const size_t E = gen::state_elems(p.S, p.D);
+  gen::chunk_scan<<<dim3((unsigned)((E + 255) / 256), p.N), 256, 0, s>>>(St, initA, initB, finA, finB, p.N, p.G, p.S,
+                                                                          p.D, reverse);
+  return check_launch("chunk_scan");
+}
+
+template <typename VT, typename OT>
+int launch_readout(const float *pk, const float *pq, const VT *V, const float *St, OT *out, const gen::Dims &p,
+                   cudaStream_t s) {
+  const size_t sm = gen::fwd_readout_smem(p.D);
+  RACE_TRY(set_smem(gen::fwd_readout<VT, OT>, sm));
+  gen::fwd_readout<VT, OT><<<dim3(p.G, p.N), gen::NT, sm, s>>>(pk, pq, V, St, out, p);
+  return check_launch("fwd_readout");
+}
+
+template <typename VT>
+int launch_bwd_totals(const float *pk, const float *pq, const VT *V, const VT *dO, const float *St, float *St2,
+                      float *dpq, const gen::Dims &p, cudaStream_t s) {
+  const size_t sm = sizeof(float) * gen::bwd_smem_floats(p.D, false);
+  RACE_TRY(set_smem(gen::bwd_totals<VT>, sm));
+  gen::bwd_totals<VT><<<dim3(p.G, p.N), gen::NT, sm, s>>>(pk, pq, V, dO, St, St2, dpq, p);
+  return check_launch("bwd_totals");
+}
+
+template <typename VT, typename OT>
+int launch_bwd_readout(const float *pk, const float *pq, const VT *V, const VT *dO, const float *St,
+                       const float *St2, float *dpk, OT *dV, const gen::Dims &p, cudaStream_t s) {
+  const size_t sm = sizeof(float) * gen::bwd_smem_floats(p.D, true);
+  RACE_TRY(set_smem(gen::bwd_readout<VT, OT>, sm));
+  gen::bwd_readout<VT, OT><<<dim3(p.G, p.N), gen::NT, sm, s>>>(pk, pq, V, dO, St, St2, dpk, dV, p);
+  return check_launch("bwd_readout");
+}
+
+template <typename XT>
+int launch_hash(const XT *X, const float *planes_T, float *probs, int64_t rows, int64_t D, int64_t L, int64_t P,
+                float scale, cudaStream_t s) {
+  const size_t sm = sizeof(float) * ((size_t)gen::HT * D + (size_t)gen::HT * L * P);
+  RACE_TRY(set_smem(gen::soft_hash_fwd<XT>, sm));
+  const unsigned grid = (unsigned)((rows + gen::HT - 1) / gen::HT);
+  gen::soft_hash_fwd<XT><<<grid, gen::NT, sm, s>>>(X, planes_T, probs, rows, (int)D, (int)L, (int)P, scale);
+  return check_launch("soft_hash_fwd");
+}
+
+template <typename XT>
+int launch_hash_bwd(const XT *X, const float *planes_T, const float *dprobs, XT *dX, int64_t rows, int64_t D,
+                    int64_t L, int64_t P, float scale, cudaStream_t s) {
+  const size_t sm = sizeof(float) * ((size_t)gen::HT * D + 2 * (size_t)gen::HT * L * P);
+  RACE_TRY(set_smem(gen::soft_hash_bwd<XT>, sm));
+  const unsigned grid = (unsigned)((rows + gen::HT - 1) / gen::HT);
+  gen::soft_hash_bwd<XT><<<grid, gen::NT, sm, s>>>(X, planes_T, dprobs, dX, rows, (int)D, (int)L, (int)P, scale);
+  return check_launch("soft_hash_bwd");
+}
+
+// ---- composite operations (templated on the activation dtype) -------------
+// Each loops over stream groups of w.grp streams (see generic_layout).
+template <typename T>
+T *off(T *p, size_t o) {
+  return p ? p + o : nullptr;
+}
+
+template <typename XT>
+int fwd_qkv_generic(const XT *Q, const XT *K, const XT *V, const float *planes_T, XT *out, const float *A0,
+                    const float *B0, float *Af, float *Bf, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                    float eps, float scale, void *ws, cudaStream_t s) {
+  const int64_t S = L << P;
+  const Layout w = generic_layout(RACE_OP_FWD_QKV, N, T, S, D);
+  float *pk = at<float>(ws, w.pk), *pq = at<float>(ws, w.pq), *St = at<float>(ws, w.st);
+  for (int64_t n0 = 0; n0 < N; n0 += w.grp) {
+    const int64_t nn = std::min(w.grp, N - n0);
+    const size_t xo = (size_t)n0 * T * D, so = (size_t)n0 * S, bo = (size_t)n0 * S * D;
+    const gen::Dims p = make_dims(nn, T, S, D, eps);
+    RACE_TRY(launch_hash<XT>(Q + xo, planes_T, pq, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_hash<XT>(K + xo, planes_T, pk, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_totals<XT>(pk, V + xo, St, p, s));
+    RACE_TRY(launch_scan(St, off(A0, so), off(B0, bo), off(Af, so), off(Bf, bo), p, 0, s));
+    RACE_TRY(launch_readout<XT, XT>(pk, pq, V + xo, St, out + xo, p, s));
+  }
+  return RACE_OK;
+}
+
+template <typename XT>
+int bwd_qkv_generic(const XT *Q, const XT *K, const XT *V, const XT *dO, const float *planes_T, XT *dQ, XT *dK,
+                    XT *dV, const float *A0, const float *B0, const float *gA, const float *gB, float *dA0,
+                    float *dB0, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps, float scale,
+                    void *ws, cudaStream_t s) {
+  const int64_t S = L << P;
+  const Layout w = generic_layout(RACE_OP_BWD_QKV, N, T, S, D);
+  float *pk = at<float>(ws, w.pk), *pq = at<float>(ws, w.pq), *dpk = at<float>(ws, w.dpk),
+        *dpq = at<float>(ws, w.dpq), *St = at<float>(ws, w.st), *St2 = at<float>(ws, w.st2);
+  for (int64_t n0 = 0; n0 < N; n0 += w.grp) {
+    const int64_t nn = std::min(w.grp, N - n0);
+    const size_t xo = (size_t)n0 * T * D, so = (size_t)n0 * S, bo = (size_t)n0 * S * D;
+    const gen::Dims p = make_dims(nn, T, S, D, eps);
+    RACE_TRY(launch_hash<XT>(Q + xo, planes_T, pq, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_hash<XT>(K + xo, planes_T, pk, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_totals<XT>(pk, V + xo, St, p, s));
+    RACE_TRY(launch_scan(St, off(A0, so), off(B0, bo), nullptr, nullptr, p, 0, s));
+    RACE_TRY(launch_bwd_totals<XT>(pk, pq, V + xo, dO + xo, St, St2, dpq, p, s));
+    RACE_TRY(launch_scan(St2, off(gA, so), off(gB, bo), off(dA0, so), off(dB0, bo), p, 1, s));
+    RACE_TRY(launch_bwd_readout<XT, XT>(pk, pq, V + xo, dO + xo, St, St2, dpk, dV + xo, p, s));
+    RACE_TRY(launch_hash_bwd<XT>(Q + xo, planes_T, dpq, dQ + xo, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_hash_bwd<XT>(K + xo, planes_T, dpk, dK + xo, nn * T, D, L, P, scale, s));
+  }
+  return RACE_OK;
+}
+
+template <typename XT>
+int state_generic(const XT *K, const XT *V, const float *planes_T, const float *A0, const float *B0, float *Ao,
+                  float *Bo, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float scale, void *ws,
+                  cudaStream_t s) {
+  const int64_t S = L << P;
+  const Layout w = generic_layout(RACE_OP_STATE, N, T, S, D);
+  float *pk = at<float>(ws, w.pk), *St = at<float>(ws, w.st);
+  for (int64_t n0 = 0; n0 < N; n0 += w.grp) {
+    const int64_t nn = std::min(w.grp, N - n0);
+    const size_t xo = (size_t)n0 * T * D, so = (size_t)n0 * S, bo = (size_t)n0 * S * D;
+    const gen::Dims p = make_dims(nn, T, S, D, 0.f);
+    RACE_TRY(launch_hash<XT>(K + xo, planes_T, pk, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_totals<XT>(pk, V + xo, St, p, s));
+    RACE_TRY(launch_scan(St, off(A0, so), off(B0, bo), Ao + so, Bo + bo, p, 0, s));
+  }
+  return RACE_OK;
+}
+
+template <typename XT>
+int bwd_totals_generic(const XT *Q, const XT *K, const XT *V, const XT *dO, const float *planes_T, const float *A0,
+                       const float *B0, float *gA, float *gB, int64_t N, int64_t T, int64_t D, int64_t L,
+                       int64_t P, float eps, float scale, void *ws, cudaStream_t s) {
+  const int64_t S = L << P;
+  const Layout w = generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D);
+  float *pk = at<float>(ws, w.pk), *pq = at<float>(ws, w.pq), *St = at<float>(ws, w.st), *St2 = at<float>(ws, w.st2);
+  for (int64_t n0 = 0; n0 < N; n0 += w.grp) {
+    const int64_t nn = std::min(w.grp, N - n0);
+    const size_t xo = (size_t)n0 * T * D, so = (size_t)n0 * S, bo = (size_t)n0 * S * D;
+    const gen::Dims p = make_dims(nn, T, S, D, eps);
+    RACE_TRY(launch_hash<XT>(Q + xo, planes_T, pq, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_hash<XT>(K + xo, planes_T, pk, nn * T, D, L, P, scale, s));
+    RACE_TRY(launch_totals<XT>(pk, V + xo, St, p, s));
+    RACE_TRY(launch_scan(St, off(A0, so), off(B0, bo), nullptr, nullptr, p, 0, s));
+    RACE_TRY(launch_bwd_totals<XT>(pk, pq, V + xo, dO + xo, St, St2, nullptr, p, s));
+    RACE_TRY(launch_scan(St2, nullptr, nullptr, gA + so, gB + bo, p, 1, s));
+  }
+  return RACE_OK;
+}
+
+cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+// ============================================================================
+extern "C" {
+
+int race_abi_version(void) { return 1; }
+
+const char *race_status_string(int status) {
+  switch (status) {
+    case RACE_OK: return "ok";
+    case RACE_ERR_ARG: return "invalid argument";
+    case RACE_ERR_SHAPE: return "invalid or unsupported shape";
+    case RACE_ERR_DTYPE: return "unsupported dtype";
+    case RACE_ERR_ALIGN: return "misaligned pointer";
+    case RACE_ERR_WORKSPACE: return "workspace missing or too small";
+    case RACE_ERR_CUDA: return "CUDA error";
+    case RACE_ERR_TIMEOUT: return "device-side wait timed out";
+    case RACE_ERR_UNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+  }
+}
+
+const char *race_last_error(void) { return g_err; }
+
+unsigned long long race_launch_counter(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int64_t L, int64_t P, int dtype,
+                         int64_t chunk, size_t *bytes) {
+  (void)chunk;
+  RACE_NONNULL(bytes);
+  *bytes = 0;
+  if (op == RACE_OP_FWD_QKV || op == RACE_OP_BWD_QKV || op == RACE_OP_STATE || op == RACE_OP_BWD_TOTALS) {
+    RACE_TRY(check_dtype(dtype));
+    RACE_TRY(check_lp(L, P, &S));
+  } else if (op != RACE_OP_FWD_PROBS && op != RACE_OP_BWD_PROBS) {
+    return fail(RACE_ERR_ARG, "unknown op %d", op);
+  }
+  RACE_TRY(check_nts(N, T, S, D));
+  *bytes = generic_layout(op, N, T, S, D).total;
+  return ok();
+}
+
+int race_fwd_probs(const float *probsK, const float *probsQ, const float *V2, float *out, float *A_final,
+                   float *B_final, int64_t N, int64_t T, int64_t S, int64_t D, float eps, int64_t chunk,
+                   void *workspace, size_t workspace_bytes, void *stream) {
+  (void)chunk;
+  RACE_NONNULL(probsK);
+  RACE_NONNULL(probsQ);
+  RACE_NONNULL(V2);
+  RACE_NONNULL(out);
+  RACE_TRY(check_nts(N, T, S, D));
+  const Layout w = generic_layout(RACE_OP_FWD_PROBS, N, T, S, D);
+  RACE_TRY(check_ws(workspace, workspace_bytes, w.total));
+  cudaStream_t s = as_stream(stream);
+  float *St = at<float>(workspace, w.st);
+  for (int64_t n0 = 0; n0 < N; n0 += w.grp) {
+    const int64_t nn = std::min(w.grp, N - n0);
+    const size_t po = (size_t)n0 * T * S, xo = (size_t)n0 * T * D, so = (size_t)n0 * S, bo = (size_t)n0 * S * D;
+    const gen::Dims p = make_dims(nn, T, S, D, eps);
+    RACE_TRY(launch_totals<float>(probsK + po, V2 + xo, St, p, s));
+    RACE_TRY(launch_scan(St, nullptr, nullptr, off(A_final, so), off(B_final, bo), p, 0, s));
+    RACE_TRY(launch_readout<float, float>(probsK + po, probsQ + po, V2 + xo, St, out + xo, p, s));
+  }
+  return ok();
+}
+
+int race_bwd_probs(const float *probsK, const float *probsQ, const float *V2, const float *grad_out,
+                   float *grad_probsK, float *grad_probsQ, float *grad_V2, int64_t N, int64_t T, int64_t S, int64_t D,
+                   float eps, int64_t chunk, void *workspace, size_t workspace_bytes, void *stream) {
+  (void)chunk;
+  RACE_NONNULL(probsK);
+  RACE_NONNULL(probsQ);
+  RACE_NONNULL(V2);
+  RACE_NONNULL(grad_out);
+  RACE_NONNULL(grad_probsK);
+  RACE_NONNULL(grad_probsQ);
+  RACE_NONNULL(grad_V2);
+  RACE_TRY(check_nts(N, T, S, D));
+  const Layout w = generic_layout(RACE_OP_BWD_PROBS, N, T, S, D);
+  RACE_TRY(check_ws(workspace, workspace_bytes, w.total));
+  cudaStream_t s = as_stream(stream);
+  float *St = at<float>(workspace, w.st), *St2 = at<float>(workspace, w.st2);
+  for (int64_t n0 = 0; n0 < N; n0 += w.grp) {
+    const int64_t nn = std::min(w.grp, N - n0);
+    const size_t po = (size_t)n0 * T * S, xo = (size_t)n0 * T * D;
+    const gen::Dims p = make_dims(nn, T, S, D, eps);
+    RACE_TRY(launch_totals<float>(probsK + po, V2 + xo, St, p, s));
+    RACE_TRY(launch_scan(St, nullptr, nullptr, nullptr, nullptr, p, 0, s));
+    RACE_TRY(launch_bwd_totals<float>(probsK + po, probsQ + po, V2 + xo, grad_out + xo, St, St2, grad_probsQ + po,
+                                      p, s));
+    RACE_TRY(launch_scan(St2, nullptr, nullptr, nullptr, nullptr, p, 1, s));
+    RACE_TRY(launch_bwd_readout<float, float>(probsK + po, probsQ + po, V2 + xo, grad_out + xo, St, St2,
+                                              grad_probsK + po, grad_V2 + xo, p, s));
+  }
+  return ok();
+}
+
+int race_soft_hash(const void *X, int dtype, const float *planes_T, float *probs, int64_t N, int64_t T, int64_t D,
+                   int64_t L, int64_t P, float logit_scale, void *stream) {
+  RACE_NONNULL(X);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(probs);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32)
+    RACE_TRY(launch_hash<float>((const float *)X, planes_T, probs, N * T, D, L, P, logit_scale, s));
+  else
+    RACE_TRY(launch_hash<__nv_bfloat16>((const __nv_bfloat16 *)X, planes_T, probs, N * T, D, L, P, logit_scale, s));
+  return ok();
+}
+
+int race_soft_hash_bwd(const void *X, int dtype, const float *planes_T, const float *dprobs, void *dX, int64_t N,
+                       int64_t T, int64_t D, int64_t L, int64_t P, float logit_scale, void *stream) {
+  RACE_NONNULL(X);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(dprobs);
+  RACE_NONNULL(dX);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32)
+    RACE_TRY(launch_hash_bwd<float>((const float *)X, planes_T, dprobs, (float *)dX, N * T, D, L, P, logit_scale, s));
+  else
+    RACE_TRY(launch_hash_bwd<__nv_bfloat16>((const __nv_bfloat16 *)X, planes_T, dprobs, (__nv_bfloat16 *)dX, N * T,
+                                            D, L, P, logit_scale, s));
+  return ok();
+}
+
+int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
+                 const float *A0, const float *B0, float *A_final, float *B_final, int64_t N, int64_t T, int64_t D,
+                 int64_t L, int64_t P, float eps, float logit_scale, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(out);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32)
+    RACE_TRY(fwd_qkv_generic<float>((const float *)Q, (const float *)K, (const float *)V, planes_T, (float *)out, A0,
+                                    B0, A_final, B_final, N, T, D, L, P, eps, logit_scale, workspace, s));
+  else
+    RACE_TRY(fwd_qkv_generic<__nv_bfloat16>((const __nv_bfloat16 *)Q, (const __nv_bfloat16 *)K,
+                                            (const __nv_bfloat16 *)V, planes_T, (__nv_bfloat16 *)out, A0, B0,
+                                            A_final, B_final, N, T, D, L, P, eps, logit_scale, workspace, s));
+  return ok();
+}
+
+int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                 void *dQ, void *dK, void *dV, const float *A0, const float *B0, const float *gA_in,
+                 const float *gB_in, float *dA0, float *dB0, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                 float eps, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(dO);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(dQ);
+  RACE_NONNULL(dK);
+  RACE_NONNULL(dV);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32)
+    RACE_TRY(bwd_qkv_generic<float>((const float *)Q, (const float *)K, (const float *)V, (const float *)dO, planes_T,
+                                    (float *)dQ, (float *)dK, (float *)dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, D,
+                                    L, P, eps, logit_scale, workspace, s));
+  else
+    RACE_TRY(bwd_qkv_generic<__nv_bfloat16>(
+        (const __nv_bfloat16 *)Q, (const __nv_bfloat16 *)K, (const __nv_bfloat16 *)V, (const __nv_bfloat16 *)dO,
+        planes_T, (__nv_bfloat16 *)dQ, (__nv_bfloat16 *)dK, (__nv_bfloat16 *)dV, A0, B0, gA_in, gB_in, dA0, dB0, N,
+        T, D, L, P, eps, logit_scale, workspace, s));
+  return ok();
+}
+
+int race_state_from_prefill(const void *K, const void *V, int dtype, const float *planes_T, const float *A0,
+                            const float *B0, float *A_out, float *B_out, int64_t N, int64_t T, int64_t D, int64_t L,
+                            int64_t P, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(A_out);
+  RACE_NONNULL(B_out);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_STATE, N, T, S, D).total));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32)
+    RACE_TRY(state_generic<float>((const float *)K, (const float *)V, planes_T, A0, B0, A_out, B_out, N, T, D, L, P,
+                                  logit_scale, workspace, s));
+  else
+    RACE_TRY(state_generic<__nv_bfloat16>((const __nv_bfloat16 *)K, (const __nv_bfloat16 *)V, planes_T, A0, B0,
+                                          A_out, B_out, N, T, D, L, P, logit_scale, workspace, s));
+  return ok();
+}
+
+int race_fwd_sharded_phaseA(const void *K, const void *V, int dtype, const float *planes_T, float *A_tot,
+                            float *B_tot, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float logit_scale,
+                            void *workspace, size_t workspace_bytes, void *stream) {
+  return race_state_from_prefill(K, V, dtype, planes_T, nullptr, nullptr, A_tot, B_tot, N, T, D, L, P, logit_scale,
+                                 workspace, workspace_bytes, stream);
+}
+
+int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                            const float *planes_T, const float *A0, const float *B0, float *gA_tot, float *gB_tot,
+                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps, float logit_scale,
+                            void *workspace, size_t workspace_bytes, void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(dO);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(gA_tot);
+  RACE_NONNULL(gB_tot);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total));
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32)
+    RACE_TRY(bwd_totals_generic<float>((const float *)Q, (const float *)K, (const float *)V, (const float *)dO,
+                                       planes_T, A0, B0, gA_tot, gB_tot, N, T, D, L, P, eps, logit_scale, workspace,
+                                       s));
+  else
+    RACE_TRY(bwd_totals_generic<__nv_bfloat16>((const __nv_bfloat16 *)Q, (const __nv_bfloat16 *)K,
+                                               (const __nv_bfloat16 *)V, (const __nv_bfloat16 *)dO, planes_T, A0, B0,
+                                               gA_tot, gB_tot, N, T, D, L, P, eps, logit_scale, workspace, s));
+  return ok();
+}
+
+int race_decode_step(const void *q, const void *k, const void *v, int dtype, const float *planes_T, float *A,
+                     float *B, void *out, int64_t Nq, int64_t Nkv, int64_t D, int64_t L, int64_t P, float eps,
+                     float logit_scale, void *stream) {
+  RACE_NONNULL(q);
+  RACE_NONNULL(k);
+  RACE_NONNULL(v);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(A);
+  RACE_NONNULL(B);
+  RACE_NONNULL(out);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  if (Nkv < 1 || Nkv > (int64_t(1) << 31) - 1) return fail(RACE_ERR_SHAPE, "Nkv=%lld out of range", (long long)Nkv);
+  if (Nq < Nkv || Nq % Nkv) return fail(RACE_ERR_SHAPE, "Nq=%lld must be a positive multiple of Nkv=%lld",
+                                        (long long)Nq, (long long)Nkv);
+  const int64_t group = Nq / Nkv;
+  if (group > race::dec::MAX_GROUP)
+    return fail(RACE_ERR_UNSUPPORTED, "query group %lld > %d", (long long)group, race::dec::MAX_GROUP);
+  if (D < 1 || D > race::dec::NT) return fail(RACE_ERR_SHAPE, "D=%lld out of range [1,%d]", (long long)D, race::dec::NT);
+  const size_t sm = sizeof(float) * race::dec::smem_floats((int)D, (int)S, (int)(L * P), (int)group);
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RACE_F32) {
+    RACE_TRY(set_smem(race::dec::decode_step<float>, sm));
+    race::dec::decode_step<float><<<(unsigned)Nkv, race::dec::NT, sm, s>>>(
+        (const float *)q, (const float *)k, (const float *)v, planes_T, A, B, (float *)out, (int)group, (int)D,
+        (int)L, (int)P, eps, logit_scale);
+  } else {
+    RACE_TRY(set_smem(race::dec::decode_step<__nv_bfloat16>, sm));
+    race::dec::decode_step<__nv_bfloat16><<<(unsigned)Nkv, race::dec::NT, sm, s>>>(
+        (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, planes_T, A, B,
+        (__nv_bfloat16 *)out, (int)group, (int)D, (int)L, (int)P, eps, logit_scale);
+  }
+  RACE_TRY(check_launch("decode_step"));
+  return ok();
+}
+
+}  // extern "C"

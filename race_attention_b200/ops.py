@@ -1,0 +1,281 @@
+"""Torch-level calls into the C ABI (no autograd here; see race_causal_cuda.py).
+
+Each function validates its tensors the way the reference extension does
+(CUDA-only, dtype, rank -> RuntimeError, kernels/gpu/forward_kernel.cu:112-114,
+kernels/gpu/backward_kernels.cu:176-179), allocates outputs and workspace with
+torch on the inputs' device, and launches on torch's current stream under a
+device guard.  torch is only plumbing here: memory, streams and devices.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.RACE_F32, torch.bfloat16: _lib.RACE_BF16}
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _check_cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("CUDA only")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+    return dev
+
+
+def _dtype_code(t):
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise RuntimeError(f"unsupported dtype {t.dtype} (float32 or bfloat16)") from None
+
+
+def _workspace(op, N, T, S, D, L, P, dtype, dev):
+    lib = _lib.load()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.race_workspace_bytes(op, N, T, S, D, L, P, dtype, 0, ctypes.byref(nbytes)),
+               "race_workspace_bytes")
+    n = int(nbytes.value)
+    return torch.empty(max(n, 1), dtype=torch.uint8, device=dev), n
+
+
+def _as_ntd(x, name):
+    if x.dim() == 4:
+        x = x.reshape(-1, x.shape[2], x.shape[3])
+    if x.dim() != 3:
+        raise RuntimeError(f"{name} must be [N,T,D] or [B,H,T,D]")
+    return x.contiguous()
+
+
+def _opt_state(A, B, N, S, D, dev):
+    if A is None and B is None:
+        return None, None
+    if A is None or B is None:
+        raise RuntimeError("state A and B must be given together")
+    A = A.to(device=dev, dtype=torch.float32).reshape(N, S).contiguous()
+    B = B.to(device=dev, dtype=torch.float32).reshape(N, S, D).contiguous()
+    return A, B
+
+
+def default_logit_scale(D: int) -> float:
+    """The reference divides tanh(proj) by sqrt(D) (scaling/race_common.py:46,68)."""
+    return 1.0 / math.sqrt(D)
+
+
+# ---------------------------------------------------------------------------
+# probability-level (reference extension surface)
+def race_fused_fwd(probsK, probsQ, V2, eps, chunk=0, return_state=False):
+    """out[N,T,D] = causal RACE forward (kernels/gpu/forward_kernel.cu:110 semantics)."""
+    dev = _check_cuda(probsK, probsQ, V2)
+    if probsK.dtype != torch.float32 or probsQ.dtype != torch.float32 or V2.dtype != torch.float32:
+        raise RuntimeError("fp32 only")
+    if probsK.dim() != 3 or probsQ.dim() != 3 or V2.dim() != 3:
+        raise RuntimeError("shapes [N,T,S],[N,T,S],[N,T,D]")
+    probsK, probsQ, V2 = probsK.contiguous(), probsQ.contiguous(), V2.contiguous()
+    N, T, S = probsK.shape
+    D = V2.shape[2]
+    if probsQ.shape != probsK.shape or V2.shape[:2] != probsK.shape[:2]:
+        raise RuntimeError("shapes [N,T,S],[N,T,S],[N,T,D]")
+    out = torch.empty((N, T, D), dtype=torch.float32, device=dev)
+    Af = torch.empty((N, S), dtype=torch.float32, device=dev) if return_state else None
+    Bf = torch.empty((N, S, D), dtype=torch.float32, device=dev) if return_state else None
+    if T == 0:
+        if return_state:
+            Af.zero_()
+            Bf.zero_()
+        return (out, Af, Bf) if return_state else out
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_FWD_PROBS, N, T, S, D, 0, 0, 0, dev)
+        _lib.check(lib.race_fwd_probs(_ptr(probsK), _ptr(probsQ), _ptr(V2), _ptr(out), _ptr(Af), _ptr(Bf),
+                                      N, T, S, D, float(eps), int(chunk), _ptr(ws), nb, _stream(dev)),
+                   "race_fwd_probs")
+    return (out, Af, Bf) if return_state else out
+
+
+def race_backward(probsK, probsQ, V2, grad_out, eps, chunk=0):
+    """[gradProbsK, gradProbsQ, gradV] (kernels/gpu/backward_kernels.cu:174 semantics)."""
+    dev = _check_cuda(probsK, probsQ, V2, grad_out)
+    for t in (probsK, probsQ, V2, grad_out):
+        if t.dtype != torch.float32:
+            raise RuntimeError("fp32 only")
+    probsK, probsQ, V2, grad_out = (t.contiguous() for t in (probsK, probsQ, V2, grad_out))
+    N, T, S = probsK.shape
+    D = V2.shape[2]
+    if S > 1024:
+        raise RuntimeError("S must be <= 1024")
+    gpk = torch.empty_like(probsK)
+    gpq = torch.empty_like(probsQ)
+    gv = torch.empty_like(V2)
+    if T == 0:
+        return [gpk, gpq, gv]
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_BWD_PROBS, N, T, S, D, 0, 0, 0, dev)
+        _lib.check(lib.race_bwd_probs(_ptr(probsK), _ptr(probsQ), _ptr(V2), _ptr(grad_out), _ptr(gpk), _ptr(gpq),
+                                      _ptr(gv), N, T, S, D, float(eps), int(chunk), _ptr(ws), nb, _stream(dev)),
+                   "race_bwd_probs")
+    return [gpk, gpq, gv]
+
+
+# ---------------------------------------------------------------------------
+# soft hash
+def soft_hash(X, planes_T, L, P, logit_scale=None):
+    """probs[N,T,L*2^P] fp32 of X [N,T,D] (bf16 or fp32)."""
+    dev = _check_cuda(X, planes_T)
+    X = _as_ntd(X, "X")
+    N, T, D = X.shape
+    S = L << P
+    planes_T = planes_T.to(torch.float32).contiguous()
+    if planes_T.shape != (D, L * P):
+        raise RuntimeError(f"planes_T must be [D, L*P] = [{D}, {L * P}]")
+    scale = default_logit_scale(D) if logit_scale is None else float(logit_scale)
+    probs = torch.empty((N, T, S), dtype=torch.float32, device=dev)
+    if N * T == 0:
+        return probs
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.race_soft_hash(_ptr(X), _dtype_code(X), _ptr(planes_T), _ptr(probs), N, T, D, L, P, scale,
+                                      _stream(dev)), "race_soft_hash")
+    return probs
+
+
+def soft_hash_bwd(X, planes_T, dprobs, L, P, logit_scale=None):
+    dev = _check_cuda(X, planes_T, dprobs)
+    X = _as_ntd(X, "X")
+    N, T, D = X.shape
+    planes_T = planes_T.to(torch.float32).contiguous()
+    dprobs = dprobs.to(torch.float32).reshape(N, T, L << P).contiguous()
+    scale = default_logit_scale(D) if logit_scale is None else float(logit_scale)
+    dX = torch.empty_like(X)
+    if N * T == 0:
+        return dX
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.race_soft_hash_bwd(_ptr(X), _dtype_code(X), _ptr(planes_T), _ptr(dprobs), _ptr(dX), N, T, D,
+                                          L, P, scale, _stream(dev)), "race_soft_hash_bwd")
+    return dX
+
+
+# ---------------------------------------------------------------------------
+# fused layer
+def _qkv_common(Q, K, V, planes_T, L, P, logit_scale):
+    dev = _check_cuda(Q, K, V, planes_T)
+    Q, K, V = _as_ntd(Q, "Q"), _as_ntd(K, "K"), _as_ntd(V, "V")
+    if not (Q.shape == K.shape == V.shape):
+        raise RuntimeError("Q, K, V must have the same shape")
+    if not (Q.dtype == K.dtype == V.dtype):
+        raise RuntimeError("Q, K, V must have the same dtype")
+    N, T, D = Q.shape
+    planes_T = planes_T.to(torch.float32).contiguous()
+    if planes_T.shape != (D, L * P):
+        raise RuntimeError(f"planes_T must be [D, L*P] = [{D}, {L * P}]")
+    scale = default_logit_scale(D) if logit_scale is None else float(logit_scale)
+    return dev, Q, K, V, planes_T, N, T, D, L << P, scale
+
+
+def fwd_qkv(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None, return_state=False):
+    """Fused soft hash + causal scan + readout; out has Q's dtype and [N,T,D] shape."""
+    dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
+    A0, B0 = _opt_state(A0, B0, N, S, D, dev)
+    out = torch.empty_like(Q)
+    Af = torch.empty((N, S), dtype=torch.float32, device=dev) if return_state else None
+    Bf = torch.empty((N, S, D), dtype=torch.float32, device=dev) if return_state else None
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_FWD_QKV, N, T, S, D, L, P, _dtype_code(Q), dev)
+        _lib.check(lib.race_fwd_qkv(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out), _ptr(A0),
+                                    _ptr(B0), _ptr(Af), _ptr(Bf), N, T, D, L, P, float(eps), scale, _ptr(ws), nb,
+                                    _stream(dev)), "race_fwd_qkv")
+    return (out, Af, Bf) if return_state else out
+
+
+def bwd_qkv(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None, gA=None, gB=None,
+            return_state_grad=False):
+    """(dQ, dK, dV[, dA0, dB0]) of the fused layer."""
+    dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
+    dO = _as_ntd(dO, "dO").to(Q.dtype)
+    A0, B0 = _opt_state(A0, B0, N, S, D, dev)
+    gA, gB = _opt_state(gA, gB, N, S, D, dev)
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    dA0 = torch.empty((N, S), dtype=torch.float32, device=dev) if return_state_grad else None
+    dB0 = torch.empty((N, S, D), dtype=torch.float32, device=dev) if return_state_grad else None
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_BWD_QKV, N, T, S, D, L, P, _dtype_code(Q), dev)
+        _lib.check(lib.race_bwd_qkv(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T), _ptr(dQ),
+                                    _ptr(dK), _ptr(dV), _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), _ptr(dA0), _ptr(dB0),
+                                    N, T, D, L, P, float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_bwd_qkv")
+    return (dQ, dK, dV, dA0, dB0) if return_state_grad else (dQ, dK, dV)
+
+
+def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None):
+    """(A[N,S], B[N,S,D]) fp32 state after the prefill tokens K, V [N,T,D]."""
+    dev, K, _, V, planes_T, N, T, D, S, scale = _qkv_common(K, K, V, planes_T, L, P, logit_scale)
+    A0, B0 = _opt_state(A0, B0, N, S, D, dev)
+    A = torch.empty((N, S), dtype=torch.float32, device=dev)
+    B = torch.empty((N, S, D), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_STATE, N, T, S, D, L, P, _dtype_code(K), dev)
+        _lib.check(lib.race_state_from_prefill(_ptr(K), _ptr(V), _dtype_code(K), _ptr(planes_T), _ptr(A0), _ptr(B0),
+                                               _ptr(A), _ptr(B), N, T, D, L, P, scale, _ptr(ws), nb, _stream(dev)),
+                   "race_state_from_prefill")
+    return A, B
+
+
+def bwd_totals(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None):
+    """(gA_tot[N,S], gB_tot[N,S,D]): this shard's final-state gradient totals."""
+    dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
+    dO = _as_ntd(dO, "dO").to(Q.dtype)
+    A0, B0 = _opt_state(A0, B0, N, S, D, dev)
+    gA = torch.empty((N, S), dtype=torch.float32, device=dev)
+    gB = torch.empty((N, S, D), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_BWD_TOTALS, N, T, S, D, L, P, _dtype_code(Q), dev)
+        _lib.check(lib.race_bwd_sharded_phaseA(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T),
+                                               _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), N, T, D, L, P, float(eps),
+                                               scale, _ptr(ws), nb, _stream(dev)), "race_bwd_sharded_phaseA")
+    return gA, gB
+
+
+def decode_step(q, k, v, planes_T, A, B, L, P, eps=1e-6, logit_scale=None):
+    """One decode token.  q [Nq,D], k/v [Nkv,D] (Nq = group*Nkv); updates A/B in place; returns out [Nq,D]."""
+    dev = _check_cuda(q, k, v, planes_T, A, B)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if not (q.dtype == k.dtype == v.dtype):
+        raise RuntimeError("q, k, v must have the same dtype")
+    Nq, D = q.shape
+    Nkv = k.shape[0]
+    S = L << P
+    if A.dtype != torch.float32 or B.dtype != torch.float32 or not A.is_contiguous() or not B.is_contiguous():
+        raise RuntimeError("decode state A/B must be contiguous float32")
+    if A.shape != (Nkv, S) or B.shape != (Nkv, S, D):
+        raise RuntimeError(f"decode state must be A[{Nkv},{S}], B[{Nkv},{S},{D}]")
+    planes_T = planes_T.to(torch.float32).contiguous()
+    scale = default_logit_scale(D) if logit_scale is None else float(logit_scale)
+    out = torch.empty_like(q)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.race_decode_step(_ptr(q), _ptr(k), _ptr(v), _dtype_code(q), _ptr(planes_T), _ptr(A), _ptr(B),
+                                        _ptr(out), Nq, Nkv, D, L, P, float(eps), scale, _stream(dev)),
+                   "race_decode_step")
+    return out

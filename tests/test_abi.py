@@ -1,0 +1,91 @@
+"""The C ABI library loads and exports every entry point include/race_b200.h
+declares; host-side validation returns the documented status codes before any
+CUDA call (so these run without a GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from race_attention_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "race_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(race_\w+)\s*\(", src, flags=re.M)))
+
+
+def status_codes():
+    src = open(HEADER).read()
+    return {k: int(v) for k, v in re.findall(r"#define (RACE_(?:OK|ERR_\w+))\s+(\d+)", src)}
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in race_b200.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert lib.race_abi_version() == 1
+
+
+def test_status_strings():
+    lib = _lib.load()
+    for name, code in status_codes().items():
+        s = lib.race_status_string(code).decode()
+        assert s and s != "unknown status", name
+
+
+def test_workspace_query_is_host_only():
+    lib = _lib.load()
+    nb = ctypes.c_size_t(0)
+    # config-1 shape, fused forward fp32
+    rc = lib.race_workspace_bytes(_lib.OP_FWD_QKV, 8, 4096, 0, 64, 8, 4, _lib.RACE_F32, 0, ctypes.byref(nb))
+    assert rc == 0 and nb.value > 0
+    rc = lib.race_workspace_bytes(_lib.OP_BWD_PROBS, 2, 1024, 64, 64, 0, 0, 0, 0, ctypes.byref(nb))
+    assert rc == 0 and nb.value > 0
+    # bad op / bad dtype
+    assert lib.race_workspace_bytes(99, 1, 1, 1, 1, 1, 1, 0, 0, ctypes.byref(nb)) == status_codes()["RACE_ERR_ARG"]
+    assert lib.race_workspace_bytes(_lib.OP_FWD_QKV, 1, 1, 0, 8, 1, 1, 7, 0, ctypes.byref(nb)) == \
+        status_codes()["RACE_ERR_DTYPE"]
+
+
+@pytest.mark.parametrize("N,T,S,D,code", [
+    (0, 8, 8, 8, "RACE_ERR_SHAPE"),
+    (1, 0, 8, 8, "RACE_ERR_SHAPE"),
+    (1, 8, 1025, 8, "RACE_ERR_SHAPE"),
+    (1, 8, 8, 257, "RACE_ERR_SHAPE"),
+    (1, 8, 8, 8, "RACE_ERR_WORKSPACE"),
+])
+def test_fwd_probs_validation(N, T, S, D, code):
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    rc = lib.race_fwd_probs(p, p, p, p, None, None, N, T, S, D, 1e-6, 0, None, 0, None)
+    assert rc == status_codes()[code]
+    assert lib.race_last_error().decode()
+
+
+def test_null_pointer_rejected():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    rc = lib.race_fwd_probs(None, p, p, p, None, None, 1, 8, 8, 8, 1e-6, 0, None, 0, None)
+    assert rc == status_codes()["RACE_ERR_ARG"]
+    assert "probsK" in lib.race_last_error().decode()
+
+
+def test_decode_validation():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    codes = status_codes()
+    # Nq not a multiple of Nkv
+    assert lib.race_decode_step(p, p, p, 0, p, p, p, p, 5, 2, 64, 8, 4, 1e-6, 0.125, None) == codes["RACE_ERR_SHAPE"]
+    # P out of range
+    assert lib.race_decode_step(p, p, p, 0, p, p, p, p, 4, 2, 64, 8, 11, 1e-6, 0.125, None) == codes["RACE_ERR_SHAPE"]
+    # group too large
+    assert lib.race_decode_step(p, p, p, 0, p, p, p, p, 64, 2, 64, 8, 4, 1e-6, 0.125, None) == \
+        codes["RACE_ERR_UNSUPPORTED"]

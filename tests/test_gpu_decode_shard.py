@@ -1,0 +1,84 @@
+"""Decode step, prefill->state handoff and sequence-shard phases vs the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from conftest import relerr
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
+@pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 2)])
+def test_prefill_then_decode(dtype, tol, Hq, Hkv):
+    import race_attention_b200 as rb
+    B, T0, steps, D, L, P = 3, 40, 6, 64, 8, 4
+    g = torch.Generator().manual_seed(Hq * 10 + Hkv)
+    T = T0 + steps
+    Q = torch.randn(B, Hq, T, D, generator=g).to(dtype)
+    K = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    V = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device="cpu", seed=1)
+    grp = Hq // Hkv
+    Ke, Ve = K.repeat_interleave(grp, 1), V.repeat_interleave(grp, 1)
+    ref, _, _ = O.race_qkv_fwd(Q, Ke, Ve, planes, L, P)  # [B*Hq, T, D]
+    ref = ref.reshape(B, Hq, T, D)
+    out0, st = rb.prefill_with_state(Q[:, :, :T0].cuda(), K[:, :, :T0].cuda(), V[:, :, :T0].cuda(),
+                                     planes.cuda(), L, P)
+    assert relerr(out0, ref[:, :, :T0]) < tol
+    _, Ar, Br = O.race_qkv_fwd(K[:, :, :T0], K[:, :, :T0], V[:, :, :T0], planes, L, P)
+    assert relerr(st.A, Ar) < 1e-5 and relerr(st.B, Br) < max(tol, 1e-5)
+    for t in range(T0, T):
+        o = st.step(Q[:, :, t].cuda(), K[:, :, t].cuda(), V[:, :, t].cuda())
+        assert relerr(o, ref[:, :, t]) < tol, t
+    assert st.tokens == T
+
+
+def test_state_from_prefill_with_initial_state():
+    import race_attention_b200 as rb
+    g = torch.Generator().manual_seed(0)
+    K, V = torch.randn(4, 100, 32, generator=g), torch.randn(4, 100, 32, generator=g)
+    planes = torch.randn(32, 12, generator=g)
+    A1, B1 = rb.ops.state_from_prefill(K[:, :60].cuda(), V[:, :60].cuda(), planes.cuda(), 4, 3)
+    A2, B2 = rb.ops.state_from_prefill(K[:, 60:].cuda(), V[:, 60:].cuda(), planes.cuda(), 4, 3, None, A1, B1)
+    _, Ar, Br = O.race_qkv_fwd(K, K, V, planes, 4, 3)
+    assert relerr(A2, Ar) < 1e-5 and relerr(B2, Br) < 1e-5
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
+def test_sequence_shard_phases_emulated(world, dtype, tol):
+    """W ranks emulated on one GPU: phase A totals -> host prefix/suffix sums ->
+    phase B; the concatenation equals the single-run result (oracle)."""
+    import race_attention_b200 as rb
+    N, T, D, L, P = 4, 333, 64, 8, 4
+    g = torch.Generator().manual_seed(world)
+    Q, K, V, dO = (torch.randn(N, T, D, generator=g).to(dtype) for _ in range(4))
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device="cpu", seed=0)
+    pc = planes.cuda()
+    bounds = np.linspace(0, T, world + 1).astype(int)
+    sl = [slice(bounds[r], bounds[r + 1]) for r in range(world)]
+    c = lambda x, r: x[:, sl[r]].cuda().contiguous()  # noqa: E731
+    tots = [rb.ops.state_from_prefill(c(K, r), c(V, r), pc, L, P) for r in range(world)]
+    pref = []
+    for r in range(world):
+        A = sum((tots[i][0].double() for i in range(r)), torch.zeros_like(tots[0][0], dtype=torch.float64))
+        B = sum((tots[i][1].double() for i in range(r)), torch.zeros_like(tots[0][1], dtype=torch.float64))
+        pref.append((A.float(), B.float()))
+    outs = [rb.ops.fwd_qkv(c(Q, r), c(K, r), c(V, r), pc, L, P, A0=pref[r][0], B0=pref[r][1]) for r in range(world)]
+    gt = [rb.ops.bwd_totals(c(Q, r), c(K, r), c(V, r), c(dO, r), pc, L, P, A0=pref[r][0], B0=pref[r][1])
+          for r in range(world)]
+    grads = []
+    for r in range(world):
+        gA = sum((gt[i][0].double() for i in range(r + 1, world)), torch.zeros_like(gt[0][0], dtype=torch.float64))
+        gB = sum((gt[i][1].double() for i in range(r + 1, world)), torch.zeros_like(gt[0][1], dtype=torch.float64))
+        grads.append(rb.ops.bwd_qkv(c(Q, r), c(K, r), c(V, r), c(dO, r), pc, L, P, A0=pref[r][0], B0=pref[r][1],
+                                    gA=gA.float(), gB=gB.float()))
+    out_r, _, _ = O.race_qkv_fwd(Q, K, V, planes, L, P)
+    dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, L, P)
+    cat = lambda xs: torch.cat([x.float().cpu() for x in xs], 1)  # noqa: E731
+    assert relerr(cat(outs), out_r) < tol
+    assert relerr(cat([x[0] for x in grads]), dQ_r) < tol
+    assert relerr(cat([x[1] for x in grads]), dK_r) < tol
+    assert relerr(cat([x[2] for x in grads]), dV_r) < tol

@@ -1,0 +1,131 @@
+"""Fused layer (soft hash + scan + readout, forward and backward) vs the oracle
+and vs the reference's own outputs (golden), fp32 and bf16."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from conftest import close, relerr
+
+pytestmark = pytest.mark.gpu
+
+
+def qkv(B, H, T, D, seed, scale=1.0, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    Q, K, V, dO = (torch.randn(B, H, T, D, generator=g) for _ in range(4))
+    Q, K, V = Q * scale, K * scale, V * scale
+    return [x.to(dtype) for x in (Q, K, V, dO)]
+
+
+def test_golden_module_cases(golden):
+    """RaceCausalCuda vs the reference's RaceCumsumCausal outputs and grads
+    (scaling/test_kernels.py:107-129 tolerances: out 2e-5, grads 2e-3)."""
+    import race_attention_b200 as rb
+    for i, c in enumerate(golden["e2e_cases"]):
+        B, H, T, D, kb, L, M, share, seed = (int(x) for x in c)
+        g = lambda k: torch.from_numpy(golden[f"e2e{i}_{k}"]).cuda()  # noqa: E731
+        mod = rb.RaceCausalCuda(D, kb, L, M, device="cuda", share_planes=bool(share), seed=seed)
+        assert torch.equal(mod.planes_T, g("planes_T"))
+        q, k, v = (g(n).clone().requires_grad_(True) for n in ("Q", "K", "V"))
+        out = mod(q, k, v)
+        (out * g("dO")).sum().backward()
+        assert close(out, g("out"), 2e-5)[0], (i, relerr(out, g("out")))
+        for n, t in (("dQ", q), ("dK", k), ("dV", v)):
+            assert close(t.grad, g(n), 2e-3)[0], (i, n, relerr(t.grad, g(n)))
+
+
+def test_soft_hash_matches_reference(golden):
+    import race_attention_b200 as rb
+    for i, (B, H, T, D, kb, L, seed) in enumerate(golden["hash_cases"]):
+        pT = torch.from_numpy(golden[f"hash{i}_planes_T"]).cuda()
+        for X, ref in (("Q", "probsQ"), ("K", "probsK")):
+            x = torch.from_numpy(golden[f"hash{i}_{X}"]).cuda()
+            p = rb.ops.soft_hash(x, pT, int(L), int(kb))
+            assert (p.cpu() - torch.from_numpy(golden[f"hash{i}_{ref}"])).abs().max() < 1e-6
+
+
+def test_soft_hash_grad():
+    import race_attention_b200 as rb
+    g = torch.Generator().manual_seed(5)
+    X = torch.randn(3, 40, 64, generator=g)
+    planes = torch.randn(64, 32, generator=g)
+    dp = torch.randn(3, 40, 128, generator=g)
+    dX = rb.ops.soft_hash_bwd(X.cuda(), planes.cuda(), dp.cuda(), 8, 4)
+    ref = O.soft_hash_bwd(X, planes, 8, 4, dp)
+    assert relerr(dX, ref) < 1e-5
+
+
+@pytest.mark.parametrize("T", [1, 2, 7, 33, 512, 4096])
+def test_fp32_config1_shape(T):
+    """BASELINE config 1 geometry (H=8, D=64, L=8, P=4, seed-0 planes), fp32:
+    north-star tolerance rel 1e-4 on the output and all gradients."""
+    import race_attention_b200 as rb
+    Q, K, V, dO = qkv(1, 8, T, 64, seed=T)
+    planes, _ = rb.build_planes_protos(64, 4, 8, 1, device="cpu", seed=0)
+    out_r, _, _ = O.race_qkv_fwd(Q, K, V, planes, 8, 4)
+    dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, 8, 4)
+    q, k, v = (x.cuda().requires_grad_(True) for x in (Q, K, V))
+    out = rb.race_causal(q, k, v, planes.cuda(), 8, 4)
+    out.backward(dO.cuda())
+    assert relerr(out, out_r) < 1e-4
+    assert relerr(q.grad, dQ_r) < 1e-4
+    assert relerr(k.grad, dK_r) < 1e-4
+    assert relerr(v.grad, dV_r) < 1e-4
+
+
+@pytest.mark.parametrize("T,L,H", [(1, 16, 2), (7, 16, 2), (300, 16, 4), (2048, 16, 4), (1500, 8, 3)])
+def test_bf16_vs_fp32_oracle(T, L, H):
+    """BASELINE config 2 geometry (L=16 or 8, P=4, D=64, inputs N(0,1)/8) in bf16:
+    north-star tolerance rel 2e-2 against the oracle on the same (bf16-rounded) inputs."""
+    import race_attention_b200 as rb
+    Q, K, V, dO = qkv(1, H, T, 64, seed=11 * T + L, scale=1.0 / 8.0, dtype=torch.bfloat16)
+    planes, _ = rb.build_planes_protos(64, 4, L, 1, device="cpu", seed=0)
+    out_r, _, _ = O.race_qkv_fwd(Q, K, V, planes, L, 4)
+    dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, L, 4)
+    q, k, v = (x.cuda().requires_grad_(True) for x in (Q, K, V))
+    out = rb.race_causal(q, k, v, planes.cuda(), L, 4)
+    out.backward(dO.cuda())
+    assert out.dtype == torch.bfloat16 and q.grad.dtype == torch.bfloat16
+    assert relerr(out, out_r) < 2e-2
+    assert relerr(q.grad, dQ_r) < 2e-2
+    assert relerr(k.grad, dK_r) < 2e-2
+    assert relerr(v.grad, dV_r) < 2e-2
+
+
+def test_fused_equals_probs_composition():
+    """race_causal == soft_hash_probs + RaceCausalFn (the reference module's composition)."""
+    import race_attention_b200 as rb
+    Q, K, V, dO = qkv(2, 3, 200, 32, seed=2)
+    planes, protos = rb.build_planes_protos(32, 3, 4, 1, device="cuda", seed=4)
+    Q, K, V, dO = (x.cuda() for x in (Q, K, V, dO))
+    pk, pq, V2, N = rb.soft_hash_probs(Q, K, V, planes, protos, 4, 3, 1)
+    a = rb.RaceCausalFn.apply(pk, pq, V2, 1e-6).view(2, 3, 200, 32)
+    b = rb.race_causal(Q, K, V, planes, 4, 3)
+    assert relerr(b, a) < 1e-5
+
+
+def test_carried_state_and_final_state():
+    """fwd_qkv with a carried-in state == the tail of a full run; finals match the oracle."""
+    import race_attention_b200 as rb
+    Q, K, V, dO = qkv(1, 2, 300, 64, seed=9)
+    planes, _ = rb.build_planes_protos(64, 4, 8, 1, device="cpu", seed=0)
+    Qc, Kc, Vc, pc = Q.cuda(), K.cuda(), V.cuda(), planes.cuda()
+    full, Af, Bf = rb.ops.fwd_qkv(Qc, Kc, Vc, pc, 8, 4, return_state=True)
+    _, A1, B1 = rb.ops.fwd_qkv(Qc[:, :, :120], Kc[:, :, :120], Vc[:, :, :120], pc, 8, 4, return_state=True)
+    tail = rb.ops.fwd_qkv(Qc[:, :, 120:], Kc[:, :, 120:], Vc[:, :, 120:], pc, 8, 4, A0=A1, B0=B1)
+    assert relerr(tail, full.view(1, 2, 300, 64)[:, :, 120:].reshape(tail.shape)) < 1e-5
+    _, Ar, Br = O.race_qkv_fwd(Q, K, V, planes, 8, 4)
+    assert relerr(Af, Ar) < 1e-5 and relerr(Bf, Br) < 1e-5
+    # total soft-bucket mass: every table's probabilities sum to 1 per token
+    assert abs(float(Af.sum(1)[0]) - 300 * 8) < 1e-2
+
+
+def test_logit_scale_argument():
+    import race_attention_b200 as rb
+    Q, K, V, _ = qkv(1, 2, 50, 64, seed=1)
+    planes, _ = rb.build_planes_protos(64, 4, 8, 1, device="cpu", seed=0)
+    out = rb.race_causal(Q.cuda(), K.cuda(), V.cuda(), planes.cuda(), 8, 4, logit_scale=1.0)
+    ref, _, _ = O.race_qkv_fwd(Q, K, V, planes, 8, 4, logit_scale=1.0)
+    assert relerr(out, ref) < 1e-4

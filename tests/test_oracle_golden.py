@@ -1,0 +1,98 @@
+"""Pin the CPU oracle to the reference: every golden vector in tests/golden/golden.npz
+was produced by running the reference's own code (tests/golden/make_golden.py)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from conftest import relerr
+
+
+def test_soft_hash_matches_reference(golden):
+    for i, (B, H, T, D, kb, L, seed) in enumerate(golden["hash_cases"]):
+        pT = golden[f"hash{i}_planes_T"]
+        pk = O.soft_hash(golden[f"hash{i}_K"], pT, int(L), int(kb))
+        pq = O.soft_hash(golden[f"hash{i}_Q"], pT, int(L), int(kb))
+        # reference computes in fp32; the oracle in fp64
+        assert np.abs(pk - golden[f"hash{i}_probsK"].reshape(pk.shape)).max() < 2e-7
+        assert np.abs(pq - golden[f"hash{i}_probsQ"].reshape(pq.shape)).max() < 2e-7
+
+
+@pytest.mark.parametrize("i", range(8))
+def test_scan_fwd_bwd_matches_reference_fp64(golden, i):
+    g = lambda k: golden[f"scan{i}_{k}"]  # noqa: E731
+    out, Af, Bf = O.race_fwd(g("pk"), g("pq"), g("V"))
+    assert relerr(out, g("out")) < 1e-12
+    assert relerr(Af, g("A_final")) < 1e-12
+    assert relerr(Bf, g("B_final")) < 1e-12
+    dpk, dpq, dV, _, _ = O.race_bwd(g("pk"), g("pq"), g("V"), g("dO"))
+    # T=1 gradProbsK is an exact cancellation (gA + V.gB): compare on an absolute floor
+    assert relerr(dpk, g("dpk")) < 1e-10 or np.abs(dpk - g("dpk")).max() < 1e-12
+    assert relerr(dpq, g("dpq")) < 1e-12
+    assert relerr(dV, g("dV")) < 1e-12
+
+
+def test_reference_cpu_kernel_matches_oracle(golden):
+    """The reference's compiled OpenMP kernel (fp32) agrees with the oracle at its own tolerances."""
+    g = lambda k: golden[f"scan0_{k}"]  # noqa: E731
+    out, _, _ = O.race_fwd(g("pk"), g("pq"), g("V"))
+    dpk, dpq, dV, _, _ = O.race_bwd(g("pk"), g("pq"), g("V"), g("dO"))
+    assert relerr(golden["refcpu_out"], out) < 1e-4
+    assert relerr(golden["refcpu_dpk"], dpk) < 1e-3
+    assert relerr(golden["refcpu_dpq"], dpq) < 1e-3
+    assert relerr(golden["refcpu_dV"], dV) < 1e-3
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_full_layer_matches_reference_module(golden, i):
+    """Soft hash + scan + ensemble mean vs the reference's RaceCumsumCausal (fp32)."""
+    B, H, T, D, kb, L, M, share, seed = (int(x) for x in golden["e2e_cases"][i])
+    g = lambda k: golden[f"e2e{i}_{k}"]  # noqa: E731
+    pl = g("planes_T")
+    planes = [pl] * M if share else [pl[m] for m in range(M)]
+    outs, grads = [], []
+    for pm in planes:
+        outs.append(O.race_qkv_fwd(g("Q"), g("K"), g("V"), pm, L, kb)[0])
+        grads.append(O.race_qkv_bwd(g("Q"), g("K"), g("V"), g("dO") / M, pm, L, kb)[:3])
+    out = sum(outs) / M
+    dQ, dK, dV = (sum(x[j] for x in grads) for j in range(3))
+    assert relerr(out, g("out")) < 2e-5
+    assert relerr(dQ, g("dQ")) < 2e-3
+    assert relerr(dK, g("dK")) < 2e-3
+    assert relerr(dV, g("dV")) < 2e-3
+
+
+def test_state_carry_equals_full_sequence(golden):
+    """Splitting the sequence with a carried state reproduces the full scan (decode / shard oracle)."""
+    g = lambda k: golden[f"scan4_{k}"]  # noqa: E731
+    pk, pq, V, dO = g("pk"), g("pq"), g("V"), g("dO")
+    full, Af, Bf = O.race_fwd(pk, pq, V)
+    c = 37
+    o1, A1, B1 = O.race_fwd(pk[:, :c], pq[:, :c], V[:, :c])
+    o2, A2, B2 = O.race_fwd(pk[:, c:], pq[:, c:], V[:, c:], A0=A1, B0=B1)
+    assert relerr(np.concatenate([o1, o2], 1), full) < 1e-13
+    assert relerr(A2, Af) < 1e-13 and relerr(B2, Bf) < 1e-13
+    # backward across the split: later half's dA0/dB0 is the earlier half's incoming gradient
+    dpk_f, dpq_f, dV_f, _, _ = O.race_bwd(pk, pq, V, dO)
+    dpk2, dpq2, dV2, gA, gB = O.race_bwd(pk[:, c:], pq[:, c:], V[:, c:], dO[:, c:], A0=A1, B0=B1)
+    dpk1, dpq1, dV1, _, _ = O.race_bwd(pk[:, :c], pq[:, :c], V[:, :c], dO[:, :c], gA=gA, gB=gB)
+    assert relerr(np.concatenate([dpk1, dpk2], 1), dpk_f) < 1e-12
+    assert relerr(np.concatenate([dpq1, dpq2], 1), dpq_f) < 1e-12
+    assert relerr(np.concatenate([dV1, dV2], 1), dV_f) < 1e-12
+
+
+def test_oracle_soft_hash_grad_matches_autograd():
+    """oracle_soft_hash_bwd vs torch autograd of the reference's soft-hash formula (fp64)."""
+    import itertools
+    g = torch.Generator().manual_seed(3)
+    X = torch.randn(2, 9, 16, generator=g, dtype=torch.float64, requires_grad=True)
+    L, P = 3, 3
+    planes = torch.randn(16, L * P, generator=g, dtype=torch.float64)
+    protos = torch.tensor(list(itertools.product([-1.0, 1.0], repeat=P)), dtype=torch.float64).T
+    proj = (X @ planes).view(2, 9, L, P)
+    probs = torch.softmax((proj.tanh() / 4.0) @ protos, -1).reshape(2, 9, -1)
+    gp = torch.randn(probs.shape, generator=g, dtype=torch.float64)
+    (probs * gp).sum().backward()
+    dX = O.soft_hash_bwd(X.detach(), planes, L, P, gp, 0.25)
+    assert relerr(dX, X.grad) < 1e-12
+    assert relerr(O.soft_hash(X.detach(), planes, L, P, 0.25), probs.detach()) < 1e-13
