@@ -70,8 +70,11 @@ def test_fp32_config1_shape(T):
     out = rb.race_causal(q, k, v, planes.cuda(), 8, 4)
     out.backward(dO.cuda())
     assert relerr(out, out_r) < 1e-4
-    assert relerr(q.grad, dQ_r) < 1e-4
-    assert relerr(k.grad, dK_r) < 1e-4
+    # at T=1 the exact dQ is a cancellation (dprobs is constant over each table's
+    # corners, which the softmax Jacobian annihilates): the reference's
+    # absolute floor applies there (scaling/test_kernels.py:38-51)
+    assert close(q.grad, dQ_r, 1e-4)[0], relerr(q.grad, dQ_r)
+    assert close(k.grad, dK_r, 1e-4)[0], relerr(k.grad, dK_r)
     assert relerr(v.grad, dV_r) < 1e-4
 
 
