@@ -186,6 +186,24 @@ int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V,
                             float eps, float logit_scale,
                             void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- allocation-free variant ----------------------------------------------
+ * No counterpart in the reference.  Same math and outputs as race_fwd_probs
+ * (without A_final/B_final), for callers that cannot give the library device
+ * memory: a host that owns a fixed device pool and forbids side allocations,
+ * a plugin callback that may only enqueue work on the stream it is handed,
+ * or a launch loop that cannot afford cudaMalloc/cudaFree (cudaFree waits for
+ * the whole device).  The scan's chunk records live in a library-owned static
+ * device array of RACE_NOALLOC_SCRATCH_BYTES bytes, reserved on each GPU when
+ * first used there and held until the process exits.  The first call on a
+ * device looks up that array's address, so make it outside any stream
+ * capture.  All calls share the array: calls whose GPU work overlaps race and
+ * must be serialised.  Sizes whose per-stream records (4*ceil(T/32)*(S+S*D)
+ * bytes) exceed the array return RACE_ERR_WORKSPACE. */
+#define RACE_NOALLOC_SCRATCH_BYTES (32u << 20)
+int race_fwd_probs_noalloc(const float *probsK, const float *probsQ, const float *V2,
+                           float *out, int64_t N, int64_t T, int64_t S, int64_t D,
+                           float eps, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,7 @@ SIGNATURES = {
     "race_state_from_prefill": [_P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
     "race_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P],
     "race_fwd_sharded_phaseA": [_P, _P, _I, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
+    "race_fwd_probs_noalloc": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
     "race_bwd_sharded_phaseA": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F,
                                 _P, _SZ, _P],
 }

@@ -30,7 +30,7 @@ def _nvcc() -> str:
 
 def sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cuh"))
-                  + glob.glob(os.path.join(INCLUDE, "*.h")))
+                  + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(INCLUDE, "*.h")))
 
 
 def is_stale() -> bool:
@@ -49,7 +49,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         "-Xcompiler", "-fPIC,-O3", "-shared", "-cudart", "shared",
         "-I", INCLUDE, "-I", CSRC,
         "-Xlinker", f"-rpath,{os.path.join(cuda_home, 'lib64')}",
-        "-o", LIB + ".tmp", os.path.join(CSRC, "race_api.cu"),
+        "-o", LIB + ".tmp", *sorted(glob.glob(os.path.join(CSRC, "*.cu"))),
     ] + list(extra or [])
     if verbose:
         print(" ".join(cmd), flush=True)

@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(NT) fwd_totals(const float *__restrict__ pk, c
 // in-place exclusive scan of the chunk records over g (forward or reverse),
 // seeded with init (may be NULL), inclusive total written to fin (may be NULL).
 // grid (ceil(E/256), N), block 256.  Running sums are kept in double.
-__global__ void chunk_scan(float *__restrict__ St, const float *__restrict__ initA,
+static __global__ void chunk_scan(float *__restrict__ St, const float *__restrict__ initA,
                            const float *__restrict__ initB, float *__restrict__ finA,
                            float *__restrict__ finB, int N, int G, int S, int D, int reverse) {
   const size_t E = state_elems(S, D);

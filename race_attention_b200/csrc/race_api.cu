@@ -315,6 +315,16 @@ cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 }  // namespace
 
+// Shared with the other translation units of the library (csrc/internal.h).
+namespace race {
+int report_error(int code, const char *msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+void clear_error() { g_err[0] = 0; }
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace race
+
 // ============================================================================
 extern "C" {
 
