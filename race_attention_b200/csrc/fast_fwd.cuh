@@ -1,0 +1,608 @@
+// fast_fwd.cuh -- fused tcgen05 forward for bf16, D = 64, P = 4, S in {128, 256}.
+//
+// One CTA walks one (stream n, segment) -- a contiguous run of 128-token
+// chunks -- carrying the bucket state on chip:
+//   Bstate[s, :]  fp32 in TMEM (lanes = buckets of a 128-bucket group),
+//   A_start[s]    fp32 in shared memory.
+// Per chunk (all MMAs tcgen05 kind::f16, bf16 operands, fp32 accumulation):
+//   projK/projQ  = K/Q tile [128 x 64] x planes^T [64 x L*P]          (TMEM)
+//   per bucket group g (128 buckets = 8 tables):
+//     Pk_g       = soft hash of projK (epilogue warps, factorised: the
+//                  softmax over the 16 corners of a table is the product of
+//                  4 per-plane sigmoids)                                (smem bf16)
+//     Apref_g    = tril(1) x Pk_g      -> A_t = A_start + Apref         (TMEM)
+//     W_g        = pq / (A_t + eps)                                     (smem bf16)
+//     Smat_g     = W_g x Pk_g^T ;  out (+)= W_g x bf16(Bstate_g)        (TMEM)
+//     Smask_g    = tril(Smat_g)                                         (smem bf16)
+//     out       += Smask_g x V ;  Bstate_g += Pk_g^T x V                (TMEM)
+//   out -> bf16 -> HBM.
+// The segment-start state comes from fast_totals (one pass over K, V) and the
+// chunk_scan over segments.  Q, K, V tiles arrive by TMA (3-D maps [N][T][64],
+// 128B swizzle; rows past T read as zero).  Every wait on an mbarrier is
+// bounded: on expiry the CTA raises *err, skips the rest of its work, frees its
+// TMEM and returns.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "tc_ptx.cuh"
+
+namespace race {
+namespace fast {
+
+constexpr int C = 128;             // tokens per chunk (MMA M)
+constexpr int HD = 64;             // head dim
+constexpr int GB = 128;            // buckets per group
+constexpr int NEPI = 8;            // epilogue warps (2 per TMEM lane quarter)
+constexpr int NTHR = (NEPI + 1) * 32;
+constexpr int NEPI_T = NEPI * 32;
+constexpr uint32_t TILE = C * 128;  // one [128 x 64] bf16 tile = 16 KB
+
+// TMEM column map of the forward kernel (512 columns allocated)
+constexpr uint32_t T_PK = 0, T_PQ = 64, T_G = 128, T_OUT = 256, T_B = 320;
+
+struct FwdArgs {
+  int N, T, L, LP, S, ngroups;
+  int nseg, seg_chunks, nchunks;  // chunks per segment; total chunks per stream
+  float eps, scale;
+  const float *planes;    // [64, LP] fp32
+  const float *seg_state;  // [N, nseg, S + S*64]  (A part, then B part) exclusive segment prefixes
+  float *seg_tot;          // totals kernel output, same layout
+  __nv_bfloat16 *out;      // [N, T, 64]
+  int *err;
+};
+
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// probabilities of the 16 corners of one table from its 4 projections
+// (corner r: bit (3-p) of r selects sigma(+2a_p) vs sigma(-2a_p))
+__device__ __forceinline__ void table_probs(const float *proj4, float scale, float *p16) {
+  float q[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float a = tanh_fast(proj4[p]) * scale;
+    q[p] = __fdividef(1.f, 1.f + __expf(-2.f * a));
+  }
+  float x[4], y[8];
+#pragma unroll
+  for (int b0 = 0; b0 < 2; ++b0)
+#pragma unroll
+    for (int b1 = 0; b1 < 2; ++b1) x[b0 * 2 + b1] = (b0 ? q[0] : 1.f - q[0]) * (b1 ? q[1] : 1.f - q[1]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    y[2 * i] = x[i] * (1.f - q[2]);
+    y[2 * i + 1] = x[i] * q[2];
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    p16[2 * i] = y[i] * (1.f - q[3]);
+    p16[2 * i + 1] = y[i] * q[3];
+  }
+}
+
+// --------------------------------------------------------------------------
+// shared-memory plan (byte offsets from a 1024-aligned base)
+struct FwdSmem {
+  uint32_t q[2], k[2], v, pk, w, bst, tril, planes, a0, a1, bars, total;
+};
+
+__host__ __device__ __forceinline__ FwdSmem fwd_smem_plan(int ngroups, int LP) {
+  FwdSmem m;
+  uint32_t o = 0;
+  m.q[0] = o; o += TILE;
+  m.q[1] = o; o += TILE;
+  m.k[0] = o; o += TILE;
+  m.k[1] = o; o += TILE;
+  m.v = o; o += TILE;
+  m.pk = o; o += 2 * TILE;
+  m.w = o; o += 2 * TILE;
+  m.bst = o; o += (uint32_t)ngroups * TILE;
+  m.tril = o; o += 2 * TILE;
+  m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.a0 = o; o += 1024;
+  m.a1 = o; o += 1024;
+  m.bars = o; o += 256;
+  m.total = o + 1024;  // + alignment slack
+  return m;
+}
+
+// barrier slots
+enum { B_QK0 = 0, B_QK1, B_V, B_PROJ, B_PK, B_APREF, B_W, B_SMAT, B_SMASK, B_GDONE, B_BST0, B_BST1, B_OUTFREE,
+       B_FINAL, B_COUNT };
+
+__global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                              const __grid_constant__ CUtensorMap tmK,
+                                                              const __grid_constant__ CUtensorMap tmV, FwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  const FwdSmem P = fwd_smem_plan(a.ngroups, a.LP);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int c_begin = seg * a.seg_chunks;
+  const int c_end = min(a.nchunks, c_begin + a.seg_chunks);
+  const int nch = c_end - c_begin;
+  const int S = a.S;
+  const size_t E = (size_t)S + (size_t)S * HD;
+  const float *state0 = a.seg_state + ((size_t)n * a.nseg + seg) * E;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    tc::mbar_init(&bars[B_QK0], 1);
+    tc::mbar_init(&bars[B_QK1], 1);
+    tc::mbar_init(&bars[B_V], 1);
+    tc::mbar_init(&bars[B_PROJ], 1);
+    tc::mbar_init(&bars[B_PK], NEPI_T);
+    tc::mbar_init(&bars[B_APREF], 1);
+    tc::mbar_init(&bars[B_W], NEPI_T);
+    tc::mbar_init(&bars[B_SMAT], 1);
+    tc::mbar_init(&bars[B_SMASK], NEPI_T);
+    tc::mbar_init(&bars[B_GDONE], 1);
+    tc::mbar_init(&bars[B_BST0], NEPI_T);
+    tc::mbar_init(&bars[B_BST1], NEPI_T);
+    tc::mbar_init(&bars[B_OUTFREE], NEPI_T);
+    tc::mbar_init(&bars[B_FINAL], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  volatile int *abort = &s_abort;
+
+  if (warp == NEPI) {
+    // ===================== control warp: TMA producer + MMA issuer (one lane)
+    if (lane == 0 && nch > 0) {
+      tc::prefetch_tmap(&tmQ);
+      tc::prefetch_tmap(&tmK);
+      tc::prefetch_tmap(&tmV);
+      const int t0 = c_begin * C;
+      tc::mbar_arrive_expect_tx(&bars[B_QK0], 2 * TILE);
+      tc::tma_load_3d(sm + P.q[0], &tmQ, &bars[B_QK0], 0, t0, n);
+      tc::tma_load_3d(sm + P.k[0], &tmK, &bars[B_QK0], 0, t0, n);
+      if (nch > 1) {
+        tc::mbar_arrive_expect_tx(&bars[B_QK1], 2 * TILE);
+        tc::tma_load_3d(sm + P.q[1], &tmQ, &bars[B_QK1], 0, t0 + C, n);
+        tc::tma_load_3d(sm + P.k[1], &tmK, &bars[B_QK1], 0, t0 + C, n);
+      }
+      tc::mbar_arrive_expect_tx(&bars[B_V], TILE);
+      tc::tma_load_3d(sm + P.v, &tmV, &bars[B_V], 0, t0, n);
+
+      const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
+      const uint32_t id_apref = tc::idesc_bf16(C, GB, false, true);
+      const uint32_t id_smat = tc::idesc_bf16(C, C, false, false);
+      const uint32_t id_out = tc::idesc_bf16(C, HD, false, true);
+      const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
+      // the epilogue prologue (planes, tril, A/B state) must be in smem before
+      // the first MMA reads it; its completion is phase 0 of every BST barrier
+      bool ok = true;
+      for (int g = 0; g < a.ngroups && ok; ++g) ok = tc::mbar_wait(&bars[B_BST0 + g], 0, abort);
+      for (int c = 0; c < nch && ok; ++c) {
+        const int st = c & 1;
+        ok = tc::mbar_wait(&bars[B_QK0 + st], (c >> 1) & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        for (int k0 = 0; k0 < HD; k0 += 16) {
+          const uint64_t bp = tc::desc_kmajor(sbase + P.planes, k0, 0);
+          tc::mma_bf16(tmem + T_PK, tc::desc_kmajor(sbase + P.k[st], k0, TILE), bp, id_proj, k0 > 0);
+          tc::mma_bf16(tmem + T_PQ, tc::desc_kmajor(sbase + P.q[st], k0, TILE), bp, id_proj, k0 > 0);
+        }
+        tc::mma_commit(&bars[B_PROJ]);
+        for (int g = 0; g < a.ngroups && ok; ++g) {
+          const int u = c * a.ngroups + g;
+          ok = tc::mbar_wait(&bars[B_PK], u & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          if (g == 0 && c + 2 < nch) {
+            // the proj MMAs that read this Q/K stage completed before the
+            // epilogue could produce Pk: refill the stage with chunk c+2
+            tc::mbar_arrive_expect_tx(&bars[B_QK0 + st], 2 * TILE);
+            tc::tma_load_3d(sm + P.q[st], &tmQ, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
+            tc::tma_load_3d(sm + P.k[st], &tmK, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
+          }
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + T_G, tc::desc_kmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.pk, k0, TILE), id_apref, k0 > 0);
+          tc::mma_commit(&bars[B_APREF]);
+          ok = tc::mbar_wait(&bars[B_W], u & 1, abort);
+          if (ok && g == 0 && c > 0) ok = tc::mbar_wait(&bars[B_OUTFREE], (c - 1) & 1, abort);
+          if (ok) ok = tc::mbar_wait(&bars[B_BST0 + g], c & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          const uint32_t bst = sbase + P.bst + (uint32_t)g * TILE;
+          for (int k0 = 0; k0 < GB; k0 += 16) {
+            const uint64_t aw = tc::desc_kmajor(sbase + P.w, k0, TILE);
+            tc::mma_bf16(tmem + T_G, aw, tc::desc_kmajor(sbase + P.pk, k0, TILE), id_smat, k0 > 0);
+            tc::mma_bf16(tmem + T_OUT, aw, tc::desc_mnmajor(bst, k0, TILE), id_out, g > 0 || k0 > 0);
+          }
+          tc::mma_commit(&bars[B_SMAT]);
+          ok = tc::mbar_wait(&bars[B_SMASK], u & 1, abort);
+          if (ok && g == 0) ok = tc::mbar_wait(&bars[B_V], c & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          for (int k0 = 0; k0 < C; k0 += 16) {
+            const uint64_t bv = tc::desc_mnmajor(sbase + P.v, k0, TILE);
+            tc::mma_bf16(tmem + T_OUT, tc::desc_kmajor(sbase + P.w, k0, TILE), bv, id_out, true);
+            tc::mma_bf16(tmem + T_B + 64 * g, tc::desc_mnmajor(sbase + P.pk, k0, TILE), bv, id_bupd, true);
+          }
+          tc::mma_commit(&bars[B_GDONE]);
+        }
+        if (!ok) break;
+        if (c + 1 < nch) {
+          // V is free once this chunk's last group finished
+          ok = tc::mbar_wait(&bars[B_GDONE], (c * a.ngroups + a.ngroups - 1) & 1, abort);
+          if (!ok) break;
+          tc::mbar_arrive_expect_tx(&bars[B_V], TILE);
+          tc::tma_load_3d(sm + P.v, &tmV, &bars[B_V], 0, (c_begin + c + 1) * C, n);
+        }
+      }
+      // drain: every MMA this thread issued has completed before TMEM is freed
+      tc::mma_commit(&bars[B_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[B_FINAL], 0)) atomicExch(a.err, 2);
+    }
+    __syncwarp();
+  } else {
+    // ===================== epilogue warps: row t of the chunk, column half h
+    const int q4 = warp & 3, h = warp >> 2;
+    const int t = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    float *sA[2] = {reinterpret_cast<float *>(sm + P.a0), reinterpret_cast<float *>(sm + P.a1)};
+    // ---- prologue: planes (bf16, K-major rows j), tril, A_start, Bstate
+    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
+      const int j = i / HD, d = i % HD;
+      const uint32_t off = P.planes + tc::sw128_off(j, d >> 3) + (d & 7) * 2;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + off) = __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
+    }
+    {
+      // tril[t][tau] = tau <= t, two 64-column blocks; this thread writes row t, block h
+      float v[8];
+      for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = (h * 64 + ch * 8 + e) <= t ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
+      }
+    }
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sA[0][s] = state0[s];
+    for (int g = 0; g < a.ngroups; ++g) {
+      float v[32];
+      const float *src = state0 + S + (size_t)(g * GB + t) * HD + 32 * h;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = src[i];
+      tc::tmem_st32(tmem + lane_off + T_B + 64 * g + 32 * h, v);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 4 * h + ch, v + 8 * ch);
+    }
+    tc::tmem_wait_st();
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    tc::named_bar_sync(1, NEPI_T);  // prologue smem (planes, tril, A) complete before first use
+    for (int g = 0; g < a.ngroups; ++g) tc::mbar_arrive(&bars[B_BST0 + g]);
+
+    bool ok = true;
+    for (int c = 0; c < nch && ok; ++c) {
+      const int tok0 = (c_begin + c) * C;
+      const int nt = min(C, a.T - tok0);
+      const float *Acur = sA[c & 1];
+      float *Anxt = sA[(c + 1) & 1];
+      ok = tc::mbar_wait(&bars[B_PROJ], c & 1, abort);
+      if (!ok) break;
+      __syncwarp();
+      tc::tc_fence_after();
+      for (int g = 0; g < a.ngroups && ok; ++g) {
+        const int u = c * a.ngroups + g;
+        const int j0 = (g * 8 + h * 4) * 4;  // first projection column of this thread's 4 tables
+        // ---- Pk (this thread: row t, buckets [64h, 64h+64) of group g)
+        {
+          float pj[16], pr[64];
+          tc::tmem_ld16(tmem + lane_off + T_PK + j0, pj);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
+          if (t >= nt) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) pr[i] = 0.f;
+          }
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.pk + h * TILE, t, ch, pr + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[B_PK]);
+        // ---- W = pq / (A_start + Apref + eps)
+        ok = tc::mbar_wait(&bars[B_APREF], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float pj[16], pq[64], ap[64];
+          tc::tmem_ld16(tmem + lane_off + T_PQ + j0, pj);
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, *reinterpret_cast<float(*)[32]>(ap));
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, *reinterpret_cast<float(*)[32]>(ap + 32));
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pq + 16 * i);
+          const int sb = g * GB + 64 * h;
+          if (t == C - 1) {
+#pragma unroll 8
+            for (int i = 0; i < 64; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 64; ++i) pq[i] = __fdividef(pq[i], Acur[sb + i] + ap[i] + a.eps);
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, pq + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[B_W]);
+        // ---- Smask = tril(Smat)
+        ok = tc::mbar_wait(&bars[B_SMAT], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float sv[64];
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, *reinterpret_cast<float(*)[32]>(sv));
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (64 * h + i > t) sv[i] = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, sv + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[B_SMASK]);
+        // ---- refresh the bf16 copy of Bstate_g (lane t = bucket t of group g)
+        ok = tc::mbar_wait(&bars[B_GDONE], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float bv[32];
+          tc::tmem_ld32(tmem + lane_off + T_B + 64 * g + 32 * h, bv);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 4 * h + ch, bv + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[B_BST0 + g]);
+      }
+      if (!ok) break;
+      // ---- out rows (the last group's GDONE wait covered all MMAs into out)
+      {
+        float ov[32];
+        tc::tmem_ld32(tmem + lane_off + T_OUT + 32 * h, ov);
+        tc::tmem_wait_ld();
+        if (t < nt) {
+          uint4 *dst = reinterpret_cast<uint4 *>(a.out + ((size_t)n * a.T + tok0 + t) * HD + 32 * h);
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            uint4 w4;
+            w4.x = tc::pack_bf16(ov[8 * ch + 0], ov[8 * ch + 1]);
+            w4.y = tc::pack_bf16(ov[8 * ch + 2], ov[8 * ch + 3]);
+            w4.z = tc::pack_bf16(ov[8 * ch + 4], ov[8 * ch + 5]);
+            w4.w = tc::pack_bf16(ov[8 * ch + 6], ov[8 * ch + 7]);
+            dst[ch] = w4;
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[B_OUTFREE]);
+    }
+    if (!ok && lane == 0) atomicExch(a.err, 1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == NEPI) {
+    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Segment totals: A_tot[s] = sum_t pk[t,s], B_tot[s,:] = sum_t pk[t,s] V[t,:]
+// over one (stream, segment), written as a record of the chunk_scan layout.
+// Same warp roles; A_tot comes from an MMA against a ones column.
+struct TotSmem {
+  uint32_t k[2], v[2], pk, ones, planes, bars, total;
+};
+
+__host__ __device__ __forceinline__ TotSmem tot_smem_plan(int ngroups, int LP) {
+  TotSmem m;
+  uint32_t o = 0;
+  m.k[0] = o; o += TILE;
+  m.k[1] = o; o += TILE;
+  m.v[0] = o; o += TILE;
+  m.v[1] = o; o += TILE;
+  m.pk = o; o += (uint32_t)ngroups * 2 * TILE;
+  m.ones = o; o += TILE;
+  m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.bars = o; o += 256;
+  m.total = o + 1024;
+  return m;
+}
+
+// TMEM map of the totals kernel (256 columns): projK 0..63, Bstate g at 64+64g, A at 192 + 16g
+enum { TB_FULL0 = 0, TB_FULL1, TB_PROJ, TB_PK, TB_DONE, TB_FINAL, TB_INIT, TB_COUNT };
+
+__global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                             const __grid_constant__ CUtensorMap tmV, FwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  const TotSmem P = tot_smem_plan(a.ngroups, a.LP);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int c_begin = seg * a.seg_chunks;
+  const int c_end = min(a.nchunks, c_begin + a.seg_chunks);
+  const int nch = c_end - c_begin;
+  const int S = a.S;
+  const size_t E = (size_t)S + (size_t)S * HD;
+  float *rec = a.seg_tot + ((size_t)n * a.nseg + seg) * E;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    tc::mbar_init(&bars[TB_FULL0], 1);
+    tc::mbar_init(&bars[TB_FULL1], 1);
+    tc::mbar_init(&bars[TB_PROJ], 1);
+    tc::mbar_init(&bars[TB_PK], NEPI_T);
+    tc::mbar_init(&bars[TB_DONE], 1);
+    tc::mbar_init(&bars[TB_FINAL], 1);
+    tc::mbar_init(&bars[TB_INIT], NEPI_T);
+    tc::fence_mbar_init();
+  }
+  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 256);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  volatile int *abort = &s_abort;
+
+  if (warp == NEPI) {
+    if (lane == 0 && nch > 0) {
+      tc::prefetch_tmap(&tmK);
+      tc::prefetch_tmap(&tmV);
+      for (int c = 0; c < 2 && c < nch; ++c) {
+        tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + c], 2 * TILE);
+        tc::tma_load_3d(sm + P.k[c], &tmK, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
+        tc::tma_load_3d(sm + P.v[c], &tmV, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
+      }
+      const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
+      const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
+      const uint32_t id_ones = tc::idesc_bf16(GB, 16, true, true);
+      bool ok = tc::mbar_wait(&bars[TB_INIT], 0, abort);  // planes + ones column written
+      for (int c = 0; c < nch && ok; ++c) {
+        const int st = c & 1;
+        ok = tc::mbar_wait(&bars[TB_FULL0 + st], (c >> 1) & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        for (int k0 = 0; k0 < HD; k0 += 16)
+          tc::mma_bf16(tmem + 0, tc::desc_kmajor(sbase + P.k[st], k0, TILE),
+                       tc::desc_kmajor(sbase + P.planes, k0, 0), id_proj, k0 > 0);
+        tc::mma_commit(&bars[TB_PROJ]);
+        ok = tc::mbar_wait(&bars[TB_PK], c & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        for (int g = 0; g < a.ngroups; ++g) {
+          const uint32_t pk = sbase + P.pk + (uint32_t)g * 2 * TILE;
+          for (int k0 = 0; k0 < C; k0 += 16) {
+            const uint64_t ap = tc::desc_mnmajor(pk, k0, TILE);
+            tc::mma_bf16(tmem + 64 + 64 * g, ap, tc::desc_mnmajor(sbase + P.v[st], k0, TILE), id_bupd,
+                         c > 0 || k0 > 0);
+            tc::mma_bf16(tmem + 192 + 16 * g, ap, tc::desc_mnmajor(sbase + P.ones, k0, TILE), id_ones,
+                         c > 0 || k0 > 0);
+          }
+        }
+        tc::mma_commit(&bars[TB_DONE]);
+        if (c + 2 < nch) {
+          ok = tc::mbar_wait(&bars[TB_DONE], c & 1, abort);
+          if (!ok) break;
+          tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + st], 2 * TILE);
+          tc::tma_load_3d(sm + P.k[st], &tmK, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
+          tc::tma_load_3d(sm + P.v[st], &tmV, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
+        }
+      }
+      tc::mma_commit(&bars[TB_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[TB_FINAL], 0)) atomicExch(a.err, 2);
+    }
+    __syncwarp();
+  } else {
+    const int q4 = warp & 3, h = warp >> 2;
+    const int t = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
+      const int j = i / HD, d = i % HD;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(j, d >> 3) + (d & 7) * 2) =
+          __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
+    }
+    {
+      float v[8];
+      for (int ch = 4 * h; ch < 4 * h + 4; ++ch) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = (ch * 8 + e) < 16 ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.ones, t, ch, v);
+      }
+    }
+    tc::fence_async_smem();
+    tc::mbar_arrive(&bars[TB_INIT]);
+    bool ok = true;
+    for (int c = 0; c < nch && ok; ++c) {
+      const int nt = min(C, a.T - (c_begin + c) * C);
+      ok = tc::mbar_wait(&bars[TB_PROJ], c & 1, abort);
+      if (ok && c > 0) ok = tc::mbar_wait(&bars[TB_DONE], (c - 1) & 1, abort);  // Pk buffers free
+      if (!ok) break;
+      __syncwarp();
+      tc::tc_fence_after();
+      for (int g = 0; g < a.ngroups; ++g) {
+        const int j0 = (g * 8 + h * 4) * 4;
+        float pj[16], pr[64];
+        tc::tmem_ld16(tmem + lane_off + j0, pj);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
+        if (t >= nt) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) pr[i] = 0.f;
+        }
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.pk + (g * 2 + h) * TILE, t, ch, pr + 8 * ch);
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[TB_PK]);
+    }
+    // write the totals record
+    if (ok && nch > 0) ok = tc::mbar_wait(&bars[TB_DONE], (nch - 1) & 1, abort);
+    __syncwarp();
+    tc::tc_fence_after();
+    if (ok) {
+      for (int g = 0; g < a.ngroups; ++g) {
+        float bv[32];
+        tc::tmem_ld32(tmem + lane_off + 64 + 64 * g + 32 * h, bv);
+        tc::tmem_wait_ld();
+        float *dst = rec + S + (size_t)(g * GB + t) * HD + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[i] = bv[i];
+        if (h == 0) {
+          float av[16];
+          tc::tmem_ld16(tmem + lane_off + 192 + 16 * g, av);
+          tc::tmem_wait_ld();
+          rec[g * GB + t] = av[0];
+        } else {
+          float av[16];
+          tc::tmem_ld16(tmem + lane_off + 192 + 16 * g, av);  // keep the warp's tcgen05.ld uniform
+          tc::tmem_wait_ld();
+        }
+      }
+    }
+    if (nch == 0) {  // empty segment: zero record
+      for (int i = threadIdx.x; i < (int)E; i += NEPI_T) rec[i] = 0.f;
+    }
+    if (!ok && lane == 0) atomicExch(a.err, 1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == NEPI) {
+    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace fast
+}  // namespace race

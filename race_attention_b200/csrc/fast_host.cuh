@@ -1,0 +1,95 @@
+// fast_host.cuh -- host side of the tcgen05 path: eligibility, planning,
+// tensor maps and launches.  Included once, by race_api.cu.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "fast_fwd.cuh"
+#include "generic.cuh"
+
+namespace race {
+namespace fasthost {
+
+namespace fk = race::fast;
+
+// The tcgen05 path covers bf16 activations with D = 64, P = 4 and S = 128 or
+// 256 (L = 8 or 16): the BASELINE configurations.  Everything else runs on
+// the generic kernels.
+inline bool eligible(int dtype, int64_t D, int64_t L, int64_t P) {
+  return dtype == RACE_BF16 && D == fk::HD && P == 4 && (L == 8 || L == 16);
+}
+
+struct Plan {
+  int nchunks, nseg, seg_chunks;
+  size_t status_off, rec_off, total;
+};
+
+inline int sm_count() {
+  static int cached[128] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (cached[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cached[dev] = v;
+  }
+  return cached[dev];
+}
+
+// One CTA (one SM) per (stream, segment); about four waves of CTAs.
+inline Plan plan(int64_t N, int64_t T, int64_t S, int sms) {
+  Plan p;
+  p.nchunks = (int)((T + fk::C - 1) / fk::C);
+  int64_t want = (4 * (int64_t)sms) / N;
+  if (want < 1) want = 1;
+  if (want > p.nchunks) want = p.nchunks;
+  p.seg_chunks = (int)((p.nchunks + want - 1) / want);
+  p.nseg = (p.nchunks + p.seg_chunks - 1) / p.seg_chunks;
+  const size_t E = (size_t)S + (size_t)S * fk::HD;
+  p.status_off = 0;
+  p.rec_off = 256;
+  p.total = p.rec_off + align_up(sizeof(float) * (size_t)N * p.nseg * E, 256);
+  return p;
+}
+
+// Workspace of the fast forward (planned for the worst case of the SM count
+// so the size does not depend on the device: 4 waves at up to 256 SMs).
+inline size_t fwd_workspace_bytes(int64_t N, int64_t T, int64_t S) { return plan(N, T, S, 256).total; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D map over a [N][T][64] bf16 tensor, box [1][128][64], 128-byte swizzle.
+inline bool make_map(CUtensorMap *m, const void *base, int64_t N, int64_t T) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)fk::HD, (cuuint64_t)T, (cuuint64_t)N};
+  cuuint64_t strides[2] = {(cuuint64_t)fk::HD * 2, (cuuint64_t)T * fk::HD * 2};
+  cuuint32_t box[3] = {(cuuint32_t)fk::HD, (cuuint32_t)fk::C, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace fasthost
+}  // namespace race

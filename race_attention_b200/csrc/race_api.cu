@@ -9,9 +9,11 @@
 #include <atomic>
 #include <algorithm>
 #include <cstring>
+#include <initializer_list>
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "fast_host.cuh"
 #include "generic.cuh"
 
 using race::align_up;
@@ -313,6 +315,71 @@ int bwd_totals_generic(const XT *Q, const XT *K, const XT *V, const XT *dO, cons
 
 cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// ---- tcgen05 path (bf16, D=64, P=4, L in {8,16}) -----------------------------
+namespace fh = race::fasthost;
+namespace fk = race::fast;
+
+int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t L, float eps, float scale,
+              const float *planes_T, void *ws) {
+  a.N = (int)N;
+  a.T = (int)T;
+  a.L = (int)L;
+  a.LP = (int)(4 * L);
+  a.S = (int)(16 * L);
+  a.ngroups = a.S / fk::GB;
+  a.nseg = pl.nseg;
+  a.seg_chunks = pl.seg_chunks;
+  a.nchunks = pl.nchunks;
+  a.eps = eps;
+  a.scale = scale;
+  a.planes = planes_T;
+  a.seg_state = at<float>(ws, pl.rec_off);
+  a.seg_tot = at<float>(ws, pl.rec_off);
+  a.out = nullptr;
+  a.err = at<int>(ws, pl.status_off);
+  return RACE_OK;
+}
+
+int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, const float *A0, const float *B0,
+                         float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
+                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV) {
+  const int64_t S = 16 * L;
+  const fh::Plan pl = fh::plan(N, T, S, fh::sm_count());
+  fast_args(a, pl, N, T, L, eps, scale, planes_T, ws);
+  if (!fh::make_map(&mK, K, N, T) || !fh::make_map(&mV, V, N, T))
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable or bad tensor)");
+  cudaError_t e = cudaMemsetAsync(at<int>(ws, pl.status_off), 0, sizeof(int), s);
+  if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  const fk::TotSmem ts = fk::tot_smem_plan(a.ngroups, a.LP);
+  RACE_TRY(set_smem(fk::fwd_totals_kernel, ts.total));
+  fk::fwd_totals_kernel<<<(unsigned)(N * pl.nseg), fk::NTHR, ts.total, s>>>(mK, mV, a);
+  RACE_TRY(check_launch("fast fwd_totals"));
+  gen::Dims p = make_dims(N, T, S, fk::HD, eps);
+  p.G = pl.nseg;
+  return launch_scan(at<float>(ws, pl.rec_off), A0, B0, Af, Bf, p, 0, s);
+}
+
+int fast_forward(const void *Q, const void *K, const void *V, const float *planes_T, void *out, const float *A0,
+                 const float *B0, float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale,
+                 void *ws, cudaStream_t s) {
+  fk::FwdArgs a;
+  CUtensorMap mQ, mK, mV;
+  RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV));
+  if (!fh::make_map(&mQ, Q, N, T)) return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed for Q");
+  a.out = static_cast<__nv_bfloat16 *>(out);
+  const fk::FwdSmem fs = fk::fwd_smem_plan(a.ngroups, a.LP);
+  RACE_TRY(set_smem(fk::fwd_readout_kernel, fs.total));
+  fk::fwd_readout_kernel<<<(unsigned)(N * a.nseg), fk::NTHR, fs.total, s>>>(mQ, mK, mV, a);
+  return check_launch("fast fwd_readout");
+}
+
+int check_fast_ptrs(std::initializer_list<const void *> ptrs) {
+  for (const void *p : ptrs)
+    if (p && !fh::aligned16(p)) return fail(RACE_ERR_ALIGN, "bf16 activations must be 16-byte aligned");
+  return RACE_OK;
+}
+
+
 }  // namespace
 
 // Shared with the other translation units of the library (csrc/internal.h).
@@ -361,7 +428,10 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int
     return fail(RACE_ERR_ARG, "unknown op %d", op);
   }
   RACE_TRY(check_nts(N, T, S, D));
-  *bytes = generic_layout(op, N, T, S, D).total;
+  if ((op == RACE_OP_FWD_QKV || op == RACE_OP_STATE) && fh::eligible(dtype, D, L, P))
+    *bytes = fh::fwd_workspace_bytes(N, T, S);
+  else
+    *bytes = generic_layout(op, N, T, S, D).total;
   return ok();
 }
 
@@ -469,8 +539,14 @@ int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype, const f
   int64_t S = 0;
   RACE_TRY(check_lp(L, P, &S));
   RACE_TRY(check_nts(N, T, S, D));
-  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total));
   cudaStream_t s = as_stream(stream);
+  if (fh::eligible(dtype, D, L, P)) {
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::fwd_workspace_bytes(N, T, S)));
+    RACE_TRY(check_fast_ptrs({Q, K, V, out}));
+    RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, A_final, B_final, N, T, L, eps, logit_scale, workspace, s));
+    return ok();
+  }
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total));
   if (dtype == RACE_F32)
     RACE_TRY(fwd_qkv_generic<float>((const float *)Q, (const float *)K, (const float *)V, planes_T, (float *)out, A0,
                                     B0, A_final, B_final, N, T, D, L, P, eps, logit_scale, workspace, s));
@@ -523,8 +599,17 @@ int race_state_from_prefill(const void *K, const void *V, int dtype, const float
   int64_t S = 0;
   RACE_TRY(check_lp(L, P, &S));
   RACE_TRY(check_nts(N, T, S, D));
-  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_STATE, N, T, S, D).total));
   cudaStream_t s = as_stream(stream);
+  if (fh::eligible(dtype, D, L, P)) {
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::fwd_workspace_bytes(N, T, S)));
+    RACE_TRY(check_fast_ptrs({K, V}));
+    fk::FwdArgs a;
+    CUtensorMap mK, mV;
+    RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, A_out, B_out, N, T, L, 0.f, logit_scale, workspace, s, a,
+                                  mK, mV));
+    return ok();
+  }
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_STATE, N, T, S, D).total));
   if (dtype == RACE_F32)
     RACE_TRY(state_generic<float>((const float *)K, (const float *)V, planes_T, A0, B0, A_out, B_out, N, T, D, L, P,
                                   logit_scale, workspace, s));

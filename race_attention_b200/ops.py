@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 
 import torch
 
@@ -72,6 +73,22 @@ def _opt_state(A, B, N, S, D, dev):
     A = A.to(device=dev, dtype=torch.float32).reshape(N, S).contiguous()
     B = B.to(device=dev, dtype=torch.float32).reshape(N, S, D).contiguous()
     return A, B
+
+
+def fast_path(dtype, D, L, P) -> bool:
+    """Whether the library runs the tcgen05 kernels for this configuration
+    (same rule as csrc/fast_host.cuh: bf16, D=64, P=4, L in {8,16})."""
+    return dtype == torch.bfloat16 and D == 64 and P == 4 and L in (8, 16)
+
+
+def _check_status(ws, what):
+    """With RACE_B200_CHECK=1, read the device status word the tcgen05 kernels
+    keep at the head of their workspace (non-zero = a bounded wait expired).
+    Call only for tcgen05-path launches."""
+    if os.environ.get("RACE_B200_CHECK") == "1" and ws.numel() >= 4:
+        st = int(ws[:4].view(torch.int32).item())
+        if st != 0:
+            raise RuntimeError(f"{what}: device status {st} (a bounded device-side wait expired)")
 
 
 def default_logit_scale(D: int) -> float:
@@ -204,6 +221,8 @@ def fwd_qkv(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=Non
         _lib.check(lib.race_fwd_qkv(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out), _ptr(A0),
                                     _ptr(B0), _ptr(Af), _ptr(Bf), N, T, D, L, P, float(eps), scale, _ptr(ws), nb,
                                     _stream(dev)), "race_fwd_qkv")
+        if fast_path(Q.dtype, D, L, P):
+            _check_status(ws, "race_fwd_qkv")
     return (out, Af, Bf) if return_state else out
 
 
@@ -238,6 +257,8 @@ def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None)
         _lib.check(lib.race_state_from_prefill(_ptr(K), _ptr(V), _dtype_code(K), _ptr(planes_T), _ptr(A0), _ptr(B0),
                                                _ptr(A), _ptr(B), N, T, D, L, P, scale, _ptr(ws), nb, _stream(dev)),
                    "race_state_from_prefill")
+        if fast_path(K.dtype, D, L, P):
+            _check_status(ws, "race_state_from_prefill")
     return A, B
 
 

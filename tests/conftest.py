@@ -9,6 +9,8 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.npz")
+# surface any expired bounded device-side wait of the tcgen05 kernels as an error
+os.environ.setdefault("RACE_B200_CHECK", "1")
 
 
 def pytest_configure(config):

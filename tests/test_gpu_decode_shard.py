@@ -28,7 +28,8 @@ def test_prefill_then_decode(dtype, tol, Hq, Hkv):
                                      planes.cuda(), L, P)
     assert relerr(out0, ref[:, :, :T0]) < tol
     _, Ar, Br = O.race_qkv_fwd(K[:, :, :T0], K[:, :, :T0], V[:, :, :T0], planes, L, P)
-    assert relerr(st.A, Ar) < 1e-5 and relerr(st.B, Br) < max(tol, 1e-5)
+    # bf16 path: the state accumulates bf16-rounded bucket probabilities (fp32 sums)
+    assert relerr(st.A, Ar) < tol and relerr(st.B, Br) < tol
     for t in range(T0, T):
         o = st.step(Q[:, :, t].cuda(), K[:, :, t].cuda(), V[:, :, t].cuda())
         assert relerr(o, ref[:, :, t]) < tol, t
