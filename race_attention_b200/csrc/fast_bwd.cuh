@@ -1,0 +1,907 @@
+// fast_bwd.cuh -- fused tcgen05 backward for bf16, D = 64, P = 4, S in {128, 256}.
+//
+// Exact gradients of the causal RACE layer (scaling/race_common.py:76-90 with
+// the soft hash of :36-73), per stream n, with W = pq/(A_t+eps):
+//   G_t[s]  = dO_t . B_t[s]                    dpq = G/(A_t+eps)
+//   dA_t[s] = -W_t[s] G_t[s] / (A_t[s]+eps)
+//   gA_t    = sum_{t'>=t} dA_t'   gB_t = sum_{t'>=t} W_t' (x) dO_t'   (suffix states)
+//   dpk     = gA_t + V_t . gB_t   dV_t = sum_s pk[t,s] gB_t[s]
+// Two walks per (stream, segment) of 128-token chunks, with buckets handled in
+// groups of 64 (4 tables).  Per-bucket state accumulators are M=64 tcgen05
+// tiles, two groups sharing a TMEM column block (lane offsets 0 and 16).
+//
+//   bwd_fwd_kernel (forward walk, exact forward state carried in TMEM):
+//     P1 = dO V^T (masked t>=tau) ; per group: Pk, Apref = tril Pk, W, inv,
+//     G = dO Bst^T + P1m Pk, dA, dpq -> d proj_Q ; totals gB += W^T dO,
+//     gA += dA^T 1 ; Bstate += Pk^T V ; then dQ = dprojQ planes.
+//     Stores each chunk's start state (A fp32, B bf16) for the reverse walk.
+//   bwd_rev_kernel (reverse walk, suffix state carried in TMEM):
+//     per group: W, inv, G, dA as above from the stored chunk state;
+//     dpk = tril^T dA + V gBst^T + P1m^T W + gA_suffix -> d proj_K ;
+//     Q2 = Pk W^T (masked t>=tau) ; dV += Pk gBst + Q2m dO ;
+//     gB += W^T dO ; gA += dA^T 1 ; then dK = dprojK planes.
+// The segment-level suffix states come from a reverse chunk_scan of the first
+// walk's totals.  All waits are bounded (see fast_fwd.cuh).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "fast_fwd.cuh"
+#include "tc_ptx.cuh"
+
+namespace race {
+namespace fast {
+
+constexpr int GW = 64;  // buckets per backward group
+
+struct BwdArgs {
+  int N, T, L, LP, S, ngroups;  // ngroups = S / 64
+  int nseg, seg_chunks, nchunks;
+  float eps, scale;
+  const float *planes;      // [64, LP]
+  const float *fwd_state;   // [N, nseg, E]  forward exclusive segment prefixes
+  float *tot;               // [N, nseg, E]  first walk: segment gradient totals
+  const float *suf_state;   // [N, nseg, E]  reverse-scanned totals (suffix at segment end)
+  float *chunkA;            // [N, nchunks, S]        fp32 A at chunk start
+  __nv_bfloat16 *chunkB;    // [N, nchunks, S, 64]    bf16 B at chunk start
+  __nv_bfloat16 *dQ, *dK, *dV;  // [N, T, 64]
+  int *err;
+};
+
+// probabilities of one table's 16 corners from tanh(proj) of its 4 planes
+__device__ __forceinline__ void table_probs_th(const float *th4, float scale, float *p16) {
+  float q[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) q[p] = __fdividef(1.f, 1.f + __expf(-2.f * scale * th4[p]));
+  float x[4], y[8];
+#pragma unroll
+  for (int b0 = 0; b0 < 2; ++b0)
+#pragma unroll
+    for (int b1 = 0; b1 < 2; ++b1) x[b0 * 2 + b1] = (b0 ? q[0] : 1.f - q[0]) * (b1 ? q[1] : 1.f - q[1]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    y[2 * i] = x[i] * (1.f - q[2]);
+    y[2 * i + 1] = x[i] * q[2];
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    p16[2 * i] = y[i] * (1.f - q[3]);
+    p16[2 * i + 1] = y[i] * q[3];
+  }
+}
+
+// d proj of one table: softmax backward over the corners, through sum_p, tanh
+__device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g16, const float *th4, float scale,
+                                                float *out4) {
+  float c = 0.f;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) c = fmaf(p16[r], g16[r], c);
+  float dl[16], all = 0.f;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    dl[r] = p16[r] * (g16[r] - c);
+    all += dl[r];
+  }
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    float set = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      if ((r >> (3 - p)) & 1) set += dl[r];
+    out4[p] = (2.f * set - all) * scale * (1.f - th4[p] * th4[p]);
+  }
+}
+
+__device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float *v) {
+  uint4 w;
+  w.x = tc::pack_bf16(v[0], v[1]);
+  w.y = tc::pack_bf16(v[2], v[3]);
+  w.z = tc::pack_bf16(v[4], v[5]);
+  w.w = tc::pack_bf16(v[6], v[7]);
+  *reinterpret_cast<uint4 *>(dst) = w;
+}
+
+// --------------------------------------------------------------------------
+struct BwdSmem {
+  uint32_t q, k, v, o, p1m, tril, planes, pk, w, da, bst, gbst, dproj, a0, a1, ga, bars, total;
+};
+
+__host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
+  BwdSmem m;
+  uint32_t o = 0;
+  m.q = o; o += TILE;
+  m.k = o; o += TILE;
+  m.v = o; o += TILE;
+  m.o = o; o += TILE;
+  m.p1m = o; o += 2 * TILE;
+  m.tril = o; o += 2 * TILE;
+  m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.pk = o; o += TILE;
+  m.w = o; o += TILE;
+  m.da = o; o += TILE;  // must follow w: [w | da] is the 2-block Q2m tile of the reverse walk
+  m.bst = o; o += GW * 128;
+  m.gbst = o; o += GW * 128;
+  m.dproj = o; o += TILE;
+  m.a0 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
+  m.a1 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
+  m.ga = o; o += GW * 4;
+  m.bars = o; o += 256;
+  m.total = o + 1024;
+  return m;
+}
+
+// TMEM columns: X (128) and R (64) scratch, then per-bucket M=64 state blocks
+constexpr uint32_t BT_X = 0, BT_R = 128, BT_ST = 192;
+
+enum { W_FULL = 0, W_INIT, W_P1, W_P1M, W_PROJ, W_PK, W_APREF, W_W, W_G, W_DA, W_DPK, W_Q2, W_DV, W_OUT, W_OUTFREE,
+       W_BST, W_FINAL, W_ESYNC, W_COUNT };
+
+// barriers the 256 epilogue threads arrive on; the rest complete on one arrival
+__device__ __forceinline__ void bwd_init_bars(uint64_t *bars) {
+  for (int i = 0; i < W_COUNT; ++i) {
+    const bool epi = i == W_INIT || i == W_P1M || i == W_PK || i == W_W || i == W_DA || i == W_Q2 ||
+                     i == W_OUTFREE || i == W_ESYNC;
+    tc::mbar_init(&bars[i], epi ? NEPI_T : 1);
+  }
+  tc::fence_mbar_init();
+}
+
+// row of an M=64 accumulator held by this thread's TMEM lane (lane quarter q, lane i):
+// group parity (i >= 16) and row 16q + (i & 15)
+__device__ __forceinline__ int m64_row(int q4, int lane) { return 16 * q4 + (lane & 15); }
+
+__device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g, uint32_t width) {
+  return tmem + col0 + (uint32_t)(g >> 1) * width + ((uint32_t)((g & 1) * 16) << 16);
+}
+
+// ===========================================================================
+// forward walk of the backward pass
+__global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                          const __grid_constant__ CUtensorMap tmK,
+                                                          const __grid_constant__ CUtensorMap tmV,
+                                                          const __grid_constant__ CUtensorMap tmO, BwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  const BwdSmem P = bwd_smem_plan(a.LP, a.S);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int c_begin = seg * a.seg_chunks;
+  const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
+  const int S = a.S, NG = a.ngroups, nblk = (NG + 1) / 2;
+  const size_t E = (size_t)S + (size_t)S * HD;
+  const uint32_t T_BF = BT_ST, T_GB = BT_ST + 64 * nblk, T_GA = BT_ST + 128 * nblk;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    bwd_init_bars(bars);
+  }
+  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  volatile int *abort = &s_abort;
+
+  if (warp == NEPI) {
+    if (lane == 0 && nch > 0) {
+      const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
+      const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
+      const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
+      const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
+      const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
+      const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
+      const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
+      const uint32_t id_dq = tc::idesc_bf16(C, HD, false, true);
+      auto load_chunk = [&](int c) {
+        const int t0 = (c_begin + c) * C;
+        tc::mbar_arrive_expect_tx(&bars[W_FULL], 4 * TILE);
+        tc::tma_load_3d(sm + P.q, &tmQ, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + P.k, &tmK, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + P.v, &tmV, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + P.o, &tmO, &bars[W_FULL], 0, t0, n);
+      };
+      load_chunk(0);
+      bool ok = tc::mbar_wait(&bars[W_INIT], 0, abort);
+      for (int c = 0; c < nch && ok; ++c) {
+        ok = tc::mbar_wait(&bars[W_FULL], c & 1, abort);
+        if (ok && c > 0) ok = tc::mbar_wait(&bars[W_OUTFREE], (c - 1) & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        for (int k0 = 0; k0 < HD; k0 += 16)
+          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
+                       k0 > 0);
+        tc::mma_commit(&bars[W_P1]);
+        ok = tc::mbar_wait(&bars[W_P1M], c & 1, abort);
+        if (!ok) break;
+        for (int g = 0; g < NG && ok; ++g) {
+          const int u = c * NG + g;
+          if (u > 0) ok = tc::mbar_wait(&bars[W_DA], (u - 1) & 1, abort);  // R free
+          if (!ok) break;
+          tc::tc_fence_after();
+          const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
+          for (int k0 = 0; k0 < HD; k0 += 16) {
+            const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
+            tc::mma_bf16(tmem + BT_R + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
+          }
+          if (u > 0) {
+            // the colsum of the previous group is issued here, after its dA landed
+            const int gp = (u - 1) % NG, cp = (u - 1) / NG;
+            for (int k0 = 0; k0 < C; k0 += 16)
+              tc::mma_bf16(m64_addr(tmem, T_GA, gp, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
+                           tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, cp > 0 || k0 > 0);
+          }
+          tc::mma_commit(&bars[W_PROJ]);
+          ok = tc::mbar_wait(&bars[W_PK], u & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
+          tc::mma_commit(&bars[W_APREF]);
+          ok = tc::mbar_wait(&bars[W_W], u & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          for (int k0 = 0; k0 < HD; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
+                         id_gk, k0 > 0);
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.pk, k0, 0),
+                         id_gm, true);
+          for (int k0 = 0; k0 < C; k0 += 16) {
+            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, c > 0 || k0 > 0);
+            tc::mma_bf16(m64_addr(tmem, T_BF, g, 64), tc::desc_mnmajor(sbase + P.pk, k0, 0),
+                         tc::desc_mnmajor(sbase + P.v, k0, 0), id_st, true);
+          }
+          tc::mma_commit(&bars[W_G]);
+          if (g == NG - 1 && c + 1 < nch) {
+            // every reader of this chunk's Q/K/V/dO tiles has been issued and
+            // completes with W_G: refill the single stage with the next chunk
+            ok = tc::mbar_wait(&bars[W_G], u & 1, abort);
+            if (!ok) break;
+            load_chunk(c + 1);
+          }
+        }
+        if (!ok) break;
+        ok = tc::mbar_wait(&bars[W_DA], (c * NG + NG - 1) & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        if (c + 1 == nch) {  // last chunk: the final colsum is issued here
+          const int gp = NG - 1;
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(m64_addr(tmem, T_GA, gp, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
+                         tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, c > 0 || k0 > 0);
+        }
+        for (int k0 = 0; k0 < a.LP; k0 += 16)
+          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
+                       id_dq, k0 > 0);
+        tc::mma_commit(&bars[W_OUT]);
+      }
+      tc::mma_commit(&bars[W_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[W_FINAL], 0)) atomicExch(a.err, 2);
+    }
+    __syncwarp();
+  } else {
+    // ========================================================= epilogue warps
+    const int q4 = warp & 3, h = warp >> 2;
+    const int t = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int mrow = m64_row(q4, lane), mpar = lane >> 4;
+    float *sA[2] = {reinterpret_cast<float *>(sm + P.a0), reinterpret_cast<float *>(sm + P.a1)};
+    const float *st0 = a.fwd_state + ((size_t)n * a.nseg + seg) * E;
+    // ---- prologue
+    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
+      const int j = i / HD, d = i % HD;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(j, d >> 3) + (d & 7) * 2) =
+          __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
+    }
+    {
+      float v[8];
+      for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = (h * 64 + ch * 8 + e) <= t ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
+      }
+    }
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sA[0][s] = st0[s];
+    for (int b = 0; b < nblk; ++b) {  // forward state -> TMEM (M=64 layout), this lane's row
+      const int g = 2 * b + mpar;
+      float v[32];
+      if (g < NG) {
+        const float *src = st0 + S + (size_t)(g * GW + mrow) * HD + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = src[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      tc::tmem_st32(tmem + lane_off + T_BF + 64 * b + 32 * h, v);
+    }
+    tc::tmem_wait_st();
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    tc::named_bar_sync(1, NEPI_T);
+    tc::mbar_arrive(&bars[W_INIT]);
+
+    bool ok = true;
+    for (int c = 0; c < nch && ok; ++c) {
+      const int cg = c_begin + c, tok0 = cg * C;
+      const int nt = min(C, a.T - tok0);
+      const float *Acur = sA[c & 1];
+      float *Anxt = sA[(c + 1) & 1];
+      // the row-127 threads wrote this chunk's A during the previous one
+      ok = tc::mbar_sync(&bars[W_ESYNC], c & 1, abort);
+      if (!ok) break;
+      // ---- P1m = tril-masked dO V^T ; chunk-start A to global
+      for (int s = threadIdx.x; s < S; s += NEPI_T) a.chunkA[((size_t)n * a.nchunks + cg) * S + s] = Acur[s];
+      ok = tc::mbar_wait(&bars[W_P1], c & 1, abort);
+      if (!ok) break;
+      __syncwarp();
+      tc::tc_fence_after();
+      {
+        float v[32];
+        for (int hh = 0; hh < 2; ++hh) {
+          tc::tmem_ld32(tmem + lane_off + BT_X + 64 * h + 32 * hh, v);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (64 * h + 32 * hh + i > t) v[i] = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + h * TILE, t, 4 * hh + ch, v + 8 * ch);
+        }
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[W_P1M]);
+      for (int g = 0; g < NG && ok; ++g) {
+        const int u = c * NG + g;
+        float thQ[8], inv[32];
+        // ---- Pk, pq
+        ok = tc::mbar_wait(&bars[W_PROJ], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float pk8[8], pr[32];
+          tc::tmem_ld8(tmem + lane_off + BT_R + 8 * h, pk8);
+          tc::tmem_ld8(tmem + lane_off + BT_R + 16 + 8 * h, thQ);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pk8[i] = tanh_fast(pk8[i]);
+            thQ[i] = tanh_fast(thQ[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(pk8 + 4 * i, a.scale, pr + 16 * i);
+          if (t >= nt) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+          }
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.pk, t, 4 * h + ch, pr + 8 * ch);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, pr + 16 * i);
+          if (t >= nt) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+          }
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w, t, 4 * h + ch, pr + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[W_PK]);
+        // ---- inv, W ; chunk-start B state of this group -> smem bf16 + global
+        ok = tc::mbar_wait(&bars[W_APREF], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float ap[32], pq[32];
+          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, ap);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::ld_row_chunk(sbase + P.w, t, 4 * h + ch, pq + 8 * ch);
+          const int sb = g * GW + 32 * h;
+          if (t == C - 1) {
+#pragma unroll 8
+            for (int i = 0; i < 32; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            inv[i] = __fdividef(1.f, Acur[sb + i] + ap[i] + a.eps);
+            pq[i] *= inv[i];
+          }
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w, t, 4 * h + ch, pq + 8 * ch);
+          float bv[32];
+          tc::tmem_ld32(tmem + lane_off + T_BF + 64 * (g >> 1) + 32 * h, bv);
+          tc::tmem_wait_ld();
+          if (mpar == (g & 1)) {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.bst, mrow, 4 * h + ch, bv + 8 * ch);
+            __nv_bfloat16 *dst = a.chunkB + (((size_t)n * a.nchunks + cg) * S + g * GW + mrow) * HD + 32 * h;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) st_bf16x8_global(dst + 8 * ch, bv + 8 * ch);
+          }
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[W_W]);
+        // ---- G -> dpq (-> d proj_Q) and dA
+        ok = tc::mbar_wait(&bars[W_G], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float G[32], pq[32], da[32];
+          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, G);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, pq + 16 * i);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gi = G[i] * inv[i];           // dpq
+            da[i] = -pq[i] * inv[i] * gi;              // dA
+            G[i] = gi;
+          }
+          if (t >= nt) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              da[i] = 0.f;
+              G[i] = 0.f;
+            }
+          }
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.da, t, 4 * h + ch, da + 8 * ch);
+          float dp[8];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_bwd(pq + 16 * i, G + 16 * i, thQ + 4 * i, a.scale, dp + 4 * i);
+          tc::st_row_chunk(sbase + P.dproj, t, 2 * g + h, dp);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[W_DA]);
+      }
+      if (!ok) break;
+      // ---- dQ
+      ok = tc::mbar_wait(&bars[W_OUT], c & 1, abort);
+      if (!ok) break;
+      __syncwarp();
+      tc::tc_fence_after();
+      {
+        float ov[32];
+        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * h, ov);
+        tc::tmem_wait_ld();
+        if (t < nt && a.dQ != nullptr) {
+          __nv_bfloat16 *dst = a.dQ + ((size_t)n * a.T + tok0 + t) * HD + 32 * h;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) st_bf16x8_global(dst + 8 * ch, ov + 8 * ch);
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[W_OUTFREE]);
+    }
+    // ---- segment totals record (W_OUT of the last chunk covers every accumulation)
+    __syncwarp();
+    tc::tc_fence_after();
+    if (ok && nch > 0) {
+      float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
+      for (int b = 0; b < nblk; ++b) {
+        const int g = 2 * b + mpar;
+        float bv[32], av;
+        tc::tmem_ld32(tmem + lane_off + T_GB + 64 * b + 32 * h, bv);
+        tc::tmem_ld1(tmem + lane_off + T_GA + 16 * b, av);
+        tc::tmem_wait_ld();
+        if (g < NG) {
+          float *dst = rec + S + (size_t)(g * GW + mrow) * HD + 32 * h;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) dst[i] = bv[i];
+          if (h == 0) rec[g * GW + mrow] = av;
+        }
+      }
+    } else if (nch == 0) {
+      float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
+      for (int i = threadIdx.x; i < (int)E; i += NEPI_T) rec[i] = 0.f;
+    }
+    if (!ok && lane == 0) atomicExch(a.err, 1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == NEPI) {
+    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// reverse walk of the backward pass
+__global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                          const __grid_constant__ CUtensorMap tmK,
+                                                          const __grid_constant__ CUtensorMap tmV,
+                                                          const __grid_constant__ CUtensorMap tmO,
+                                                          const __grid_constant__ CUtensorMap tmB, BwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  const BwdSmem P = bwd_smem_plan(a.LP, a.S);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int c_begin = seg * a.seg_chunks;
+  const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
+  const int S = a.S, NG = a.ngroups, nblk = (NG + 1) / 2;
+  const size_t E = (size_t)S + (size_t)S * HD;
+  const uint32_t T_GB = BT_ST, T_GA = BT_ST + 64 * nblk, T_DV = BT_ST + 80 * nblk;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    bwd_init_bars(bars);
+  }
+  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  volatile int *abort = &s_abort;
+
+  if (warp == NEPI) {
+    if (lane == 0 && nch > 0) {
+      const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
+      const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
+      const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
+      const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
+      const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
+      const uint32_t id_mm = tc::idesc_bf16(C, GW, true, true);
+      const uint32_t id_q2 = tc::idesc_bf16(C, C, false, false);
+      const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
+      const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
+      const uint32_t id_dv = tc::idesc_bf16(C, HD, false, true);
+      auto load_chunk = [&](int c) {
+        const int t0 = (c_begin + c) * C;
+        tc::mbar_arrive_expect_tx(&bars[W_FULL], 4 * TILE);
+        tc::tma_load_3d(sm + P.q, &tmQ, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + P.k, &tmK, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + P.v, &tmV, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + P.o, &tmO, &bars[W_FULL], 0, t0, n);
+      };
+      auto load_bst = [&](int c, int g) {
+        const int row = (int)(((size_t)n * a.nchunks + c_begin + c) * S + g * GW);
+        tc::mbar_arrive_expect_tx(&bars[W_BST], GW * 128);
+        tc::tma_load_2d(sm + P.bst, &tmB, &bars[W_BST], 0, row);
+      };
+      load_chunk(nch - 1);
+      load_bst(nch - 1, 0);
+      bool ok = tc::mbar_wait(&bars[W_INIT], 0, abort);
+      for (int k = 0; k < nch && ok; ++k) {
+        const int c = nch - 1 - k;
+        ok = tc::mbar_wait(&bars[W_FULL], k & 1, abort);
+        if (ok && k > 0) ok = tc::mbar_wait(&bars[W_OUTFREE], (k - 1) & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        for (int k0 = 0; k0 < HD; k0 += 16)
+          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
+                       k0 > 0);
+        tc::mma_commit(&bars[W_P1]);
+        ok = tc::mbar_wait(&bars[W_P1M], k & 1, abort);
+        if (!ok) break;
+        for (int g = 0; g < NG && ok; ++g) {
+          const int u = k * NG + g;
+          if (u > 0) ok = tc::mbar_wait(&bars[W_Q2], (u - 1) & 1, abort);  // R and X free
+          if (!ok) break;
+          tc::tc_fence_after();
+          if (g > 0) {
+            // dV of the previous group of this chunk (its Q2m is in [w | da])
+            for (int k0 = 0; k0 < GW; k0 += 16)
+              tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
+                           id_dv, g > 1 || k0 > 0);
+            for (int k0 = 0; k0 < C; k0 += 16)
+              tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0),
+                           id_dv, true);
+            // no wait: the W_PROJ commit below completes only after these MMAs,
+            // and the epilogue rewrites Pk / w / da / gbst only after W_PROJ
+          }
+          const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
+          for (int k0 = 0; k0 < HD; k0 += 16) {
+            const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
+            tc::mma_bf16(tmem + BT_R + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
+          }
+          tc::mma_commit(&bars[W_PROJ]);
+          if (g > 0) load_bst(c, g);  // the previous group's G (the bst reader) completed before its W_Q2
+          ok = tc::mbar_wait(&bars[W_PK], u & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
+          tc::mma_commit(&bars[W_APREF]);
+          ok = tc::mbar_wait(&bars[W_W], u & 1, abort);
+          if (ok) ok = tc::mbar_wait(&bars[W_BST], u & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          for (int k0 = 0; k0 < HD; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
+                         id_gk, k0 > 0);
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.pk, k0, 0),
+                         id_gm, true);
+          tc::mma_commit(&bars[W_G]);
+          ok = tc::mbar_wait(&bars[W_DA], u & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          // dpk (in R) = tril^T dA + V gBst^T + P1m^T W
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_mnmajor(sbase + P.tril, k0, TILE), tc::desc_mnmajor(sbase + P.da, k0, 0),
+                         id_mm, k0 > 0);
+          for (int k0 = 0; k0 < HD; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gbst, k0, 0),
+                         id_gk, true);
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + BT_R, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         id_mm, true);
+          // Q2 (in X) = Pk W^T
+          for (int k0 = 0; k0 < GW; k0 += 16)
+            tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
+                         id_q2, k0 > 0);
+          // suffix state: gB += W^T dO, gA += dA^T 1
+          for (int k0 = 0; k0 < C; k0 += 16) {
+            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
+            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
+                         tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, true);
+          }
+          tc::mma_commit(&bars[W_DPK]);
+        }
+        if (!ok) break;
+        // dV of the last group, then dK
+        ok = tc::mbar_wait(&bars[W_Q2], (k * NG + NG - 1) & 1, abort);
+        if (!ok) break;
+        tc::tc_fence_after();
+        for (int k0 = 0; k0 < GW; k0 += 16)
+          tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0), id_dv,
+                       NG > 1 || k0 > 0);
+        for (int k0 = 0; k0 < C; k0 += 16)
+          tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0), id_dv,
+                       true);
+        for (int k0 = 0; k0 < a.LP; k0 += 16)
+          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
+                       id_dv, k0 > 0);
+        tc::mma_commit(&bars[W_OUT]);
+        if (k + 1 < nch) {
+          ok = tc::mbar_wait(&bars[W_OUT], k & 1, abort);  // all readers of the tiles and of bst done
+          if (!ok) break;
+          load_chunk(c - 1);
+          load_bst(c - 1, 0);
+        }
+      }
+      tc::mma_commit(&bars[W_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[W_FINAL], 0)) atomicExch(a.err, 2);
+    }
+    __syncwarp();
+  } else {
+    const int q4 = warp & 3, h = warp >> 2;
+    const int t = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int mrow = m64_row(q4, lane), mpar = lane >> 4;
+    float *sA = reinterpret_cast<float *>(sm + P.a0);
+    float *sGA = reinterpret_cast<float *>(sm + P.ga);
+    const float *sst = a.suf_state + ((size_t)n * a.nseg + seg) * E;
+    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
+      const int j = i / HD, d = i % HD;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(j, d >> 3) + (d & 7) * 2) =
+          __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
+    }
+    {
+      float v[8];
+      for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = (h * 64 + ch * 8 + e) <= t ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
+      }
+    }
+    for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end -> TMEM
+      const int g = 2 * b + mpar;
+      float v[32];
+      if (g < NG) {
+        const float *src = sst + S + (size_t)(g * GW + mrow) * HD + 32 * h;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = src[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      tc::tmem_st32(tmem + lane_off + T_GB + 64 * b + 32 * h, v);
+      if (h == 0) tc::tmem_st1(tmem + lane_off + T_GA + 16 * b, g < NG ? sst[g * GW + mrow] : 0.f);
+    }
+    tc::tmem_wait_st();
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    tc::named_bar_sync(1, NEPI_T);
+    tc::mbar_arrive(&bars[W_INIT]);
+
+    bool ok = true;
+    uint32_t esync = 0;
+    for (int k = 0; k < nch && ok; ++k) {
+      const int c = nch - 1 - k, cg = c_begin + c, tok0 = cg * C;
+      const int nt = min(C, a.T - tok0);
+      // chunk-start A (stored by the forward walk)
+      for (int s = threadIdx.x; s < S; s += NEPI_T) sA[s] = a.chunkA[((size_t)n * a.nchunks + cg) * S + s];
+      ok = tc::mbar_wait(&bars[W_P1], k & 1, abort);
+      if (!ok) break;
+      __syncwarp();
+      tc::tc_fence_after();
+      {
+        float v[32];
+        for (int hh = 0; hh < 2; ++hh) {
+          tc::tmem_ld32(tmem + lane_off + BT_X + 64 * h + 32 * hh, v);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (64 * h + 32 * hh + i > t) v[i] = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + h * TILE, t, 4 * hh + ch, v + 8 * ch);
+        }
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      ok = tc::mbar_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sA visible to all epilogue threads
+      if (!ok) break;
+      tc::mbar_arrive(&bars[W_P1M]);
+      for (int g = 0; g < NG && ok; ++g) {
+        const int u = k * NG + g;
+        float thK[8], thQ[8], inv[32];
+        ok = tc::mbar_wait(&bars[W_PROJ], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float pr[32];
+          tc::tmem_ld8(tmem + lane_off + BT_R + 8 * h, thK);
+          tc::tmem_ld8(tmem + lane_off + BT_R + 16 + 8 * h, thQ);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            thK[i] = tanh_fast(thK[i]);
+            thQ[i] = tanh_fast(thQ[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(thK + 4 * i, a.scale, pr + 16 * i);
+          if (t >= nt) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+          }
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.pk, t, 4 * h + ch, pr + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[W_PK]);
+        ok = tc::mbar_wait(&bars[W_APREF], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float ap[32], w[32];
+          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, ap);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, w + 16 * i);
+          const int sb = g * GW + 32 * h;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            inv[i] = __fdividef(1.f, sA[sb + i] + ap[i] + a.eps);
+            w[i] = t < nt ? w[i] * inv[i] : 0.f;
+          }
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w, t, 4 * h + ch, w + 8 * ch);
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[W_W]);
+        ok = tc::mbar_wait(&bars[W_G], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float G[32], pq[32];
+          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, G);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, pq + 16 * i);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;  // dA
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.da, t, 4 * h + ch, G + 8 * ch);
+          // suffix state (after this chunk) of group g: bf16 copy for the MMAs, gA to smem
+          float bv[32], av;
+          tc::tmem_ld32(tmem + lane_off + T_GB + 64 * (g >> 1) + 32 * h, bv);
+          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
+          tc::tmem_wait_ld();
+          if (mpar == (g & 1)) {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 4 * h + ch, bv + 8 * ch);
+            if (h == 0) sGA[mrow] = av;
+          }
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        ok = tc::mbar_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sGA complete (read after W_DPK)
+        if (!ok) break;
+        tc::mbar_arrive(&bars[W_DA]);
+        ok = tc::mbar_wait(&bars[W_DPK], u & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+        tc::tc_fence_after();
+        {
+          float dpk[32], pk[32], dp[8];
+          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, dpk);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) dpk[i] += sGA[32 * h + i];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_th(thK + 4 * i, a.scale, pk + 16 * i);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) table_probs_bwd(pk + 16 * i, dpk + 16 * i, thK + 4 * i, a.scale, dp + 4 * i);
+          tc::st_row_chunk(sbase + P.dproj, t, 2 * g + h, dp);
+          // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64)
+          float v[32];
+          for (int hh = 0; hh < 2; ++hh) {
+            tc::tmem_ld32(tmem + lane_off + BT_X + 64 * h + 32 * hh, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (64 * h + 32 * hh + i < t) v[i] = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, 4 * hh + ch, v + 8 * ch);
+          }
+        }
+        tc::fence_async_smem();
+        tc::tc_fence_before();
+        tc::mbar_arrive(&bars[W_Q2]);
+      }
+      if (!ok) break;
+      ok = tc::mbar_wait(&bars[W_OUT], k & 1, abort);
+      if (!ok) break;
+      __syncwarp();
+      tc::tc_fence_after();
+      {
+        float kv[32], vv[32];
+        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * h, kv);
+        tc::tmem_ld32(tmem + lane_off + T_DV + 32 * h, vv);
+        tc::tmem_wait_ld();
+        if (t < nt) {
+          __nv_bfloat16 *dk = a.dK + ((size_t)n * a.T + tok0 + t) * HD + 32 * h;
+          __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + 32 * h;
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            st_bf16x8_global(dk + 8 * ch, kv + 8 * ch);
+            st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars[W_OUTFREE]);
+    }
+    if (!ok && lane == 0) atomicExch(a.err, 1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == NEPI) {
+    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fast
+}  // namespace race

@@ -113,7 +113,7 @@ __host__ __device__ __forceinline__ FwdSmem fwd_smem_plan(int ngroups, int LP) {
 
 // barrier slots
 enum { B_QK0 = 0, B_QK1, B_V, B_PROJ, B_PK, B_APREF, B_W, B_SMAT, B_SMASK, B_GDONE, B_BST0, B_BST1, B_OUTFREE,
-       B_FINAL, B_COUNT };
+       B_FINAL, B_ESYNC, B_COUNT };
 
 __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     tc::mbar_init(&bars[B_BST1], NEPI_T);
     tc::mbar_init(&bars[B_OUTFREE], NEPI_T);
     tc::mbar_init(&bars[B_FINAL], 1);
+    tc::mbar_init(&bars[B_ESYNC], NEPI_T);
     tc::fence_mbar_init();
   }
   if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
@@ -293,7 +294,9 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       const int nt = min(C, a.T - tok0);
       const float *Acur = sA[c & 1];
       float *Anxt = sA[(c + 1) & 1];
-      ok = tc::mbar_wait(&bars[B_PROJ], c & 1, abort);
+      // the row-127 threads wrote this chunk's A during the previous one
+      ok = tc::mbar_sync(&bars[B_ESYNC], c & 1, abort);
+      if (ok) ok = tc::mbar_wait(&bars[B_PROJ], c & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();

@@ -7,6 +7,7 @@
 
 #include <mutex>
 
+#include "fast_bwd.cuh"
 #include "fast_fwd.cuh"
 #include "generic.cuh"
 
@@ -90,6 +91,41 @@ inline bool make_map(CUtensorMap *m, const void *base, int64_t N, int64_t T) {
 }
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Backward workspace: status | forward segment records | backward segment
+// records | per-chunk start state (A fp32, B bf16) written by the forward walk.
+struct BwdPlan {
+  Plan p;
+  size_t fwd_rec, bwd_rec, chunkA, chunkB, total;
+};
+
+inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms) {
+  BwdPlan b;
+  b.p = plan(N, T, S, sms);
+  const size_t E = (size_t)S + (size_t)S * fk::HD;
+  const size_t rec = align_up(sizeof(float) * (size_t)N * b.p.nseg * E, 256);
+  b.fwd_rec = 256;
+  b.bwd_rec = b.fwd_rec + rec;
+  b.chunkA = b.bwd_rec + rec;
+  b.chunkB = b.chunkA + align_up(sizeof(float) * (size_t)N * b.p.nchunks * S, 256);
+  b.total = b.chunkB + align_up(sizeof(uint16_t) * (size_t)N * b.p.nchunks * S * fk::HD, 256);
+  return b;
+}
+
+inline size_t bwd_workspace_bytes(int64_t N, int64_t T, int64_t S) { return bwd_plan(N, T, S, 256).total; }
+
+// 2-D map over the per-chunk B states viewed as [rows][64] bf16, box [64 x 64].
+inline bool make_rows_map(CUtensorMap *m, const void *base, int64_t rows) {
+  EncodeTiledFn enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)fk::HD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)fk::HD * 2};
+  cuuint32_t box[2] = {(cuuint32_t)fk::HD, (cuuint32_t)fk::GW};
+  cuuint32_t es[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 }  // namespace fasthost
 }  // namespace race

@@ -342,9 +342,10 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
 
 int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, const float *A0, const float *B0,
                          float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
-                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV) {
+                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, size_t rec_off = 0) {
   const int64_t S = 16 * L;
-  const fh::Plan pl = fh::plan(N, T, S, fh::sm_count());
+  fh::Plan pl = fh::plan(N, T, S, fh::sm_count());
+  if (rec_off) pl.rec_off = rec_off;
   fast_args(a, pl, N, T, L, eps, scale, planes_T, ws);
   if (!fh::make_map(&mK, K, N, T) || !fh::make_map(&mV, V, N, T))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable or bad tensor)");
@@ -371,6 +372,57 @@ int fast_forward(const void *Q, const void *K, const void *V, const float *plane
   RACE_TRY(set_smem(fk::fwd_readout_kernel, fs.total));
   fk::fwd_readout_kernel<<<(unsigned)(N * a.nseg), fk::NTHR, fs.total, s>>>(mQ, mK, mV, a);
   return check_launch("fast fwd_readout");
+}
+
+int fast_backward(const void *Q, const void *K, const void *V, const void *dO, const float *planes_T, void *dQ,
+                  void *dK, void *dV, const float *A0, const float *B0, const float *gA, const float *gB, float *dA0,
+                  float *dB0, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws, cudaStream_t s,
+                  bool totals_only) {
+  const int64_t S = 16 * L;
+  const fh::BwdPlan bp = fh::bwd_plan(N, T, S, fh::sm_count());
+  fk::FwdArgs fa;
+  CUtensorMap mQ, mK, mV, mO, mB;
+  // forward segment prefixes (exclusive, seeded with the carried-in state)
+  RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, nullptr, nullptr, N, T, L, eps, scale, ws, s, fa, mK, mV,
+                                bp.fwd_rec));
+  if (!fh::make_map(&mQ, Q, N, T) || !fh::make_map(&mO, dO, N, T) ||
+      !fh::make_rows_map(&mB, at<void>(ws, bp.chunkB), N * (int64_t)bp.p.nchunks * S))
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed (backward)");
+  fk::BwdArgs b;
+  b.N = (int)N;
+  b.T = (int)T;
+  b.L = (int)L;
+  b.LP = (int)(4 * L);
+  b.S = (int)S;
+  b.ngroups = (int)(S / fk::GW);
+  b.nseg = bp.p.nseg;
+  b.seg_chunks = bp.p.seg_chunks;
+  b.nchunks = bp.p.nchunks;
+  b.eps = eps;
+  b.scale = scale;
+  b.planes = planes_T;
+  b.fwd_state = at<float>(ws, bp.fwd_rec);
+  b.tot = at<float>(ws, bp.bwd_rec);
+  b.suf_state = at<float>(ws, bp.bwd_rec);
+  b.chunkA = at<float>(ws, bp.chunkA);
+  b.chunkB = at<__nv_bfloat16>(ws, bp.chunkB);
+  b.dQ = totals_only ? nullptr : static_cast<__nv_bfloat16 *>(dQ);
+  b.dK = static_cast<__nv_bfloat16 *>(dK);
+  b.dV = static_cast<__nv_bfloat16 *>(dV);
+  b.err = at<int>(ws, 0);
+  const fk::BwdSmem bs = fk::bwd_smem_plan(b.LP, b.S);
+  const unsigned grid = (unsigned)(N * bp.p.nseg);
+  RACE_TRY(set_smem(fk::bwd_fwd_kernel, bs.total));
+  fk::bwd_fwd_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, b);
+  RACE_TRY(check_launch("fast bwd_fwd"));
+  gen::Dims p = make_dims(N, T, S, fk::HD, eps);
+  p.G = bp.p.nseg;
+  RACE_TRY(launch_scan(at<float>(ws, bp.bwd_rec), totals_only ? nullptr : gA, totals_only ? nullptr : gB, dA0, dB0,
+                       p, 1, s));
+  if (totals_only) return RACE_OK;
+  RACE_TRY(set_smem(fk::bwd_rev_kernel, bs.total));
+  fk::bwd_rev_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, mB, b);
+  return check_launch("fast bwd_rev");
 }
 
 int check_fast_ptrs(std::initializer_list<const void *> ptrs) {
@@ -430,6 +482,8 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int
   RACE_TRY(check_nts(N, T, S, D));
   if ((op == RACE_OP_FWD_QKV || op == RACE_OP_STATE) && fh::eligible(dtype, D, L, P))
     *bytes = fh::fwd_workspace_bytes(N, T, S);
+  else if ((op == RACE_OP_BWD_QKV || op == RACE_OP_BWD_TOTALS) && fh::eligible(dtype, D, L, P))
+    *bytes = fh::bwd_workspace_bytes(N, T, S);
   else
     *bytes = generic_layout(op, N, T, S, D).total;
   return ok();
@@ -573,8 +627,15 @@ int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, in
   int64_t S = 0;
   RACE_TRY(check_lp(L, P, &S));
   RACE_TRY(check_nts(N, T, S, D));
-  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
   cudaStream_t s = as_stream(stream);
+  if (fh::eligible(dtype, D, L, P)) {
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::bwd_workspace_bytes(N, T, S)));
+    RACE_TRY(check_fast_ptrs({Q, K, V, dO, dQ, dK, dV}));
+    RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, L, eps,
+                           logit_scale, workspace, s, false));
+    return ok();
+  }
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
   if (dtype == RACE_F32)
     RACE_TRY(bwd_qkv_generic<float>((const float *)Q, (const float *)K, (const float *)V, (const float *)dO, planes_T,
                                     (float *)dQ, (float *)dK, (float *)dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, D,
@@ -641,8 +702,15 @@ int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V, const v
   int64_t S = 0;
   RACE_TRY(check_lp(L, P, &S));
   RACE_TRY(check_nts(N, T, S, D));
-  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total));
   cudaStream_t s = as_stream(stream);
+  if (fh::eligible(dtype, D, L, P)) {
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::bwd_workspace_bytes(N, T, S)));
+    RACE_TRY(check_fast_ptrs({Q, K, V, dO}));
+    RACE_TRY(fast_backward(Q, K, V, dO, planes_T, nullptr, nullptr, nullptr, A0, B0, nullptr, nullptr, gA_tot,
+                           gB_tot, N, T, L, eps, logit_scale, workspace, s, true));
+    return ok();
+  }
+  RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total));
   if (dtype == RACE_F32)
     RACE_TRY(bwd_totals_generic<float>((const float *)Q, (const float *)K, (const float *)V, (const float *)dO,
                                        planes_T, A0, B0, gA_tot, gB_tot, N, T, D, L, P, eps, logit_scale, workspace,

@@ -242,6 +242,8 @@ def bwd_qkv(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0
         _lib.check(lib.race_bwd_qkv(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T), _ptr(dQ),
                                     _ptr(dK), _ptr(dV), _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), _ptr(dA0), _ptr(dB0),
                                     N, T, D, L, P, float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_bwd_qkv")
+        if fast_path(Q.dtype, D, L, P):
+            _check_status(ws, "race_bwd_qkv")
     return (dQ, dK, dV, dA0, dB0) if return_state_grad else (dQ, dK, dV)
 
 
@@ -275,6 +277,8 @@ def bwd_totals(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None,
         _lib.check(lib.race_bwd_sharded_phaseA(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T),
                                                _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), N, T, D, L, P, float(eps),
                                                scale, _ptr(ws), nb, _stream(dev)), "race_bwd_sharded_phaseA")
+        if fast_path(Q.dtype, D, L, P):
+            _check_status(ws, "race_bwd_sharded_phaseA")
     return gA, gB
 
 
