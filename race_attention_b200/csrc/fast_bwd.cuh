@@ -197,13 +197,14 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
       const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
       const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
       const uint32_t id_dq = tc::idesc_bf16(C, HD, false, true);
-      auto load_chunk = [&](int c) {
+      const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o;
+      auto load_chunk = [=, &tmQ, &tmK, &tmV, &tmO](int c) {
         const int t0 = (c_begin + c) * C;
         tc::mbar_arrive_expect_tx(&bars[W_FULL], 4 * TILE);
-        tc::tma_load_3d(sm + P.q, &tmQ, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + P.k, &tmK, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + P.v, &tmV, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + P.o, &tmO, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + oq, &tmQ, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + ok_, &tmK, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + ov, &tmV, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + oo, &tmO, &bars[W_FULL], 0, t0, n);
       };
       load_chunk(0);
       bool ok = tc::mbar_wait(&bars[W_INIT], 0, abort);
@@ -293,7 +294,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const int mrow = m64_row(q4, lane), mpar = lane >> 4;
-    float *sA[2] = {reinterpret_cast<float *>(sm + P.a0), reinterpret_cast<float *>(sm + P.a1)};
+    float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
+    float *const sA1 = reinterpret_cast<float *>(sm + P.a1);
     const float *st0 = a.fwd_state + ((size_t)n * a.nseg + seg) * E;
     // ---- prologue
     for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
       }
     }
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sA[0][s] = st0[s];
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = st0[s];
     for (int b = 0; b < nblk; ++b) {  // forward state -> TMEM (M=64 layout), this lane's row
       const int g = 2 * b + mpar;
       float v[32];
@@ -333,8 +335,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     for (int c = 0; c < nch && ok; ++c) {
       const int cg = c_begin + c, tok0 = cg * C;
       const int nt = min(C, a.T - tok0);
-      const float *Acur = sA[c & 1];
-      float *Anxt = sA[(c + 1) & 1];
+      const float *Acur = (c & 1) ? sA1 : sA0;
+      float *Anxt = (c & 1) ? sA0 : sA1;
       // the row-127 threads wrote this chunk's A during the previous one
       ok = tc::mbar_sync(&bars[W_ESYNC], c & 1, abort);
       if (!ok) break;
@@ -566,18 +568,21 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
       const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
       const uint32_t id_dv = tc::idesc_bf16(C, HD, false, true);
-      auto load_chunk = [&](int c) {
+      const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o;
+      auto load_chunk = [=, &tmQ, &tmK, &tmV, &tmO](int c) {
         const int t0 = (c_begin + c) * C;
         tc::mbar_arrive_expect_tx(&bars[W_FULL], 4 * TILE);
-        tc::tma_load_3d(sm + P.q, &tmQ, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + P.k, &tmK, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + P.v, &tmV, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + P.o, &tmO, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + oq, &tmQ, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + ok_, &tmK, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + ov, &tmV, &bars[W_FULL], 0, t0, n);
+        tc::tma_load_3d(sm + oo, &tmO, &bars[W_FULL], 0, t0, n);
       };
-      auto load_bst = [&](int c, int g) {
-        const int row = (int)(((size_t)n * a.nchunks + c_begin + c) * S + g * GW);
+      const uint32_t obst = P.bst;
+      const int nchunks = a.nchunks;
+      auto load_bst = [=, &tmB](int c, int g) {
+        const int row = (int)(((size_t)n * nchunks + c_begin + c) * S + g * GW);
         tc::mbar_arrive_expect_tx(&bars[W_BST], GW * 128);
-        tc::tma_load_2d(sm + P.bst, &tmB, &bars[W_BST], 0, row);
+        tc::tma_load_2d(sm + obst, &tmB, &bars[W_BST], 0, row);
       };
       load_chunk(nch - 1);
       load_bst(nch - 1, 0);

@@ -88,16 +88,14 @@ __device__ __forceinline__ void table_probs(const float *proj4, float scale, flo
 // --------------------------------------------------------------------------
 // shared-memory plan (byte offsets from a 1024-aligned base)
 struct FwdSmem {
-  uint32_t q[2], k[2], v, pk, w, bst, tril, planes, a0, a1, bars, total;
+  uint32_t q, k, v, pk, w, bst, tril, planes, a0, a1, bars, total;  // q, k: 2 stages of TILE bytes each
 };
 
 __host__ __device__ __forceinline__ FwdSmem fwd_smem_plan(int ngroups, int LP) {
   FwdSmem m;
   uint32_t o = 0;
-  m.q[0] = o; o += TILE;
-  m.q[1] = o; o += TILE;
-  m.k[0] = o; o += TILE;
-  m.k[1] = o; o += TILE;
+  m.q = o; o += 2 * TILE;
+  m.k = o; o += 2 * TILE;
   m.v = o; o += TILE;
   m.pk = o; o += 2 * TILE;
   m.w = o; o += 2 * TILE;
@@ -168,12 +166,12 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       tc::prefetch_tmap(&tmV);
       const int t0 = c_begin * C;
       tc::mbar_arrive_expect_tx(&bars[B_QK0], 2 * TILE);
-      tc::tma_load_3d(sm + P.q[0], &tmQ, &bars[B_QK0], 0, t0, n);
-      tc::tma_load_3d(sm + P.k[0], &tmK, &bars[B_QK0], 0, t0, n);
+      tc::tma_load_3d(sm + P.q, &tmQ, &bars[B_QK0], 0, t0, n);
+      tc::tma_load_3d(sm + P.k, &tmK, &bars[B_QK0], 0, t0, n);
       if (nch > 1) {
         tc::mbar_arrive_expect_tx(&bars[B_QK1], 2 * TILE);
-        tc::tma_load_3d(sm + P.q[1], &tmQ, &bars[B_QK1], 0, t0 + C, n);
-        tc::tma_load_3d(sm + P.k[1], &tmK, &bars[B_QK1], 0, t0 + C, n);
+        tc::tma_load_3d(sm + P.q + TILE, &tmQ, &bars[B_QK1], 0, t0 + C, n);
+        tc::tma_load_3d(sm + P.k + TILE, &tmK, &bars[B_QK1], 0, t0 + C, n);
       }
       tc::mbar_arrive_expect_tx(&bars[B_V], TILE);
       tc::tma_load_3d(sm + P.v, &tmV, &bars[B_V], 0, t0, n);
@@ -194,8 +192,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         tc::tc_fence_after();
         for (int k0 = 0; k0 < HD; k0 += 16) {
           const uint64_t bp = tc::desc_kmajor(sbase + P.planes, k0, 0);
-          tc::mma_bf16(tmem + T_PK, tc::desc_kmajor(sbase + P.k[st], k0, TILE), bp, id_proj, k0 > 0);
-          tc::mma_bf16(tmem + T_PQ, tc::desc_kmajor(sbase + P.q[st], k0, TILE), bp, id_proj, k0 > 0);
+          tc::mma_bf16(tmem + T_PK, tc::desc_kmajor(sbase + P.k + st * TILE, k0, TILE), bp, id_proj, k0 > 0);
+          tc::mma_bf16(tmem + T_PQ, tc::desc_kmajor(sbase + P.q + st * TILE, k0, TILE), bp, id_proj, k0 > 0);
         }
         tc::mma_commit(&bars[B_PROJ]);
         for (int g = 0; g < a.ngroups && ok; ++g) {
@@ -207,8 +205,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
             // the proj MMAs that read this Q/K stage completed before the
             // epilogue could produce Pk: refill the stage with chunk c+2
             tc::mbar_arrive_expect_tx(&bars[B_QK0 + st], 2 * TILE);
-            tc::tma_load_3d(sm + P.q[st], &tmQ, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
-            tc::tma_load_3d(sm + P.k[st], &tmK, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
+            tc::tma_load_3d(sm + P.q + st * TILE, &tmQ, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
+            tc::tma_load_3d(sm + P.k + st * TILE, &tmK, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
           }
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + T_G, tc::desc_kmajor(sbase + P.tril, k0, TILE),
@@ -256,7 +254,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     const int q4 = warp & 3, h = warp >> 2;
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    float *sA[2] = {reinterpret_cast<float *>(sm + P.a0), reinterpret_cast<float *>(sm + P.a1)};
+    float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
+    float *const sA1 = reinterpret_cast<float *>(sm + P.a1);
     // ---- prologue: planes (bf16, K-major rows j), tril, A_start, Bstate
     for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
       const int j = i / HD, d = i % HD;
@@ -272,7 +271,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
       }
     }
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sA[0][s] = state0[s];
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = state0[s];
     for (int g = 0; g < a.ngroups; ++g) {
       float v[32];
       const float *src = state0 + S + (size_t)(g * GB + t) * HD + 32 * h;
@@ -292,8 +291,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     for (int c = 0; c < nch && ok; ++c) {
       const int tok0 = (c_begin + c) * C;
       const int nt = min(C, a.T - tok0);
-      const float *Acur = sA[c & 1];
-      float *Anxt = sA[(c + 1) & 1];
+      const float *Acur = (c & 1) ? sA1 : sA0;
+      float *Anxt = (c & 1) ? sA0 : sA1;
       // the row-127 threads wrote this chunk's A during the previous one
       ok = tc::mbar_sync(&bars[B_ESYNC], c & 1, abort);
       if (ok) ok = tc::mbar_wait(&bars[B_PROJ], c & 1, abort);
@@ -326,20 +325,26 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         __syncwarp();
         tc::tc_fence_after();
         {
-          float pj[16], pq[64], ap[64];
+          float pj[16], pq[64], ap0[32], ap1[32];
           tc::tmem_ld16(tmem + lane_off + T_PQ + j0, pj);
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, *reinterpret_cast<float(*)[32]>(ap));
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, *reinterpret_cast<float(*)[32]>(ap + 32));
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, ap0);
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, ap1);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pq + 16 * i);
           const int sb = g * GB + 64 * h;
           if (t == C - 1) {
-#pragma unroll 8
-            for (int i = 0; i < 64; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              Anxt[sb + i] = Acur[sb + i] + ap0[i];
+              Anxt[sb + 32 + i] = Acur[sb + 32 + i] + ap1[i];
+            }
           }
 #pragma unroll
-          for (int i = 0; i < 64; ++i) pq[i] = __fdividef(pq[i], Acur[sb + i] + ap[i] + a.eps);
+          for (int i = 0; i < 32; ++i) {
+            pq[i] = __fdividef(pq[i], Acur[sb + i] + ap0[i] + a.eps);
+            pq[32 + i] = __fdividef(pq[32 + i], Acur[sb + 32 + i] + ap1[i] + a.eps);
+          }
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, pq + 8 * ch);
         }
@@ -352,15 +357,20 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         __syncwarp();
         tc::tc_fence_after();
         {
-          float sv[64];
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, *reinterpret_cast<float(*)[32]>(sv));
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+          float sv0[32], sv1[32];
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, sv0);
+          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, sv1);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (64 * h + i > t) sv[i] = 0.f;
+          for (int i = 0; i < 32; ++i) {
+            if (64 * h + i > t) sv0[i] = 0.f;
+            if (64 * h + 32 + i > t) sv1[i] = 0.f;
+          }
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, sv + 8 * ch);
+          for (int ch = 0; ch < 4; ++ch) {
+            tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, sv0 + 8 * ch);
+            tc::st_row_chunk(sbase + P.w + h * TILE, t, 4 + ch, sv1 + 8 * ch);
+          }
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -419,16 +429,14 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
 // over one (stream, segment), written as a record of the chunk_scan layout.
 // Same warp roles; A_tot comes from an MMA against a ones column.
 struct TotSmem {
-  uint32_t k[2], v[2], pk, ones, planes, bars, total;
+  uint32_t k, v, pk, ones, planes, bars, total;  // k, v: 2 stages of TILE bytes each
 };
 
 __host__ __device__ __forceinline__ TotSmem tot_smem_plan(int ngroups, int LP) {
   TotSmem m;
   uint32_t o = 0;
-  m.k[0] = o; o += TILE;
-  m.k[1] = o; o += TILE;
-  m.v[0] = o; o += TILE;
-  m.v[1] = o; o += TILE;
+  m.k = o; o += 2 * TILE;
+  m.v = o; o += 2 * TILE;
   m.pk = o; o += (uint32_t)ngroups * 2 * TILE;
   m.ones = o; o += TILE;
   m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
@@ -482,8 +490,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       tc::prefetch_tmap(&tmV);
       for (int c = 0; c < 2 && c < nch; ++c) {
         tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + c], 2 * TILE);
-        tc::tma_load_3d(sm + P.k[c], &tmK, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
-        tc::tma_load_3d(sm + P.v[c], &tmV, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
+        tc::tma_load_3d(sm + P.k + c * TILE, &tmK, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
+        tc::tma_load_3d(sm + P.v + c * TILE, &tmV, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
       }
       const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
       const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
@@ -495,7 +503,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
         if (!ok) break;
         tc::tc_fence_after();
         for (int k0 = 0; k0 < HD; k0 += 16)
-          tc::mma_bf16(tmem + 0, tc::desc_kmajor(sbase + P.k[st], k0, TILE),
+          tc::mma_bf16(tmem + 0, tc::desc_kmajor(sbase + P.k + st * TILE, k0, TILE),
                        tc::desc_kmajor(sbase + P.planes, k0, 0), id_proj, k0 > 0);
         tc::mma_commit(&bars[TB_PROJ]);
         ok = tc::mbar_wait(&bars[TB_PK], c & 1, abort);
@@ -505,7 +513,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           const uint32_t pk = sbase + P.pk + (uint32_t)g * 2 * TILE;
           for (int k0 = 0; k0 < C; k0 += 16) {
             const uint64_t ap = tc::desc_mnmajor(pk, k0, TILE);
-            tc::mma_bf16(tmem + 64 + 64 * g, ap, tc::desc_mnmajor(sbase + P.v[st], k0, TILE), id_bupd,
+            tc::mma_bf16(tmem + 64 + 64 * g, ap, tc::desc_mnmajor(sbase + P.v + st * TILE, k0, TILE), id_bupd,
                          c > 0 || k0 > 0);
             tc::mma_bf16(tmem + 192 + 16 * g, ap, tc::desc_mnmajor(sbase + P.ones, k0, TILE), id_ones,
                          c > 0 || k0 > 0);
@@ -516,8 +524,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           ok = tc::mbar_wait(&bars[TB_DONE], c & 1, abort);
           if (!ok) break;
           tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + st], 2 * TILE);
-          tc::tma_load_3d(sm + P.k[st], &tmK, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
-          tc::tma_load_3d(sm + P.v[st], &tmV, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
+          tc::tma_load_3d(sm + P.k + st * TILE, &tmK, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
+          tc::tma_load_3d(sm + P.v + st * TILE, &tmV, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
         }
       }
       tc::mma_commit(&bars[TB_FINAL]);
