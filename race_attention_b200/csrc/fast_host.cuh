@@ -77,17 +77,37 @@ inline EncodeTiledFn encoder() {
   return fn;
 }
 
+// Tensor-map encoding is a driver-API call and needs a current context on the
+// calling thread; a thread that has only queried the runtime (e.g. torch's
+// autograd worker) may not have one yet.  Binding the current device's primary
+// context is a no-op when it is already current.
+inline bool bind_current_context() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess;
+}
+
+// result of the last failed encode on this thread (for error messages)
+inline int &last_encode_status() {
+  static thread_local int st = 0;
+  return st;
+}
+
 // 3-D map over a [N][T][64] bf16 tensor, box [1][128][64], 128-byte swizzle.
 inline bool make_map(CUtensorMap *m, const void *base, int64_t N, int64_t T) {
   EncodeTiledFn enc = encoder();
-  if (!enc) return false;
+  if (!enc) {
+    last_encode_status() = -1;
+    return false;
+  }
   cuuint64_t dims[3] = {(cuuint64_t)fk::HD, (cuuint64_t)T, (cuuint64_t)N};
   cuuint64_t strides[2] = {(cuuint64_t)fk::HD * 2, (cuuint64_t)T * fk::HD * 2};
   cuuint32_t box[3] = {(cuuint32_t)fk::HD, (cuuint32_t)fk::C, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  last_encode_status() = (int)r;
+  return r == CUDA_SUCCESS;
 }
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -117,14 +137,19 @@ inline size_t bwd_workspace_bytes(int64_t N, int64_t T, int64_t S) { return bwd_
 // 2-D map over the per-chunk B states viewed as [rows][64] bf16, box [64 x 64].
 inline bool make_rows_map(CUtensorMap *m, const void *base, int64_t rows) {
   EncodeTiledFn enc = encoder();
-  if (!enc) return false;
+  if (!enc) {
+    last_encode_status() = -1;
+    return false;
+  }
   cuuint64_t dims[2] = {(cuuint64_t)fk::HD, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)fk::HD * 2};
   cuuint32_t box[2] = {(cuuint32_t)fk::HD, (cuuint32_t)fk::GW};
   cuuint32_t es[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  last_encode_status() = (int)r;
+  return r == CUDA_SUCCESS;
 }
 
 }  // namespace fasthost

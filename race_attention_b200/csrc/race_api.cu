@@ -344,11 +344,16 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
                          float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
                          cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, size_t rec_off = 0) {
   const int64_t S = 16 * L;
+  if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
   fh::Plan pl = fh::plan(N, T, S, fh::sm_count());
   if (rec_off) pl.rec_off = rec_off;
   fast_args(a, pl, N, T, L, eps, scale, planes_T, ws);
-  if (!fh::make_map(&mK, K, N, T) || !fh::make_map(&mV, V, N, T))
-    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed (driver entry point unavailable or bad tensor)");
+  if (!fh::make_map(&mK, K, N, T))
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(K %p, N=%lld, T=%lld) failed: CUresult %d", K, (long long)N,
+                (long long)T, fh::last_encode_status());
+  if (!fh::make_map(&mV, V, N, T))
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(V %p, N=%lld, T=%lld) failed: CUresult %d", V, (long long)N,
+                (long long)T, fh::last_encode_status());
   cudaError_t e = cudaMemsetAsync(at<int>(ws, pl.status_off), 0, sizeof(int), s);
   if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   const fk::TotSmem ts = fk::tot_smem_plan(a.ngroups, a.LP);
@@ -366,7 +371,8 @@ int fast_forward(const void *Q, const void *K, const void *V, const float *plane
   fk::FwdArgs a;
   CUtensorMap mQ, mK, mV;
   RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV));
-  if (!fh::make_map(&mQ, Q, N, T)) return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed for Q");
+  if (!fh::make_map(&mQ, Q, N, T))
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(Q) failed: CUresult %d", fh::last_encode_status());
   a.out = static_cast<__nv_bfloat16 *>(out);
   const fk::FwdSmem fs = fk::fwd_smem_plan(a.ngroups, a.LP);
   RACE_TRY(set_smem(fk::fwd_readout_kernel, fs.total));
@@ -387,7 +393,8 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
                                 bp.fwd_rec));
   if (!fh::make_map(&mQ, Q, N, T) || !fh::make_map(&mO, dO, N, T) ||
       !fh::make_rows_map(&mB, at<void>(ws, bp.chunkB), N * (int64_t)bp.p.nchunks * S))
-    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed (backward)");
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed in the backward: CUresult %d",
+                fh::last_encode_status());
   fk::BwdArgs b;
   b.N = (int)N;
   b.T = (int)T;
