@@ -137,7 +137,7 @@ constexpr uint32_t BT_X = 0, BT_R = 128, BT_ST = 192;
 enum { W_FULL = 0, W_INIT, W_P1, W_P1M, W_PROJ, W_PK, W_APREF, W_W, W_G, W_DA, W_DPK, W_Q2, W_DV, W_OUT, W_OUTFREE,
        W_BST, W_FINAL, W_ESYNC, W_COUNT };
 
-// barriers the 256 epilogue threads arrive on; the rest complete on one arrival
+// barriers all epilogue threads arrive on; the rest complete on one arrival
 __device__ __forceinline__ void bwd_init_bars(uint64_t *bars) {
   for (int i = 0; i < W_COUNT; ++i) {
     const bool epi = i == W_INIT || i == W_P1M || i == W_PK || i == W_W || i == W_DA || i == W_Q2 ||
@@ -289,10 +289,13 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     }
     __syncwarp();
   } else {
-    // ========================================================= epilogue warps
-    const int q4 = warp & 3, h = warp >> 2;
+    // ============================== epilogue warps: row t, column quarter hq
+    // (in a 64-bucket group, quarter hq owns table 4g + hq: buckets [16hq, 16hq+16))
+    const int q4 = warp & 3, hq = warp >> 2;
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
+    const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
     const int mrow = m64_row(q4, lane), mpar = lane >> 4;
     float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
     float *const sA1 = reinterpret_cast<float *>(sm + P.a1);
@@ -305,25 +308,25 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     }
     {
       float v[8];
-      for (int ch = 0; ch < 8; ++ch) {
+      for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (h * 64 + ch * 8 + e) <= t ? 1.f : 0.f;
-        tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
+        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) <= t ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
     for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = st0[s];
-    for (int b = 0; b < nblk; ++b) {  // forward state -> TMEM (M=64 layout), this lane's row
+    for (int b = 0; b < nblk; ++b) {  // forward state -> TMEM (M=64 layout), this lane's row, d in [16hq, +16)
       const int g = 2 * b + mpar;
-      float v[32];
+      float v[16];
       if (g < NG) {
-        const float *src = st0 + S + (size_t)(g * GW + mrow) * HD + 32 * h;
+        const float *src = st0 + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = src[i];
+        for (int i = 0; i < 16; ++i) v[i] = src[i];
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
       }
-      tc::tmem_st32(tmem + lane_off + T_BF + 64 * b + 32 * h, v);
+      tc::tmem_st16(tmem + lane_off + T_BF + 64 * b + 16 * hq, v);
     }
     tc::tmem_wait_st();
     tc::fence_async_smem();
@@ -348,53 +351,49 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
       tc::tc_fence_after();
       {
         float v[32];
-        for (int hh = 0; hh < 2; ++hh) {
-          tc::tmem_ld32(tmem + lane_off + BT_X + 64 * h + 32 * hh, v);
-          tc::tmem_wait_ld();
+        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * hq, v);
+        tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (64 * h + 32 * hh + i > t) v[i] = 0.f;
+        for (int i = 0; i < 32; ++i)
+          if (32 * hq + i > t) v[i] = 0.f;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + h * TILE, t, 4 * hh + ch, v + 8 * ch);
-        }
+        for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(&bars[W_P1M]);
       for (int g = 0; g < NG && ok; ++g) {
         const int u = c * NG + g;
-        float thQ[8], inv[32];
+        float thQ[4], inv[16];
         // ---- Pk, pq
         ok = tc::mbar_wait(&bars[W_PROJ], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
         {
-          float pk8[8], pr[32];
-          tc::tmem_ld8(tmem + lane_off + BT_R + 8 * h, pk8);
-          tc::tmem_ld8(tmem + lane_off + BT_R + 16 + 8 * h, thQ);
+          float pk4[4], pr[16];
+          tc::tmem_ld4(tmem + lane_off + BT_R + 4 * hq, pk4);
+          tc::tmem_ld4(tmem + lane_off + BT_R + 16 + 4 * hq, thQ);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            pk8[i] = tanh_fast(pk8[i]);
+          for (int i = 0; i < 4; ++i) {
+            pk4[i] = tanh_fast(pk4[i]);
             thQ[i] = tanh_fast(thQ[i]);
           }
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(pk8 + 4 * i, a.scale, pr + 16 * i);
+          table_probs_th(pk4, a.scale, pr);
           if (t >= nt) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+            for (int i = 0; i < 16; ++i) pr[i] = 0.f;
           }
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.pk, t, 4 * h + ch, pr + 8 * ch);
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, pr + 16 * i);
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
+          table_probs_th(thQ, a.scale, pr);
           if (t >= nt) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+            for (int i = 0; i < 16; ++i) pr[i] = 0.f;
           }
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w, t, 4 * h + ch, pr + 8 * ch);
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, pr + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -405,32 +404,30 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         __syncwarp();
         tc::tc_fence_after();
         {
-          float ap[32], pq[32];
-          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, ap);
+          float ap[16], pq[16], bv[16];
+          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, ap);
+          tc::tmem_ld16(tmem + lane_off + T_BF + 64 * (g >> 1) + 16 * hq, bv);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::ld_row_chunk(sbase + P.w, t, 4 * h + ch, pq + 8 * ch);
-          const int sb = g * GW + 32 * h;
+          for (int ch = 0; ch < 2; ++ch) tc::ld_row_chunk(sbase + P.w, t, 2 * hq + ch, pq + 8 * ch);
+          const int sb = g * GW + 16 * hq;
           if (t == C - 1) {
-#pragma unroll 8
-            for (int i = 0; i < 32; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
           }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < 16; ++i) {
             inv[i] = __fdividef(1.f, Acur[sb + i] + ap[i] + a.eps);
             pq[i] *= inv[i];
           }
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w, t, 4 * h + ch, pq + 8 * ch);
-          float bv[32];
-          tc::tmem_ld32(tmem + lane_off + T_BF + 64 * (g >> 1) + 32 * h, bv);
-          tc::tmem_wait_ld();
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, pq + 8 * ch);
           if (mpar == (g & 1)) {
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.bst, mrow, 4 * h + ch, bv + 8 * ch);
-            __nv_bfloat16 *dst = a.chunkB + (((size_t)n * a.nchunks + cg) * S + g * GW + mrow) * HD + 32 * h;
+            for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst, mrow, 2 * hq + ch, bv + 8 * ch);
+            __nv_bfloat16 *dst = a.chunkB + (((size_t)n * a.nchunks + cg) * S + g * GW + mrow) * HD + 16 * hq;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) st_bf16x8_global(dst + 8 * ch, bv + 8 * ch);
+            for (int ch = 0; ch < 2; ++ch) st_bf16x8_global(dst + 8 * ch, bv + 8 * ch);
           }
         }
         tc::fence_async_smem();
@@ -442,49 +439,47 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         __syncwarp();
         tc::tc_fence_after();
         {
-          float G[32], pq[32], da[32];
-          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, G);
+          float G[16], pq[16], da[16];
+          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, G);
           tc::tmem_wait_ld();
+          table_probs_th(thQ, a.scale, pq);
 #pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, pq + 16 * i);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < 16; ++i) {
             const float gi = G[i] * inv[i];           // dpq
             da[i] = -pq[i] * inv[i] * gi;              // dA
             G[i] = gi;
           }
           if (t >= nt) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < 16; ++i) {
               da[i] = 0.f;
               G[i] = 0.f;
             }
           }
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.da, t, 4 * h + ch, da + 8 * ch);
-          float dp[8];
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_bwd(pq + 16 * i, G + 16 * i, thQ + 4 * i, a.scale, dp + 4 * i);
-          tc::st_row_chunk(sbase + P.dproj, t, 2 * g + h, dp);
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, da + 8 * ch);
+          float dp[4];
+          table_probs_bwd(pq, G, thQ, a.scale, dp);
+          tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::mbar_arrive(&bars[W_DA]);
       }
       if (!ok) break;
-      // ---- dQ
+      // ---- dQ, d in [16hq, 16hq+16)
       ok = tc::mbar_wait(&bars[W_OUT], c & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
       {
-        float ov[32];
-        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * h, ov);
+        float ov[16];
+        tc::tmem_ld16(tmem + lane_off + BT_X + 16 * hq, ov);
         tc::tmem_wait_ld();
         if (t < nt && a.dQ != nullptr) {
-          __nv_bfloat16 *dst = a.dQ + ((size_t)n * a.T + tok0 + t) * HD + 32 * h;
+          __nv_bfloat16 *dst = a.dQ + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) st_bf16x8_global(dst + 8 * ch, ov + 8 * ch);
+          for (int ch = 0; ch < 2; ++ch) st_bf16x8_global(dst + 8 * ch, ov + 8 * ch);
         }
       }
       tc::tc_fence_before();
@@ -497,15 +492,15 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
       float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
       for (int b = 0; b < nblk; ++b) {
         const int g = 2 * b + mpar;
-        float bv[32], av;
-        tc::tmem_ld32(tmem + lane_off + T_GB + 64 * b + 32 * h, bv);
+        float bv[16], av;
+        tc::tmem_ld16(tmem + lane_off + T_GB + 64 * b + 16 * hq, bv);
         tc::tmem_ld1(tmem + lane_off + T_GA + 16 * b, av);
         tc::tmem_wait_ld();
         if (g < NG) {
-          float *dst = rec + S + (size_t)(g * GW + mrow) * HD + 32 * h;
+          float *dst = rec + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) dst[i] = bv[i];
-          if (h == 0) rec[g * GW + mrow] = av;
+          for (int i = 0; i < 16; ++i) dst[i] = bv[i];
+          if (hq == 0) rec[g * GW + mrow] = av;
         }
       }
     } else if (nch == 0) {
@@ -694,9 +689,13 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     }
     __syncwarp();
   } else {
-    const int q4 = warp & 3, h = warp >> 2;
+    // ============================== epilogue warps: row t, column quarter hq
+    // (in a 64-bucket group, quarter hq owns table 4g + hq: buckets [16hq, 16hq+16))
+    const int q4 = warp & 3, hq = warp >> 2;
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
+    const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
     const int mrow = m64_row(q4, lane), mpar = lane >> 4;
     float *sA = reinterpret_cast<float *>(sm + P.a0);
     float *sGA = reinterpret_cast<float *>(sm + P.ga);
@@ -708,25 +707,25 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     }
     {
       float v[8];
-      for (int ch = 0; ch < 8; ++ch) {
+      for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (h * 64 + ch * 8 + e) <= t ? 1.f : 0.f;
-        tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
+        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) <= t ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
-    for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end -> TMEM
+    for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end -> TMEM, d in [16hq, +16)
       const int g = 2 * b + mpar;
-      float v[32];
+      float v[16];
       if (g < NG) {
-        const float *src = sst + S + (size_t)(g * GW + mrow) * HD + 32 * h;
+        const float *src = sst + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = src[i];
+        for (int i = 0; i < 16; ++i) v[i] = src[i];
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
       }
-      tc::tmem_st32(tmem + lane_off + T_GB + 64 * b + 32 * h, v);
-      if (h == 0) tc::tmem_st1(tmem + lane_off + T_GA + 16 * b, g < NG ? sst[g * GW + mrow] : 0.f);
+      tc::tmem_st16(tmem + lane_off + T_GB + 64 * b + 16 * hq, v);
+      if (hq == 0) tc::tmem_st1(tmem + lane_off + T_GA + 16 * b, g < NG ? sst[g * GW + mrow] : 0.f);
     }
     tc::tmem_wait_st();
     tc::fence_async_smem();
@@ -747,15 +746,13 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       tc::tc_fence_after();
       {
         float v[32];
-        for (int hh = 0; hh < 2; ++hh) {
-          tc::tmem_ld32(tmem + lane_off + BT_X + 64 * h + 32 * hh, v);
-          tc::tmem_wait_ld();
+        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * hq, v);
+        tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (64 * h + 32 * hh + i > t) v[i] = 0.f;
+        for (int i = 0; i < 32; ++i)
+          if (32 * hq + i > t) v[i] = 0.f;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + h * TILE, t, 4 * hh + ch, v + 8 * ch);
-        }
+        for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
@@ -764,29 +761,28 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       tc::mbar_arrive(&bars[W_P1M]);
       for (int g = 0; g < NG && ok; ++g) {
         const int u = k * NG + g;
-        float thK[8], thQ[8], inv[32];
+        float thK[4], thQ[4], inv[16];
         ok = tc::mbar_wait(&bars[W_PROJ], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
         {
-          float pr[32];
-          tc::tmem_ld8(tmem + lane_off + BT_R + 8 * h, thK);
-          tc::tmem_ld8(tmem + lane_off + BT_R + 16 + 8 * h, thQ);
+          float pr[16];
+          tc::tmem_ld4(tmem + lane_off + BT_R + 4 * hq, thK);
+          tc::tmem_ld4(tmem + lane_off + BT_R + 16 + 4 * hq, thQ);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < 4; ++i) {
             thK[i] = tanh_fast(thK[i]);
             thQ[i] = tanh_fast(thQ[i]);
           }
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(thK + 4 * i, a.scale, pr + 16 * i);
+          table_probs_th(thK, a.scale, pr);
           if (t >= nt) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+            for (int i = 0; i < 16; ++i) pr[i] = 0.f;
           }
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.pk, t, 4 * h + ch, pr + 8 * ch);
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -796,19 +792,18 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         __syncwarp();
         tc::tc_fence_after();
         {
-          float ap[32], w[32];
-          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, ap);
+          float ap[16], w[16];
+          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, ap);
           tc::tmem_wait_ld();
+          table_probs_th(thQ, a.scale, w);
+          const int sb = g * GW + 16 * hq;
 #pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, w + 16 * i);
-          const int sb = g * GW + 32 * h;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < 16; ++i) {
             inv[i] = __fdividef(1.f, sA[sb + i] + ap[i] + a.eps);
             w[i] = t < nt ? w[i] * inv[i] : 0.f;
           }
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w, t, 4 * h + ch, w + 8 * ch);
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, w + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -818,24 +813,21 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         __syncwarp();
         tc::tc_fence_after();
         {
-          float G[32], pq[32];
-          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, G);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(thQ + 4 * i, a.scale, pq + 16 * i);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;  // dA
-#pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.da, t, 4 * h + ch, G + 8 * ch);
+          float G[16], pq[16], bv[16], av;
+          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, G);
           // suffix state (after this chunk) of group g: bf16 copy for the MMAs, gA to smem
-          float bv[32], av;
-          tc::tmem_ld32(tmem + lane_off + T_GB + 64 * (g >> 1) + 32 * h, bv);
+          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
           tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
           tc::tmem_wait_ld();
+          table_probs_th(thQ, a.scale, pq);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;  // dA
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, G + 8 * ch);
           if (mpar == (g & 1)) {
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 4 * h + ch, bv + 8 * ch);
-            if (h == 0) sGA[mrow] = av;
+            for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 2 * hq + ch, bv + 8 * ch);
+            if (hq == 0) sGA[mrow] = av;
           }
         }
         tc::fence_async_smem();
@@ -848,27 +840,23 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         __syncwarp();
         tc::tc_fence_after();
         {
-          float dpk[32], pk[32], dp[8];
-          tc::tmem_ld32(tmem + lane_off + BT_R + 32 * h, dpk);
+          float dpk[16], pk[16], dp[4];
+          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, dpk);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) dpk[i] += sGA[32 * h + i];
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_th(thK + 4 * i, a.scale, pk + 16 * i);
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs_bwd(pk + 16 * i, dpk + 16 * i, thK + 4 * i, a.scale, dp + 4 * i);
-          tc::st_row_chunk(sbase + P.dproj, t, 2 * g + h, dp);
+          for (int i = 0; i < 16; ++i) dpk[i] += sGA[16 * hq + i];
+          table_probs_th(thK, a.scale, pk);
+          table_probs_bwd(pk, dpk, thK, a.scale, dp);
+          tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
           // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64)
           float v[32];
-          for (int hh = 0; hh < 2; ++hh) {
-            tc::tmem_ld32(tmem + lane_off + BT_X + 64 * h + 32 * hh, v);
-            tc::tmem_wait_ld();
+          tc::tmem_ld32(tmem + lane_off + BT_X + 32 * hq, v);
+          tc::tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (64 * h + 32 * hh + i < t) v[i] = 0.f;
+          for (int i = 0; i < 32; ++i)
+            if (32 * hq + i < t) v[i] = 0.f;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, 4 * hh + ch, v + 8 * ch);
-          }
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, v + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -880,15 +868,15 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       __syncwarp();
       tc::tc_fence_after();
       {
-        float kv[32], vv[32];
-        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * h, kv);
-        tc::tmem_ld32(tmem + lane_off + T_DV + 32 * h, vv);
+        float kv[16], vv[16];
+        tc::tmem_ld16(tmem + lane_off + BT_X + 16 * hq, kv);
+        tc::tmem_ld16(tmem + lane_off + T_DV + 16 * hq, vv);
         tc::tmem_wait_ld();
         if (t < nt) {
-          __nv_bfloat16 *dk = a.dK + ((size_t)n * a.T + tok0 + t) * HD + 32 * h;
-          __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + 32 * h;
+          __nv_bfloat16 *dk = a.dK + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
+          __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int ch = 0; ch < 2; ++ch) {
             st_bf16x8_global(dk + 8 * ch, kv + 8 * ch);
             st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
           }
@@ -910,3 +898,4 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
 
 }  // namespace fast
 }  // namespace race
+

@@ -34,7 +34,7 @@ namespace fast {
 constexpr int C = 128;             // tokens per chunk (MMA M)
 constexpr int HD = 64;             // head dim
 constexpr int GB = 128;            // buckets per group
-constexpr int NEPI = 8;            // epilogue warps (2 per TMEM lane quarter)
+constexpr int NEPI = 16;           // epilogue warps (4 per TMEM lane quarter, one column quarter each)
 constexpr int NTHR = (NEPI + 1) * 32;
 constexpr int NEPI_T = NEPI * 32;
 constexpr uint32_t TILE = C * 128;  // one [128 x 64] bf16 tile = 16 KB
@@ -250,10 +250,12 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     }
     __syncwarp();
   } else {
-    // ===================== epilogue warps: row t of the chunk, column half h
-    const int q4 = warp & 3, h = warp >> 2;
+    // ===================== epilogue warps: row t of the chunk, column quarter hq
+    const int q4 = warp & 3, hq = warp >> 2;
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
+    const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
     float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
     float *const sA1 = reinterpret_cast<float *>(sm + P.a1);
     // ---- prologue: planes (bf16, K-major rows j), tril, A_start, Bstate
@@ -263,23 +265,23 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       *reinterpret_cast<__nv_bfloat16 *>(sm + off) = __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
     }
     {
-      // tril[t][tau] = tau <= t, two 64-column blocks; this thread writes row t, block h
+      // tril[t][tau] = tau <= t; this thread writes row t, columns [32hq, 32hq+32)
       float v[8];
-      for (int ch = 0; ch < 8; ++ch) {
+      for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (h * 64 + ch * 8 + e) <= t ? 1.f : 0.f;
-        tc::st_row_chunk(sbase + P.tril + h * TILE, t, ch, v);
+        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) <= t ? 1.f : 0.f;
+        tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
     for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = state0[s];
     for (int g = 0; g < a.ngroups; ++g) {
-      float v[32];
-      const float *src = state0 + S + (size_t)(g * GB + t) * HD + 32 * h;
+      float v[16];
+      const float *src = state0 + S + (size_t)(g * GB + t) * HD + 16 * hq;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = src[i];
-      tc::tmem_st32(tmem + lane_off + T_B + 64 * g + 32 * h, v);
+      for (int i = 0; i < 16; ++i) v[i] = src[i];
+      tc::tmem_st16(tmem + lane_off + T_B + 64 * g + 16 * hq, v);
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 4 * h + ch, v + 8 * ch);
+      for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 2 * hq + ch, v + 8 * ch);
     }
     tc::tmem_wait_st();
     tc::fence_async_smem();
@@ -301,20 +303,20 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       tc::tc_fence_after();
       for (int g = 0; g < a.ngroups && ok; ++g) {
         const int u = c * a.ngroups + g;
-        const int j0 = (g * 8 + h * 4) * 4;  // first projection column of this thread's 4 tables
-        // ---- Pk (this thread: row t, buckets [64h, 64h+64) of group g)
+        const int j0 = (g * 8 + hq * 2) * 4;  // first projection column of this thread's 2 tables
+        // ---- Pk (row t, buckets [32hq, 32hq+32) of group g)
         {
-          float pj[16], pr[64];
-          tc::tmem_ld16(tmem + lane_off + T_PK + j0, pj);
+          float pj[8], pr[32];
+          tc::tmem_ld8(tmem + lane_off + T_PK + j0, pj);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
+          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
           if (t >= nt) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) pr[i] = 0.f;
+            for (int i = 0; i < 32; ++i) pr[i] = 0.f;
           }
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.pk + h * TILE, t, ch, pr + 8 * ch);
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.pk + blk, t, ch0 + ch, pr + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -325,82 +327,69 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         __syncwarp();
         tc::tc_fence_after();
         {
-          float pj[16], pq[64], ap0[32], ap1[32];
-          tc::tmem_ld16(tmem + lane_off + T_PQ + j0, pj);
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, ap0);
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, ap1);
+          float pj[8], pq[32], ap[32];
+          tc::tmem_ld8(tmem + lane_off + T_PQ + j0, pj);
+          tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, ap);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pq + 16 * i);
-          const int sb = g * GB + 64 * h;
+          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, pq + 16 * i);
+          const int sb = g * GB + 32 * hq;
           if (t == C - 1) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              Anxt[sb + i] = Acur[sb + i] + ap0[i];
-              Anxt[sb + 32 + i] = Acur[sb + 32 + i] + ap1[i];
-            }
+            for (int i = 0; i < 32; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
           }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            pq[i] = __fdividef(pq[i], Acur[sb + i] + ap0[i] + a.eps);
-            pq[32 + i] = __fdividef(pq[32 + i], Acur[sb + 32 + i] + ap1[i] + a.eps);
-          }
+          for (int i = 0; i < 32; ++i) pq[i] = __fdividef(pq[i], Acur[sb + i] + ap[i] + a.eps);
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, pq + 8 * ch);
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, pq + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::mbar_arrive(&bars[B_W]);
-        // ---- Smask = tril(Smat)
+        // ---- Smask = tril(Smat), columns tau in [32hq, 32hq+32)
         ok = tc::mbar_wait(&bars[B_SMAT], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
         {
-          float sv0[32], sv1[32];
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h, sv0);
-          tc::tmem_ld32(tmem + lane_off + T_G + 64 * h + 32, sv1);
+          float sv[32];
+          tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, sv);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (64 * h + i > t) sv0[i] = 0.f;
-            if (64 * h + 32 + i > t) sv1[i] = 0.f;
-          }
+          for (int i = 0; i < 32; ++i)
+            if (32 * hq + i > t) sv[i] = 0.f;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            tc::st_row_chunk(sbase + P.w + h * TILE, t, ch, sv0 + 8 * ch);
-            tc::st_row_chunk(sbase + P.w + h * TILE, t, 4 + ch, sv1 + 8 * ch);
-          }
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, sv + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::mbar_arrive(&bars[B_SMASK]);
-        // ---- refresh the bf16 copy of Bstate_g (lane t = bucket t of group g)
+        // ---- refresh the bf16 copy of Bstate_g (lane t = bucket t of group g), d in [16hq, 16hq+16)
         ok = tc::mbar_wait(&bars[B_GDONE], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
         {
-          float bv[32];
-          tc::tmem_ld32(tmem + lane_off + T_B + 64 * g + 32 * h, bv);
+          float bv[16];
+          tc::tmem_ld16(tmem + lane_off + T_B + 64 * g + 16 * hq, bv);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 4 * h + ch, bv + 8 * ch);
+          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 2 * hq + ch, bv + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::mbar_arrive(&bars[B_BST0 + g]);
       }
       if (!ok) break;
-      // ---- out rows (the last group's GDONE wait covered all MMAs into out)
+      // ---- out rows, d in [16hq, 16hq+16) (the last group's GDONE covered all MMAs into out)
       {
-        float ov[32];
-        tc::tmem_ld32(tmem + lane_off + T_OUT + 32 * h, ov);
+        float ov[16];
+        tc::tmem_ld16(tmem + lane_off + T_OUT + 16 * hq, ov);
         tc::tmem_wait_ld();
         if (t < nt) {
-          uint4 *dst = reinterpret_cast<uint4 *>(a.out + ((size_t)n * a.T + tok0 + t) * HD + 32 * h);
+          uint4 *dst = reinterpret_cast<uint4 *>(a.out + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq);
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
+          for (int ch = 0; ch < 2; ++ch) {
             uint4 w4;
             w4.x = tc::pack_bf16(ov[8 * ch + 0], ov[8 * ch + 1]);
             w4.y = tc::pack_bf16(ov[8 * ch + 2], ov[8 * ch + 3]);
@@ -533,7 +522,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     }
     __syncwarp();
   } else {
-    const int q4 = warp & 3, h = warp >> 2;
+    const int q4 = warp & 3, hq = warp >> 2;
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
@@ -543,7 +532,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     }
     {
       float v[8];
-      for (int ch = 4 * h; ch < 4 * h + 4; ++ch) {
+      for (int ch = 2 * hq; ch < 2 * hq + 2; ++ch) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = (ch * 8 + e) < 16 ? 1.f : 0.f;
         tc::st_row_chunk(sbase + P.ones, t, ch, v);
@@ -560,18 +549,19 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       __syncwarp();
       tc::tc_fence_after();
       for (int g = 0; g < a.ngroups; ++g) {
-        const int j0 = (g * 8 + h * 4) * 4;
-        float pj[16], pr[64];
-        tc::tmem_ld16(tmem + lane_off + j0, pj);
+        const int j0 = (g * 8 + hq * 2) * 4;
+        float pj[8], pr[32];
+        tc::tmem_ld8(tmem + lane_off + j0, pj);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
+        for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
         if (t >= nt) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) pr[i] = 0.f;
+          for (int i = 0; i < 32; ++i) pr[i] = 0.f;
         }
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) tc::st_row_chunk(sbase + P.pk + (g * 2 + h) * TILE, t, ch, pr + 8 * ch);
+        for (int ch = 0; ch < 4; ++ch)
+          tc::st_row_chunk(sbase + P.pk + (g * 2 + (hq >> 1)) * TILE, t, (hq & 1) * 4 + ch, pr + 8 * ch);
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
@@ -583,22 +573,14 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     tc::tc_fence_after();
     if (ok) {
       for (int g = 0; g < a.ngroups; ++g) {
-        float bv[32];
-        tc::tmem_ld32(tmem + lane_off + 64 + 64 * g + 32 * h, bv);
+        float bv[16], av;
+        tc::tmem_ld16(tmem + lane_off + 64 + 64 * g + 16 * hq, bv);
+        tc::tmem_ld1(tmem + lane_off + 192 + 16 * g, av);
         tc::tmem_wait_ld();
-        float *dst = rec + S + (size_t)(g * GB + t) * HD + 32 * h;
+        float *dst = rec + S + (size_t)(g * GB + t) * HD + 16 * hq;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[i] = bv[i];
-        if (h == 0) {
-          float av[16];
-          tc::tmem_ld16(tmem + lane_off + 192 + 16 * g, av);
-          tc::tmem_wait_ld();
-          rec[g * GB + t] = av[0];
-        } else {
-          float av[16];
-          tc::tmem_ld16(tmem + lane_off + 192 + 16 * g, av);  // keep the warp's tcgen05.ld uniform
-          tc::tmem_wait_ld();
-        }
+        for (int i = 0; i < 16; ++i) dst[i] = bv[i];
+        if (hq == 0) rec[g * GB + t] = av;
       }
     }
     if (nch == 0) {  // empty segment: zero record
