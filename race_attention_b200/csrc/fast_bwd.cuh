@@ -39,6 +39,8 @@ struct BwdArgs {
   int N, T, L, LP, S, ngroups;  // ngroups = S / 64
   int nseg, seg_chunks, nchunks;
   float eps, scale;
+  int poly;                 // plane sigmoids by series (2|scale| <= 1/2)
+  int batch_rcp;            // reciprocals of A + eps four at a time (eps >= 1e-8)
   const float *planes;      // [64, LP]
   const float *fwd_state;   // [N, nseg, E]  forward exclusive segment prefixes
   float *tot;               // [N, nseg, E]  first walk: segment gradient totals
@@ -48,28 +50,6 @@ struct BwdArgs {
   __nv_bfloat16 *dQ, *dK, *dV;  // [N, T, 64]
   int *err;
 };
-
-// probabilities of one table's 16 corners from tanh(proj) of its 4 planes
-__device__ __forceinline__ void table_probs_th(const float *th4, float scale, float *p16) {
-  float q[4];
-#pragma unroll
-  for (int p = 0; p < 4; ++p) q[p] = __fdividef(1.f, 1.f + __expf(-2.f * scale * th4[p]));
-  float x[4], y[8];
-#pragma unroll
-  for (int b0 = 0; b0 < 2; ++b0)
-#pragma unroll
-    for (int b1 = 0; b1 < 2; ++b1) x[b0 * 2 + b1] = (b0 ? q[0] : 1.f - q[0]) * (b1 ? q[1] : 1.f - q[1]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    y[2 * i] = x[i] * (1.f - q[2]);
-    y[2 * i + 1] = x[i] * q[2];
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    p16[2 * i] = y[i] * (1.f - q[3]);
-    p16[2 * i + 1] = y[i] * q[3];
-  }
-}
 
 // d proj of one table: softmax backward over the corners, through sum_p, tanh
 __device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g16, const float *th4, float scale,
@@ -142,7 +122,7 @@ __device__ __forceinline__ void bwd_init_bars(uint64_t *bars) {
   for (int i = 0; i < W_COUNT; ++i) {
     const bool epi = i == W_INIT || i == W_P1M || i == W_PK || i == W_W || i == W_DA || i == W_Q2 ||
                      i == W_OUTFREE || i == W_ESYNC;
-    tc::mbar_init(&bars[i], epi ? NEPI_T : 1);
+    tc::mbar_init(&bars[i], epi ? NARR : 1);
   }
   tc::fence_mbar_init();
 }
@@ -314,7 +294,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = st0[s];
+    // the A arrays (and the per-chunk A records) hold A + eps
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = st0[s] + a.eps;
     for (int b = 0; b < nblk; ++b) {  // forward state -> TMEM (M=64 layout), this lane's row, d in [16hq, +16)
       const int g = 2 * b + mpar;
       float v[16];
@@ -332,20 +313,20 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     tc::fence_async_smem();
     tc::tc_fence_before();
     tc::named_bar_sync(1, NEPI_T);
-    tc::mbar_arrive(&bars[W_INIT]);
+    tc::warp_arrive(&bars[W_INIT]);
 
     bool ok = true;
     for (int c = 0; c < nch && ok; ++c) {
       const int cg = c_begin + c, tok0 = cg * C;
       const int nt = min(C, a.T - tok0);
       const float *Acur = (c & 1) ? sA1 : sA0;
-      float *Anxt = (c & 1) ? sA0 : sA1;
+      const uint32_t aCur = sbase + ((c & 1) ? P.a1 : P.a0), aNxt = sbase + ((c & 1) ? P.a0 : P.a1);
       // the row-127 threads wrote this chunk's A during the previous one
-      ok = tc::mbar_sync(&bars[W_ESYNC], c & 1, abort);
+      ok = tc::warp_sync(&bars[W_ESYNC], c & 1, abort);
       if (!ok) break;
       // ---- P1m = tril-masked dO V^T ; chunk-start A to global
       for (int s = threadIdx.x; s < S; s += NEPI_T) a.chunkA[((size_t)n * a.nchunks + cg) * S + s] = Acur[s];
-      ok = tc::mbar_wait(&bars[W_P1], c & 1, abort);
+      ok = tc::warp_wait(&bars[W_P1], c & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -361,12 +342,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars[W_P1M]);
+      tc::warp_arrive(&bars[W_P1M]);
       for (int g = 0; g < NG && ok; ++g) {
         const int u = c * NG + g;
-        float thQ[4], inv[16];
+        float thQ[4], qQ[4], inv[16];  // this row's Q-side tanh and plane sigmoids of table 4g + hq
         // ---- Pk, pq
-        ok = tc::mbar_wait(&bars[W_PROJ], u & 1, abort);
+        ok = tc::warp_wait(&bars[W_PROJ], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -380,14 +361,16 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
             pk4[i] = tanh_fast(pk4[i]);
             thQ[i] = tanh_fast(thQ[i]);
           }
-          table_probs_th(pk4, a.scale, pr);
+          plane_sigmoids(pk4, a.scale, a.poly, pk4);
+          corner_probs(pk4, pr);
           if (t >= nt) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) pr[i] = 0.f;
           }
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
-          table_probs_th(thQ, a.scale, pr);
+          plane_sigmoids(thQ, a.scale, a.poly, qQ);
+          corner_probs(qQ, pr);
           if (t >= nt) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) pr[i] = 0.f;
@@ -397,9 +380,9 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[W_PK]);
+        tc::warp_arrive(&bars[W_PK]);
         // ---- inv, W ; chunk-start B state of this group -> smem bf16 + global
-        ok = tc::mbar_wait(&bars[W_APREF], u & 1, abort);
+        ok = tc::warp_wait(&bars[W_APREF], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -411,15 +394,11 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::ld_row_chunk(sbase + P.w, t, 2 * hq + ch, pq + 8 * ch);
           const int sb = g * GW + 16 * hq;
-          if (t == C - 1) {
+          add_shared_row<16>(aCur + 4 * sb, ap);  // + (A + eps) at chunk start
+          if (t == C - 1) store_shared_row<16>(aNxt + 4 * sb, ap);
+          rcp_n<16>(ap, inv, a.batch_rcp);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            inv[i] = __fdividef(1.f, Acur[sb + i] + ap[i] + a.eps);
-            pq[i] *= inv[i];
-          }
+          for (int i = 0; i < 16; ++i) pq[i] *= inv[i];
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, pq + 8 * ch);
           if (mpar == (g & 1)) {
@@ -432,9 +411,9 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[W_W]);
+        tc::warp_arrive(&bars[W_W]);
         // ---- G -> dpq (-> d proj_Q) and dA
-        ok = tc::mbar_wait(&bars[W_G], u & 1, abort);
+        ok = tc::warp_wait(&bars[W_G], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -442,7 +421,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
           float G[16], pq[16], da[16];
           tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, G);
           tc::tmem_wait_ld();
-          table_probs_th(thQ, a.scale, pq);
+          corner_probs(qQ, pq);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float gi = G[i] * inv[i];           // dpq
@@ -464,11 +443,11 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[W_DA]);
+        tc::warp_arrive(&bars[W_DA]);
       }
       if (!ok) break;
       // ---- dQ, d in [16hq, 16hq+16)
-      ok = tc::mbar_wait(&bars[W_OUT], c & 1, abort);
+      ok = tc::warp_wait(&bars[W_OUT], c & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -483,7 +462,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         }
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars[W_OUTFREE]);
+      tc::warp_arrive(&bars[W_OUTFREE]);
     }
     // ---- segment totals record (W_OUT of the last chunk covers every accumulation)
     __syncwarp();
@@ -731,7 +710,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     tc::fence_async_smem();
     tc::tc_fence_before();
     tc::named_bar_sync(1, NEPI_T);
-    tc::mbar_arrive(&bars[W_INIT]);
+    tc::warp_arrive(&bars[W_INIT]);
 
     bool ok = true;
     uint32_t esync = 0;
@@ -740,7 +719,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       const int nt = min(C, a.T - tok0);
       // chunk-start A (stored by the forward walk)
       for (int s = threadIdx.x; s < S; s += NEPI_T) sA[s] = a.chunkA[((size_t)n * a.nchunks + cg) * S + s];
-      ok = tc::mbar_wait(&bars[W_P1], k & 1, abort);
+      ok = tc::warp_wait(&bars[W_P1], k & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -756,27 +735,29 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
-      ok = tc::mbar_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sA visible to all epilogue threads
+      ok = tc::warp_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sA visible to all epilogue threads
       if (!ok) break;
-      tc::mbar_arrive(&bars[W_P1M]);
+      tc::warp_arrive(&bars[W_P1M]);
       for (int g = 0; g < NG && ok; ++g) {
         const int u = k * NG + g;
-        float thK[4], thQ[4], inv[16];
-        ok = tc::mbar_wait(&bars[W_PROJ], u & 1, abort);
+        float thK[4], qK[4], qQ[4], inv[16];  // K-side tanh, K and Q plane sigmoids of table 4g + hq
+        ok = tc::warp_wait(&bars[W_PROJ], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
         {
           float pr[16];
           tc::tmem_ld4(tmem + lane_off + BT_R + 4 * hq, thK);
-          tc::tmem_ld4(tmem + lane_off + BT_R + 16 + 4 * hq, thQ);
+          tc::tmem_ld4(tmem + lane_off + BT_R + 16 + 4 * hq, qQ);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             thK[i] = tanh_fast(thK[i]);
-            thQ[i] = tanh_fast(thQ[i]);
+            qQ[i] = tanh_fast(qQ[i]);
           }
-          table_probs_th(thK, a.scale, pr);
+          plane_sigmoids(thK, a.scale, a.poly, qK);
+          plane_sigmoids(qQ, a.scale, a.poly, qQ);
+          corner_probs(qK, pr);
           if (t >= nt) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) pr[i] = 0.f;
@@ -786,8 +767,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[W_PK]);
-        ok = tc::mbar_wait(&bars[W_APREF], u & 1, abort);
+        tc::warp_arrive(&bars[W_PK]);
+        ok = tc::warp_wait(&bars[W_APREF], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -795,20 +776,19 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           float ap[16], w[16];
           tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, ap);
           tc::tmem_wait_ld();
-          table_probs_th(thQ, a.scale, w);
+          corner_probs(qQ, w);
           const int sb = g * GW + 16 * hq;
+          add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
+          rcp_n<16>(ap, inv, a.batch_rcp);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            inv[i] = __fdividef(1.f, sA[sb + i] + ap[i] + a.eps);
-            w[i] = t < nt ? w[i] * inv[i] : 0.f;
-          }
+          for (int i = 0; i < 16; ++i) w[i] = t < nt ? w[i] * inv[i] : 0.f;
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, w + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[W_W]);
-        ok = tc::mbar_wait(&bars[W_G], u & 1, abort);
+        tc::warp_arrive(&bars[W_W]);
+        ok = tc::warp_wait(&bars[W_G], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -819,7 +799,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
           tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
           tc::tmem_wait_ld();
-          table_probs_th(thQ, a.scale, pq);
+          corner_probs(qQ, pq);
 #pragma unroll
           for (int i = 0; i < 16; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;  // dA
 #pragma unroll
@@ -832,10 +812,10 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        ok = tc::mbar_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sGA complete (read after W_DPK)
+        ok = tc::warp_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sGA complete (read after W_DPK)
         if (!ok) break;
-        tc::mbar_arrive(&bars[W_DA]);
-        ok = tc::mbar_wait(&bars[W_DPK], u & 1, abort);
+        tc::warp_arrive(&bars[W_DA]);
+        ok = tc::warp_wait(&bars[W_DPK], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -845,7 +825,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) dpk[i] += sGA[16 * hq + i];
-          table_probs_th(thK, a.scale, pk);
+          corner_probs(qK, pk);
           table_probs_bwd(pk, dpk, thK, a.scale, dp);
           tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
           // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64)
@@ -860,10 +840,10 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[W_Q2]);
+        tc::warp_arrive(&bars[W_Q2]);
       }
       if (!ok) break;
-      ok = tc::mbar_wait(&bars[W_OUT], k & 1, abort);
+      ok = tc::warp_wait(&bars[W_OUT], k & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -883,7 +863,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars[W_OUTFREE]);
+      tc::warp_arrive(&bars[W_OUTFREE]);
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }

@@ -36,6 +36,7 @@ constexpr int HD = 64;             // head dim
 constexpr int GB = 128;            // buckets per group
 constexpr int NEPI = 16;           // epilogue warps (4 per TMEM lane quarter, one column quarter each)
 constexpr int NTHR = (NEPI + 1) * 32;
+constexpr int NARR = NEPI;        // arrivals that complete an epilogue barrier (one per warp)
 constexpr int NEPI_T = NEPI * 32;
 constexpr uint32_t TILE = C * 128;  // one [128 x 64] bf16 tile = 16 KB
 
@@ -46,6 +47,8 @@ struct FwdArgs {
   int N, T, L, LP, S, ngroups;
   int nseg, seg_chunks, nchunks;  // chunks per segment; total chunks per stream
   float eps, scale;
+  int poly;               // plane sigmoids by series (2|scale| <= 1/2)
+  int batch_rcp;          // reciprocals of A + eps four at a time (eps >= 1e-8)
   const float *planes;    // [64, LP] fp32
   const float *seg_state;  // [N, nseg, S + S*64]  (A part, then B part) exclusive segment prefixes
   float *seg_tot;          // totals kernel output, same layout
@@ -59,15 +62,33 @@ __device__ __forceinline__ float tanh_fast(float x) {
   return y;
 }
 
-// probabilities of the 16 corners of one table from its 4 projections
-// (corner r: bit (3-p) of r selects sigma(+2a_p) vs sigma(-2a_p))
-__device__ __forceinline__ void table_probs(const float *proj4, float scale, float *p16) {
-  float q[4];
+// sigma(z) for |z| <= 1/2, from sigma(z) = (1 + tanh(z/2)) / 2 and the odd
+// Taylor series of tanh(w) = w - w^3/3 + 2w^5/15 - 17w^7/315 + 62w^9/2835 - ...
+// truncated after w^9 (|w| <= 1/4: truncation error < 3e-9).  Five FMA-pipe
+// operations instead of an exponential and a reciprocal on the SFU.
+__device__ __forceinline__ float sigmoid_small(float z) {
+  const float w = 0.5f * z, w2 = w * w;
+  float p = fmaf(w2, 62.f / 2835.f, -17.f / 315.f);
+  p = fmaf(p, w2, 2.f / 15.f);
+  p = fmaf(p, w2, -1.f / 3.f);
+  p = fmaf(p, w2, 1.f);
+  return fmaf(0.5f * w, p, 0.5f);
+}
+
+// q_p = sigma(2 * scale * tanh(proj_p)) of one table's 4 planes, from th = tanh(proj).
+// `poly` (host-chosen: 2|scale| <= 1/2, which bounds |z| since |tanh| <= 1)
+// selects the series above; otherwise the SFU exponential.
+__device__ __forceinline__ void plane_sigmoids(const float *th4, float scale, bool poly, float *q4) {
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const float a = tanh_fast(proj4[p]) * scale;
-    q[p] = __fdividef(1.f, 1.f + __expf(-2.f * a));
+    const float z = 2.f * scale * th4[p];
+    q4[p] = poly ? sigmoid_small(z) : __fdividef(1.f, 1.f + __expf(-z));
   }
+}
+
+// probabilities of the 16 corners of one table from its 4 plane sigmoids
+// (corner r: bit (3-p) of r selects sigma(+2a_p) vs sigma(-2a_p))
+__device__ __forceinline__ void corner_probs(const float *q, float *p16) {
   float x[4], y[8];
 #pragma unroll
   for (int b0 = 0; b0 < 2; ++b0)
@@ -83,6 +104,62 @@ __device__ __forceinline__ void table_probs(const float *proj4, float scale, flo
     p16[2 * i] = y[i] * (1.f - q[3]);
     p16[2 * i + 1] = y[i] * q[3];
   }
+}
+
+// corner probabilities of one table straight from its 4 raw projections
+__device__ __forceinline__ void table_probs(const float *proj4, float scale, bool poly, float *p16) {
+  float th[4], q[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) th[p] = tanh_fast(proj4[p]);
+  plane_sigmoids(th, scale, poly, q);
+  corner_probs(q, p16);
+}
+
+// Reciprocals of 4 values with one SFU operation (Montgomery's simultaneous
+// inversion: 1/x_i from 1/(x0 x1 x2 x3) and the partial products).  Needs the
+// product to be a normal float: callers use it for x = A + eps with
+// eps >= 1e-8 and A < 2^31 (host flag `batch_rcp`), else one reciprocal each.
+__device__ __forceinline__ void rcp4(const float *x, float *r) {  // r may alias x
+  const float x0 = x[0], x1 = x[1], x2 = x[2], x3 = x[3];
+  const float x01 = x0 * x1, x012 = x01 * x2;
+  float inv = __fdividef(1.f, x012 * x3);
+  r[3] = inv * x012;
+  inv *= x3;
+  r[2] = inv * x01;
+  inv *= x2;
+  r[1] = inv * x0;
+  r[0] = inv * x1;
+}
+
+// r[i] = 1 / x[i] for n (a multiple of 4) values
+template <int n>
+__device__ __forceinline__ void rcp_n(const float *x, float *r, bool batch) {
+  if (batch) {
+#pragma unroll
+    for (int i = 0; i < n; i += 4) rcp4(x + i, r + i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < n; ++i) r[i] = __fdividef(1.f, x[i]);
+  }
+}
+
+// den[i] += A[i] for n (a multiple of 4) consecutive floats of a shared array
+template <int n>
+__device__ __forceinline__ void add_shared_row(uint32_t addr, float *den) {
+#pragma unroll
+  for (int i = 0; i < n; i += 4) {
+    const float4 v = tc::ld_shared_f4(addr + 4 * i);
+    den[i] += v.x;
+    den[i + 1] += v.y;
+    den[i + 2] += v.z;
+    den[i + 3] += v.w;
+  }
+}
+
+template <int n>
+__device__ __forceinline__ void store_shared_row(uint32_t addr, const float *v) {
+#pragma unroll
+  for (int i = 0; i < n; i += 4) tc::st_shared_f4(addr + 4 * i, make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
 }
 
 // --------------------------------------------------------------------------
@@ -138,17 +215,17 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     tc::mbar_init(&bars[B_QK1], 1);
     tc::mbar_init(&bars[B_V], 1);
     tc::mbar_init(&bars[B_PROJ], 1);
-    tc::mbar_init(&bars[B_PK], NEPI_T);
+    tc::mbar_init(&bars[B_PK], NARR);
     tc::mbar_init(&bars[B_APREF], 1);
-    tc::mbar_init(&bars[B_W], NEPI_T);
+    tc::mbar_init(&bars[B_W], NARR);
     tc::mbar_init(&bars[B_SMAT], 1);
-    tc::mbar_init(&bars[B_SMASK], NEPI_T);
+    tc::mbar_init(&bars[B_SMASK], NARR);
     tc::mbar_init(&bars[B_GDONE], 1);
-    tc::mbar_init(&bars[B_BST0], NEPI_T);
-    tc::mbar_init(&bars[B_BST1], NEPI_T);
-    tc::mbar_init(&bars[B_OUTFREE], NEPI_T);
+    tc::mbar_init(&bars[B_BST0], NARR);
+    tc::mbar_init(&bars[B_BST1], NARR);
+    tc::mbar_init(&bars[B_OUTFREE], NARR);
     tc::mbar_init(&bars[B_FINAL], 1);
-    tc::mbar_init(&bars[B_ESYNC], NEPI_T);
+    tc::mbar_init(&bars[B_ESYNC], NARR);
     tc::fence_mbar_init();
   }
   if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
@@ -257,7 +334,6 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
     const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
     float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
-    float *const sA1 = reinterpret_cast<float *>(sm + P.a1);
     // ---- prologue: planes (bf16, K-major rows j), tril, A_start, Bstate
     for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
       const int j = i / HD, d = i % HD;
@@ -273,7 +349,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = state0[s];
+    // the A arrays hold A + eps (the chunk recurrence adds counts, so the offset carries)
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = state0[s] + a.eps;
     for (int g = 0; g < a.ngroups; ++g) {
       float v[16];
       const float *src = state0 + S + (size_t)(g * GB + t) * HD + 16 * hq;
@@ -287,17 +364,16 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     tc::fence_async_smem();
     tc::tc_fence_before();
     tc::named_bar_sync(1, NEPI_T);  // prologue smem (planes, tril, A) complete before first use
-    for (int g = 0; g < a.ngroups; ++g) tc::mbar_arrive(&bars[B_BST0 + g]);
+    for (int g = 0; g < a.ngroups; ++g) tc::warp_arrive(&bars[B_BST0 + g]);
 
     bool ok = true;
     for (int c = 0; c < nch && ok; ++c) {
       const int tok0 = (c_begin + c) * C;
       const int nt = min(C, a.T - tok0);
-      const float *Acur = (c & 1) ? sA1 : sA0;
-      float *Anxt = (c & 1) ? sA0 : sA1;
+      const uint32_t aCur = sbase + ((c & 1) ? P.a1 : P.a0), aNxt = sbase + ((c & 1) ? P.a0 : P.a1);
       // the row-127 threads wrote this chunk's A during the previous one
-      ok = tc::mbar_sync(&bars[B_ESYNC], c & 1, abort);
-      if (ok) ok = tc::mbar_wait(&bars[B_PROJ], c & 1, abort);
+      ok = tc::warp_sync(&bars[B_ESYNC], c & 1, abort);
+      if (ok) ok = tc::warp_wait(&bars[B_PROJ], c & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -310,7 +386,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
           tc::tmem_ld8(tmem + lane_off + T_PK + j0, pj);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
+          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pr + 16 * i);
           if (t >= nt) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) pr[i] = 0.f;
@@ -320,9 +396,9 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[B_PK]);
+        tc::warp_arrive(&bars[B_PK]);
         // ---- W = pq / (A_start + Apref + eps)
-        ok = tc::mbar_wait(&bars[B_APREF], u & 1, abort);
+        ok = tc::warp_wait(&bars[B_APREF], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -332,40 +408,49 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
           tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, ap);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, pq + 16 * i);
+          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pq + 16 * i);
           const int sb = g * GB + 32 * hq;
-          if (t == C - 1) {
+          // den = A_start + eps + Apref (vector smem loads; the row-127 thread's
+          // den is the next chunk's A + eps)
+          add_shared_row<32>(aCur + 4 * sb, ap);
+          if (t == C - 1) store_shared_row<32>(aNxt + 4 * sb, ap);
+          rcp_n<32>(ap, ap, a.batch_rcp);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) Anxt[sb + i] = Acur[sb + i] + ap[i];
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pq[i] = __fdividef(pq[i], Acur[sb + i] + ap[i] + a.eps);
+          for (int i = 0; i < 32; ++i) pq[i] *= ap[i];
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, pq + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[B_W]);
+        tc::warp_arrive(&bars[B_W]);
         // ---- Smask = tril(Smat), columns tau in [32hq, 32hq+32)
-        ok = tc::mbar_wait(&bars[B_SMAT], u & 1, abort);
+        ok = tc::warp_wait(&bars[B_SMAT], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
         {
+          // warps above the diagonal (hq > q4) store zeros without reading TMEM
           float sv[32];
-          tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, sv);
-          tc::tmem_wait_ld();
+          if (hq <= q4) {
+            tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, sv);
+            tc::tmem_wait_ld();
+            if (hq == q4) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (32 * hq + i > t) sv[i] = 0.f;
+              for (int i = 0; i < 32; ++i)
+                if (32 * hq + i > t) sv[i] = 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sv[i] = 0.f;
+          }
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, sv + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[B_SMASK]);
+        tc::warp_arrive(&bars[B_SMASK]);
         // ---- refresh the bf16 copy of Bstate_g (lane t = bucket t of group g), d in [16hq, 16hq+16)
-        ok = tc::mbar_wait(&bars[B_GDONE], u & 1, abort);
+        ok = tc::warp_wait(&bars[B_GDONE], u & 1, abort);
         if (!ok) break;
         __syncwarp();
         tc::tc_fence_after();
@@ -378,7 +463,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::mbar_arrive(&bars[B_BST0 + g]);
+        tc::warp_arrive(&bars[B_BST0 + g]);
       }
       if (!ok) break;
       // ---- out rows, d in [16hq, 16hq+16) (the last group's GDONE covered all MMAs into out)
@@ -400,7 +485,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars[B_OUTFREE]);
+      tc::warp_arrive(&bars[B_OUTFREE]);
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }
@@ -460,10 +545,10 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     tc::mbar_init(&bars[TB_FULL0], 1);
     tc::mbar_init(&bars[TB_FULL1], 1);
     tc::mbar_init(&bars[TB_PROJ], 1);
-    tc::mbar_init(&bars[TB_PK], NEPI_T);
+    tc::mbar_init(&bars[TB_PK], NARR);
     tc::mbar_init(&bars[TB_DONE], 1);
     tc::mbar_init(&bars[TB_FINAL], 1);
-    tc::mbar_init(&bars[TB_INIT], NEPI_T);
+    tc::mbar_init(&bars[TB_INIT], NARR);
     tc::fence_mbar_init();
   }
   if (warp == NEPI) tc::tmem_alloc(&s_tmem, 256);
@@ -539,12 +624,12 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       }
     }
     tc::fence_async_smem();
-    tc::mbar_arrive(&bars[TB_INIT]);
+    tc::warp_arrive(&bars[TB_INIT]);
     bool ok = true;
     for (int c = 0; c < nch && ok; ++c) {
       const int nt = min(C, a.T - (c_begin + c) * C);
-      ok = tc::mbar_wait(&bars[TB_PROJ], c & 1, abort);
-      if (ok && c > 0) ok = tc::mbar_wait(&bars[TB_DONE], (c - 1) & 1, abort);  // Pk buffers free
+      ok = tc::warp_wait(&bars[TB_PROJ], c & 1, abort);
+      if (ok && c > 0) ok = tc::warp_wait(&bars[TB_DONE], (c - 1) & 1, abort);  // Pk buffers free
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -554,7 +639,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
         tc::tmem_ld8(tmem + lane_off + j0, pj);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, pr + 16 * i);
+        for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pr + 16 * i);
         if (t >= nt) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) pr[i] = 0.f;
@@ -565,10 +650,10 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars[TB_PK]);
+      tc::warp_arrive(&bars[TB_PK]);
     }
     // write the totals record
-    if (ok && nch > 0) ok = tc::mbar_wait(&bars[TB_DONE], (nch - 1) & 1, abort);
+    if (ok && nch > 0) ok = tc::warp_wait(&bars[TB_DONE], (nch - 1) & 1, abort);
     __syncwarp();
     tc::tc_fence_after();
     if (ok) {

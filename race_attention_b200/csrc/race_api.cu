@@ -4,6 +4,7 @@
 // Nothing here allocates device memory; launches go on the caller's stream.
 #include "race_b200.h"
 
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <atomic>
@@ -332,6 +333,8 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
   a.nchunks = pl.nchunks;
   a.eps = eps;
   a.scale = scale;
+  a.poly = 2.f * std::fabs(scale) <= 0.5f ? 1 : 0;
+  a.batch_rcp = eps >= 1e-8f ? 1 : 0;
   a.planes = planes_T;
   a.seg_state = at<float>(ws, pl.rec_off);
   a.seg_tot = at<float>(ws, pl.rec_off);
@@ -407,6 +410,8 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   b.nchunks = bp.p.nchunks;
   b.eps = eps;
   b.scale = scale;
+  b.poly = 2.f * std::fabs(scale) <= 0.5f ? 1 : 0;
+  b.batch_rcp = eps >= 1e-8f ? 1 : 0;
   b.planes = planes_T;
   b.fwd_state = at<float>(ws, bp.fwd_rec);
   b.tot = at<float>(ws, bp.bwd_rec);
