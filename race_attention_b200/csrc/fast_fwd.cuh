@@ -165,15 +165,15 @@ __device__ __forceinline__ void store_shared_row(uint32_t addr, const float *v) 
 // --------------------------------------------------------------------------
 // shared-memory plan (byte offsets from a 1024-aligned base)
 struct FwdSmem {
-  uint32_t q, k, v, pk, w, bst, tril, planes, a0, a1, bars, total;  // q, k: 2 stages of TILE bytes each
+  uint32_t q, k, v, pk, w, bst, tril, planes, a0, a1, bars, total;  // v: 2 stages of TILE bytes
 };
 
 __host__ __device__ __forceinline__ FwdSmem fwd_smem_plan(int ngroups, int LP) {
   FwdSmem m;
   uint32_t o = 0;
-  m.q = o; o += 2 * TILE;
-  m.k = o; o += 2 * TILE;
-  m.v = o; o += TILE;
+  m.q = o; o += TILE;
+  m.k = o; o += TILE;
+  m.v = o; o += 2 * TILE;
   m.pk = o; o += 2 * TILE;
   m.w = o; o += 2 * TILE;
   m.bst = o; o += (uint32_t)ngroups * TILE;
@@ -186,10 +186,28 @@ __host__ __device__ __forceinline__ FwdSmem fwd_smem_plan(int ngroups, int LP) {
   return m;
 }
 
-// barrier slots
-enum { B_QK0 = 0, B_QK1, B_V, B_PROJ, B_PK, B_APREF, B_W, B_SMAT, B_SMASK, B_GDONE, B_BST0, B_BST1, B_OUTFREE,
-       B_FINAL, B_ESYNC, B_COUNT };
+// mbarrier slots (TMA and MMA completions) and named barriers (epilogue -> MMA issuer)
+enum { B_QK = 0, B_V0, B_V1, B_PROJ, B_APREF, B_SMAT, B_GDONE, B_FINAL, B_COUNT };
+enum { NB_INIT = 1, NB_PK, NB_W, NB_SMASK, NB_ESYNC };
 
+// Schedule (u = chunk * ngroups + group).  The control warp issues, per group,
+//   {PK}    Apref = tril Pk          -> APREF ;  Bstate_g += Pk^T V
+//   {W}     Smat = W Pk^T ; out (+)= W bf16(Bstate_g at chunk start) -> SMAT
+//           (after the chunk's last W: proj of the next chunk -> PROJ)
+//   {SMASK} out += Smask V           -> GDONE
+// while the epilogue warps, per group, do
+//   Pk {PK} ; pq (overlaps Apref) ; [APREF] W {W} ;
+//   bf16 refresh of the previous group's Bstate (overlaps Smat) ;
+//   [SMAT] Smask {SMASK} ; (next group's Pk overlaps Smask V)
+// and read out after the chunk's last GDONE.  {X}: the epilogue warps arrive
+// on named barrier X (bar.arrive), the control warp waits on it (bar.sync);
+// [X]: mbarrier signalled by tcgen05.commit.  A Bstate refresh and the out
+// readout precede the epilogue's next {W} arrival, which is what orders them
+// before the MMAs that overwrite their sources.  Q/K are single-buffered (the
+// next chunk's tiles load while this chunk's groups run), V double-buffered.
+// Abort: a bounded wait that gives up raises *abort; from then on no thread
+// waits or works, but every thread still takes every named-barrier step, so
+// no bar.sync can be left without its arrivals.
 __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                               const __grid_constant__ CUtensorMap tmK,
                                                               const __grid_constant__ CUtensorMap tmV, FwdArgs a) {
@@ -205,27 +223,13 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   const int c_begin = seg * a.seg_chunks;
   const int c_end = min(a.nchunks, c_begin + a.seg_chunks);
   const int nch = c_end - c_begin;
-  const int S = a.S;
+  const int S = a.S, NG = a.ngroups;
   const size_t E = (size_t)S + (size_t)S * HD;
   const float *state0 = a.seg_state + ((size_t)n * a.nseg + seg) * E;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    tc::mbar_init(&bars[B_QK0], 1);
-    tc::mbar_init(&bars[B_QK1], 1);
-    tc::mbar_init(&bars[B_V], 1);
-    tc::mbar_init(&bars[B_PROJ], 1);
-    tc::mbar_init(&bars[B_PK], NARR);
-    tc::mbar_init(&bars[B_APREF], 1);
-    tc::mbar_init(&bars[B_W], NARR);
-    tc::mbar_init(&bars[B_SMAT], 1);
-    tc::mbar_init(&bars[B_SMASK], NARR);
-    tc::mbar_init(&bars[B_GDONE], 1);
-    tc::mbar_init(&bars[B_BST0], NARR);
-    tc::mbar_init(&bars[B_BST1], NARR);
-    tc::mbar_init(&bars[B_OUTFREE], NARR);
-    tc::mbar_init(&bars[B_FINAL], 1);
-    tc::mbar_init(&bars[B_ESYNC], NARR);
+    for (int i = 0; i < B_COUNT; ++i) tc::mbar_init(&bars[i], 1);
     tc::fence_mbar_init();
   }
   if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
@@ -236,91 +240,114 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   volatile int *abort = &s_abort;
 
   if (warp == NEPI) {
-    // ===================== control warp: TMA producer + MMA issuer (one lane)
-    if (lane == 0 && nch > 0) {
+    // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
+    const bool leader = lane == 0;
+    const uint32_t oq = P.q, ok_ = P.k, ov = P.v;
+    auto load_qk = [=, &tmQ, &tmK](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[B_QK], 2 * TILE);
+      tc::tma_load_3d(sm + oq, &tmQ, &bars[B_QK], 0, t0, n);
+      tc::tma_load_3d(sm + ok_, &tmK, &bars[B_QK], 0, t0, n);
+    };
+    auto load_v = [=, &tmV](int c) {
+      const int st = c & 1;
+      tc::mbar_arrive_expect_tx(&bars[B_V0 + st], TILE);
+      tc::tma_load_3d(sm + ov + st * TILE, &tmV, &bars[B_V0 + st], 0, (c_begin + c) * C, n);
+    };
+    const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
+    const uint32_t id_apref = tc::idesc_bf16(C, GB, false, true);
+    const uint32_t id_smat = tc::idesc_bf16(C, C, false, false);
+    const uint32_t id_out = tc::idesc_bf16(C, HD, false, true);
+    const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
+    auto issue_proj = [=]() {
+#pragma unroll
+      for (int k0 = 0; k0 < HD; k0 += 16) {
+        const uint64_t bp = tc::desc_kmajor(sbase + P.planes, k0, 0);
+        tc::mma_bf16(tmem + T_PK, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
+        tc::mma_bf16(tmem + T_PQ, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
+      }
+      tc::mma_commit(&bars[B_PROJ]);
+    };
+    bool ok = true;
+    if (leader && nch > 0) {
       tc::prefetch_tmap(&tmQ);
       tc::prefetch_tmap(&tmK);
       tc::prefetch_tmap(&tmV);
-      const int t0 = c_begin * C;
-      tc::mbar_arrive_expect_tx(&bars[B_QK0], 2 * TILE);
-      tc::tma_load_3d(sm + P.q, &tmQ, &bars[B_QK0], 0, t0, n);
-      tc::tma_load_3d(sm + P.k, &tmK, &bars[B_QK0], 0, t0, n);
-      if (nch > 1) {
-        tc::mbar_arrive_expect_tx(&bars[B_QK1], 2 * TILE);
-        tc::tma_load_3d(sm + P.q + TILE, &tmQ, &bars[B_QK1], 0, t0 + C, n);
-        tc::tma_load_3d(sm + P.k + TILE, &tmK, &bars[B_QK1], 0, t0 + C, n);
-      }
-      tc::mbar_arrive_expect_tx(&bars[B_V], TILE);
-      tc::tma_load_3d(sm + P.v, &tmV, &bars[B_V], 0, t0, n);
-
-      const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
-      const uint32_t id_apref = tc::idesc_bf16(C, GB, false, true);
-      const uint32_t id_smat = tc::idesc_bf16(C, C, false, false);
-      const uint32_t id_out = tc::idesc_bf16(C, HD, false, true);
-      const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
-      // the epilogue prologue (planes, tril, A/B state) must be in smem before
-      // the first MMA reads it; its completion is phase 0 of every BST barrier
-      bool ok = true;
-      for (int g = 0; g < a.ngroups && ok; ++g) ok = tc::mbar_wait(&bars[B_BST0 + g], 0, abort);
-      for (int c = 0; c < nch && ok; ++c) {
-        const int st = c & 1;
-        ok = tc::mbar_wait(&bars[B_QK0 + st], (c >> 1) & 1, abort);
-        if (!ok) break;
+      load_qk(0);
+      load_v(0);
+    }
+    // the epilogue prologue (planes, tril, A/B state) is in smem past this point
+    tc::named_bar_sync(NB_INIT, NTHR);
+    if (leader && nch > 0) {
+      ok = tc::mbar_wait(&bars[B_QK], 0, abort);
+      if (ok) {
         tc::tc_fence_after();
-        for (int k0 = 0; k0 < HD; k0 += 16) {
-          const uint64_t bp = tc::desc_kmajor(sbase + P.planes, k0, 0);
-          tc::mma_bf16(tmem + T_PK, tc::desc_kmajor(sbase + P.k + st * TILE, k0, TILE), bp, id_proj, k0 > 0);
-          tc::mma_bf16(tmem + T_PQ, tc::desc_kmajor(sbase + P.q + st * TILE, k0, TILE), bp, id_proj, k0 > 0);
-        }
-        tc::mma_commit(&bars[B_PROJ]);
-        for (int g = 0; g < a.ngroups && ok; ++g) {
-          const int u = c * a.ngroups + g;
-          ok = tc::mbar_wait(&bars[B_PK], u & 1, abort);
-          if (!ok) break;
+        issue_proj();
+      }
+    }
+    for (int c = 0; c < nch; ++c) {
+      const uint32_t vt = sbase + P.v + (uint32_t)(c & 1) * TILE;
+      for (int g = 0; g < NG; ++g) {
+        tc::named_bar_sync(NB_PK, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
           tc::tc_fence_after();
-          if (g == 0 && c + 2 < nch) {
-            // the proj MMAs that read this Q/K stage completed before the
-            // epilogue could produce Pk: refill the stage with chunk c+2
-            tc::mbar_arrive_expect_tx(&bars[B_QK0 + st], 2 * TILE);
-            tc::tma_load_3d(sm + P.q + st * TILE, &tmQ, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
-            tc::tma_load_3d(sm + P.k + st * TILE, &tmK, &bars[B_QK0 + st], 0, (c_begin + c + 2) * C, n);
-          }
+#pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + T_G, tc::desc_kmajor(sbase + P.tril, k0, TILE),
                          tc::desc_mnmajor(sbase + P.pk, k0, TILE), id_apref, k0 > 0);
           tc::mma_commit(&bars[B_APREF]);
-          ok = tc::mbar_wait(&bars[B_W], u & 1, abort);
-          if (ok && g == 0 && c > 0) ok = tc::mbar_wait(&bars[B_OUTFREE], (c - 1) & 1, abort);
-          if (ok) ok = tc::mbar_wait(&bars[B_BST0 + g], c & 1, abort);
-          if (!ok) break;
+          if (g == 0) {
+            // Pk(0) implies the epilogue saw this chunk's proj complete and the
+            // previous chunk's last MMA done: refill Q/K and the other V stage
+            if (c + 1 < nch) {
+              load_qk(c + 1);
+              load_v(c + 1);
+            }
+            ok = tc::mbar_wait(&bars[B_V0 + (c & 1)], (c >> 1) & 1, abort);
+          }
+          if (ok) {
+            tc::tc_fence_after();
+#pragma unroll
+            for (int k0 = 0; k0 < C; k0 += 16)
+              tc::mma_bf16(tmem + T_B + 64 * g, tc::desc_mnmajor(sbase + P.pk, k0, TILE),
+                           tc::desc_mnmajor(vt, k0, TILE), id_bupd, true);
+          }
+        }
+        tc::named_bar_sync(NB_W, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
           tc::tc_fence_after();
           const uint32_t bst = sbase + P.bst + (uint32_t)g * TILE;
+#pragma unroll
           for (int k0 = 0; k0 < GB; k0 += 16) {
             const uint64_t aw = tc::desc_kmajor(sbase + P.w, k0, TILE);
             tc::mma_bf16(tmem + T_G, aw, tc::desc_kmajor(sbase + P.pk, k0, TILE), id_smat, k0 > 0);
             tc::mma_bf16(tmem + T_OUT, aw, tc::desc_mnmajor(bst, k0, TILE), id_out, g > 0 || k0 > 0);
           }
           tc::mma_commit(&bars[B_SMAT]);
-          ok = tc::mbar_wait(&bars[B_SMASK], u & 1, abort);
-          if (ok && g == 0) ok = tc::mbar_wait(&bars[B_V], c & 1, abort);
-          if (!ok) break;
-          tc::tc_fence_after();
-          for (int k0 = 0; k0 < C; k0 += 16) {
-            const uint64_t bv = tc::desc_mnmajor(sbase + P.v, k0, TILE);
-            tc::mma_bf16(tmem + T_OUT, tc::desc_kmajor(sbase + P.w, k0, TILE), bv, id_out, true);
-            tc::mma_bf16(tmem + T_B + 64 * g, tc::desc_mnmajor(sbase + P.pk, k0, TILE), bv, id_bupd, true);
+          if (g == NG - 1 && c + 1 < nch) {
+            // every reader of proj (Pk and W phases) is done: next chunk's proj
+            ok = tc::mbar_wait(&bars[B_QK], (c + 1) & 1, abort);
+            if (ok) {
+              tc::tc_fence_after();
+              issue_proj();
+            }
           }
+        }
+        tc::named_bar_sync(NB_SMASK, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + T_OUT, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(vt, k0, TILE), id_out,
+                         true);
           tc::mma_commit(&bars[B_GDONE]);
         }
-        if (!ok) break;
-        if (c + 1 < nch) {
-          // V is free once this chunk's last group finished
-          ok = tc::mbar_wait(&bars[B_GDONE], (c * a.ngroups + a.ngroups - 1) & 1, abort);
-          if (!ok) break;
-          tc::mbar_arrive_expect_tx(&bars[B_V], TILE);
-          tc::tma_load_3d(sm + P.v, &tmV, &bars[B_V], 0, (c_begin + c + 1) * C, n);
-        }
       }
+    }
+    if (leader && nch > 0) {
       // drain: every MMA this thread issued has completed before TMEM is freed
       tc::mma_commit(&bars[B_FINAL]);
       if (!tc::mbar_wait_drain(&bars[B_FINAL], 0)) atomicExch(a.err, 2);
@@ -351,7 +378,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     }
     // the A arrays hold A + eps (the chunk recurrence adds counts, so the offset carries)
     for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = state0[s] + a.eps;
-    for (int g = 0; g < a.ngroups; ++g) {
+    for (int g = 0; g < NG; ++g) {
       float v[16];
       const float *src = state0 + S + (size_t)(g * GB + t) * HD + 16 * hq;
 #pragma unroll
@@ -363,25 +390,34 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     tc::tmem_wait_st();
     tc::fence_async_smem();
     tc::tc_fence_before();
-    tc::named_bar_sync(1, NEPI_T);  // prologue smem (planes, tril, A) complete before first use
-    for (int g = 0; g < a.ngroups; ++g) tc::warp_arrive(&bars[B_BST0 + g]);
+    tc::named_bar_sync(NB_INIT, NTHR);
+
+    // bf16 copy of Bstate_gr (lane t = bucket t), d in [16hq, 16hq+16), for the
+    // next chunk's W x Bstate
+    auto refresh = [=](int gr) {
+      float bv[16];
+      tc::tmem_ld16(tmem + lane_off + T_B + 64 * gr + 16 * hq, bv);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + gr * TILE, t, 2 * hq + ch, bv + 8 * ch);
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+    };
 
     bool ok = true;
-    for (int c = 0; c < nch && ok; ++c) {
+    for (int c = 0; c < nch; ++c) {
       const int tok0 = (c_begin + c) * C;
       const int nt = min(C, a.T - tok0);
       const uint32_t aCur = sbase + ((c & 1) ? P.a1 : P.a0), aNxt = sbase + ((c & 1) ? P.a0 : P.a1);
       // the row-127 threads wrote this chunk's A during the previous one
-      ok = tc::warp_sync(&bars[B_ESYNC], c & 1, abort);
-      if (ok) ok = tc::warp_wait(&bars[B_PROJ], c & 1, abort);
-      if (!ok) break;
-      __syncwarp();
+      tc::named_bar_sync(NB_ESYNC, NEPI_T);
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[B_PROJ], c & 1, abort));
       tc::tc_fence_after();
-      for (int g = 0; g < a.ngroups && ok; ++g) {
-        const int u = c * a.ngroups + g;
+      for (int g = 0; g < NG; ++g) {
+        const int u = c * NG + g;
         const int j0 = (g * 8 + hq * 2) * 4;  // first projection column of this thread's 2 tables
         // ---- Pk (row t, buckets [32hq, 32hq+32) of group g)
-        {
+        if (ok) {
           float pj[8], pr[32];
           tc::tmem_ld8(tmem + lane_off + T_PK + j0, pj);
           tc::tmem_wait_ld();
@@ -396,22 +432,24 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[B_PK]);
-        // ---- W = pq / (A_start + Apref + eps)
-        ok = tc::warp_wait(&bars[B_APREF], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
-        tc::tc_fence_after();
-        {
-          float pj[8], pq[32], ap[32];
+        tc::named_bar_arrive(NB_PK, NTHR);
+        // ---- pq while Apref runs, then W = pq / (A_start + Apref + eps)
+        float pq[32];
+        if (ok) {
+          float pj[8];
           tc::tmem_ld8(tmem + lane_off + T_PQ + j0, pj);
-          tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, ap);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pq + 16 * i);
+          ok = tc::warp_all(tc::mbar_wait(&bars[B_APREF], u & 1, abort));
+        }
+        tc::tc_fence_after();
+        if (ok) {
+          float ap[32];
+          tc::tmem_ld32(tmem + lane_off + T_G + 32 * hq, ap);
+          tc::tmem_wait_ld();
           const int sb = g * GB + 32 * hq;
-          // den = A_start + eps + Apref (vector smem loads; the row-127 thread's
-          // den is the next chunk's A + eps)
+          // den = A_start + eps + Apref; the row-127 thread's den is the next chunk's A + eps
           add_shared_row<32>(aCur + 4 * sb, ap);
           if (t == C - 1) store_shared_row<32>(aNxt + 4 * sb, ap);
           rcp_n<32>(ap, ap, a.batch_rcp);
@@ -422,13 +460,14 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[B_W]);
+        tc::named_bar_arrive(NB_W, NTHR);
+        // ---- previous group's state refresh while Smat runs (with one group per
+        // chunk the refresh follows Smask instead: the next Bupd is this group's)
+        if (ok && NG > 1 && u > 0) refresh(g > 0 ? g - 1 : NG - 1);
         // ---- Smask = tril(Smat), columns tau in [32hq, 32hq+32)
-        ok = tc::warp_wait(&bars[B_SMAT], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[B_SMAT], u & 1, abort));
         tc::tc_fence_after();
-        {
+        if (ok) {
           // warps above the diagonal (hq > q4) store zeros without reading TMEM
           float sv[32];
           if (hq <= q4) {
@@ -448,26 +487,13 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[B_SMASK]);
-        // ---- refresh the bf16 copy of Bstate_g (lane t = bucket t of group g), d in [16hq, 16hq+16)
-        ok = tc::warp_wait(&bars[B_GDONE], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
-        tc::tc_fence_after();
-        {
-          float bv[16];
-          tc::tmem_ld16(tmem + lane_off + T_B + 64 * g + 16 * hq, bv);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 2 * hq + ch, bv + 8 * ch);
-        }
-        tc::fence_async_smem();
-        tc::tc_fence_before();
-        tc::warp_arrive(&bars[B_BST0 + g]);
+        tc::named_bar_arrive(NB_SMASK, NTHR);
+        if (ok && NG == 1) refresh(0);
       }
-      if (!ok) break;
-      // ---- out rows, d in [16hq, 16hq+16) (the last group's GDONE covered all MMAs into out)
-      {
+      // ---- out rows, d in [16hq, 16hq+16), after the chunk's last Smask V
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[B_GDONE], (c * NG + NG - 1) & 1, abort));
+      tc::tc_fence_after();
+      if (ok) {
         float ov[16];
         tc::tmem_ld16(tmem + lane_off + T_OUT + 16 * hq, ov);
         tc::tmem_wait_ld();
@@ -485,7 +511,6 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         }
       }
       tc::tc_fence_before();
-      tc::warp_arrive(&bars[B_OUTFREE]);
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }

@@ -102,6 +102,15 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Non-blocking arrival on a named barrier (producer side of a bar.sync).
+// Arrivals count whole warps; the warp must be converged.
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// warp-uniform success flag: a lane whose bounded wait gave up fails the warp
+__device__ __forceinline__ bool warp_all(bool ok) { return __all_sync(0xffffffffu, ok); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
   asm volatile(
@@ -324,12 +333,16 @@ __device__ __forceinline__ void st_row_half(uint32_t tile, int row, int chunk16,
 
 // Operand descriptors for the layouts above.
 //   K-major (rows = M or N, 64-wide column blocks along K), K step k0 (multiple of 16):
+// (The start-address field is the low 14 bits, address >> 4, and shared
+// addresses stay below 2^18: a byte offset from `base` is added to the
+// descriptor as offset >> 4, so with k0 a compile-time constant each step is
+// one add on a loop-invariant descriptor.)
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int k0, uint32_t block_bytes) {
-  return sdesc(base + (uint32_t)(k0 >> 6) * block_bytes + (uint32_t)(k0 & 63) * 2, 16, 1024);
+  return sdesc(base, 16, 1024) + (uint64_t)(((uint32_t)(k0 >> 6) * block_bytes + (uint32_t)(k0 & 63) * 2) >> 4);
 }
 //   MN-major (rows = K, 64-wide column blocks along M/N), K step k0 (multiple of 16):
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k0, uint32_t block_bytes) {
-  return sdesc(base + (uint32_t)k0 * 128, block_bytes, 1024);
+  return sdesc(base, block_bytes, 1024) + (uint64_t)(((uint32_t)k0 * 128) >> 4);
 }
 
 }  // namespace tc
