@@ -137,6 +137,30 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 
 // ===========================================================================
 // forward walk of the backward pass
+//
+// TMEM: X [0,128) = P1 at chunk start, G during the group loop ([0,64)), dQ at
+// chunk end ([0,64)); R [128,192) = Apref; PJ [192,224) = proj of one group
+// (K in 16 columns, Q in 16); then the M=64 state blocks BF (forward B state),
+// GB (gradient B totals), GA (gradient A totals).
+// Schedule (u = chunk * ngroups + group); {X} named barrier (epilogue arrives,
+// control syncs), [X] mbarrier (tcgen05.commit / TMA):
+//   control, per chunk: [VO] P1 = dO V^T -> [P1]
+//            per group: {PK} Apref -> [APREF] ; {P1M, first group}
+//                       Bfwd += Pk^T V ; G = dO Bst^T + P1m Pk -> [G] ;
+//                       proj of the next group -> [PROJ] (after the last: Q/K refill)
+//                       {DA} gB += W^T dO ; gA += dA^T 1
+//            chunk end: dQ = dprojQ planes -> [OUT] ; next chunk's proj(0) ;
+//                       V/dO refill once every reader completed
+//   epilogue, per group: [PROJ] Pk, plane sigmoids, Bst refresh {PK} ;
+//                        (first group: [P1] P1m {P1M}) ;
+//                        [APREF] inv ; [G] W, dA, dpq -> dprojQ {DA}
+//            chunk end:  [OUT] dQ rows {OUTFREE}
+// Abort: as in the forward readout, every thread keeps taking every
+// named-barrier step after a bounded wait gave up.
+enum { V1_QK = 0, V1_VO, V1_P1, V1_PROJ, V1_APREF, V1_G, V1_OUT, V1_TFREE, V1_FINAL, V1_COUNT };
+enum { N1_INIT = 1, N1_PK, N1_P1M, N1_DA, N1_OUTFREE, N1_ESYNC };
+constexpr uint32_t B1_X = 0, B1_R = 128, B1_PJ = 192, B1_ST = 224;
+
 __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                           const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV,
@@ -154,11 +178,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
   const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
   const int S = a.S, NG = a.ngroups, nblk = (NG + 1) / 2;
   const size_t E = (size_t)S + (size_t)S * HD;
-  const uint32_t T_BF = BT_ST, T_GB = BT_ST + 64 * nblk, T_GA = BT_ST + 128 * nblk;
+  const uint32_t T_BF = B1_ST, T_GB = B1_ST + 64 * nblk, T_GA = B1_ST + 128 * nblk;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    bwd_init_bars(bars);
+    for (int i = 0; i < V1_COUNT; ++i) tc::mbar_init(&bars[i], 1);
+    tc::fence_mbar_init();
   }
   if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
   tc::tc_fence_before();
@@ -168,104 +193,136 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
   volatile int *abort = &s_abort;
 
   if (warp == NEPI) {
-    if (lane == 0 && nch > 0) {
-      const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
-      const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
-      const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
-      const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
-      const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
-      const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
-      const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
-      const uint32_t id_dq = tc::idesc_bf16(C, HD, false, true);
-      const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o;
-      auto load_chunk = [=, &tmQ, &tmK, &tmV, &tmO](int c) {
-        const int t0 = (c_begin + c) * C;
-        tc::mbar_arrive_expect_tx(&bars[W_FULL], 4 * TILE);
-        tc::tma_load_3d(sm + oq, &tmQ, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + ok_, &tmK, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + ov, &tmV, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + oo, &tmO, &bars[W_FULL], 0, t0, n);
-      };
-      load_chunk(0);
-      bool ok = tc::mbar_wait(&bars[W_INIT], 0, abort);
-      for (int c = 0; c < nch && ok; ++c) {
-        ok = tc::mbar_wait(&bars[W_FULL], c & 1, abort);
-        if (ok && c > 0) ok = tc::mbar_wait(&bars[W_OUTFREE], (c - 1) & 1, abort);
-        if (!ok) break;
+    // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
+    const bool leader = lane == 0;
+    const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
+    const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
+    const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
+    const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
+    const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
+    const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
+    const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
+    const uint32_t id_dq = tc::idesc_bf16(C, HD, false, true);
+    const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o;
+    auto load_qk = [=, &tmQ, &tmK](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[V1_QK], 2 * TILE);
+      tc::tma_load_3d(sm + oq, &tmQ, &bars[V1_QK], 0, t0, n);
+      tc::tma_load_3d(sm + ok_, &tmK, &bars[V1_QK], 0, t0, n);
+    };
+    auto load_vo = [=, &tmV, &tmO](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[V1_VO], 2 * TILE);
+      tc::tma_load_3d(sm + ov, &tmV, &bars[V1_VO], 0, t0, n);
+      tc::tma_load_3d(sm + oo, &tmO, &bars[V1_VO], 0, t0, n);
+    };
+    auto issue_proj = [=](int g) {
+      const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
+#pragma unroll
+      for (int k0 = 0; k0 < HD; k0 += 16) {
+        const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
+        tc::mma_bf16(tmem + B1_PJ, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
+        tc::mma_bf16(tmem + B1_PJ + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
+      }
+      tc::mma_commit(&bars[V1_PROJ]);
+    };
+    bool ok = true;
+    if (leader && nch > 0) {
+      load_qk(0);
+      load_vo(0);
+    }
+    tc::named_bar_sync(N1_INIT, NTHR);  // planes, tril, A and B state are in place
+    if (leader && nch > 0) {
+      ok = tc::mbar_wait(&bars[V1_QK], 0, abort);
+      if (ok) {
         tc::tc_fence_after();
-        for (int k0 = 0; k0 < HD; k0 += 16)
-          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
-                       k0 > 0);
-        tc::mma_commit(&bars[W_P1]);
-        ok = tc::mbar_wait(&bars[W_P1M], c & 1, abort);
-        if (!ok) break;
-        for (int g = 0; g < NG && ok; ++g) {
-          const int u = c * NG + g;
-          if (u > 0) ok = tc::mbar_wait(&bars[W_DA], (u - 1) & 1, abort);  // R free
-          if (!ok) break;
+        issue_proj(0);
+      }
+    }
+    for (int c = 0; c < nch; ++c) {
+      if (c > 0) tc::named_bar_sync(N1_OUTFREE, NTHR);  // the previous dQ is out of X
+      ok = ok && !*abort;
+      if (leader && ok) {
+        ok = tc::mbar_wait(&bars[V1_VO], c & 1, abort);
+        if (ok) {
           tc::tc_fence_after();
-          const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
-          for (int k0 = 0; k0 < HD; k0 += 16) {
-            const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
-            tc::mma_bf16(tmem + BT_R + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
-          }
-          if (u > 0) {
-            // the colsum of the previous group is issued here, after its dA landed
-            const int gp = (u - 1) % NG, cp = (u - 1) / NG;
-            for (int k0 = 0; k0 < C; k0 += 16)
-              tc::mma_bf16(m64_addr(tmem, T_GA, gp, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
-                           tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, cp > 0 || k0 > 0);
-          }
-          tc::mma_commit(&bars[W_PROJ]);
-          ok = tc::mbar_wait(&bars[W_PK], u & 1, abort);
-          if (!ok) break;
-          tc::tc_fence_after();
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
-                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
-          tc::mma_commit(&bars[W_APREF]);
-          ok = tc::mbar_wait(&bars[W_W], u & 1, abort);
-          if (!ok) break;
-          tc::tc_fence_after();
+#pragma unroll
           for (int k0 = 0; k0 < HD; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
-                         id_gk, k0 > 0);
+            tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
+                         k0 > 0);
+          tc::mma_commit(&bars[V1_P1]);
+        }
+      }
+      for (int g = 0; g < NG; ++g) {
+        tc::named_bar_sync(N1_PK, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+#pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.pk, k0, 0),
+            tc::mma_bf16(tmem + B1_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
+          tc::mma_commit(&bars[V1_APREF]);
+        }
+        if (g == 0) {
+          tc::named_bar_sync(N1_P1M, NTHR);
+          ok = ok && !*abort;
+        }
+        if (leader && ok) {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(m64_addr(tmem, T_BF, g, 64), tc::desc_mnmajor(sbase + P.pk, k0, 0),
+                         tc::desc_mnmajor(sbase + P.v, k0, 0), id_st, true);
+#pragma unroll
+          for (int k0 = 0; k0 < HD; k0 += 16)
+            tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
+                         id_gk, k0 > 0);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.pk, k0, 0),
                          id_gm, true);
+          tc::mma_commit(&bars[V1_G]);
+          if (g + 1 < NG) {
+            issue_proj(g + 1);
+          } else if (c + 1 < nch) {
+            load_qk(c + 1);  // the last proj of this chunk was consumed before {PK}
+          }
+        }
+        tc::named_bar_sync(N1_DA, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+#pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16) {
             tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
                          tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, c > 0 || k0 > 0);
-            tc::mma_bf16(m64_addr(tmem, T_BF, g, 64), tc::desc_mnmajor(sbase + P.pk, k0, 0),
-                         tc::desc_mnmajor(sbase + P.v, k0, 0), id_st, true);
-          }
-          tc::mma_commit(&bars[W_G]);
-          if (g == NG - 1 && c + 1 < nch) {
-            // every reader of this chunk's Q/K/V/dO tiles has been issued and
-            // completes with W_G: refill the single stage with the next chunk
-            ok = tc::mbar_wait(&bars[W_G], u & 1, abort);
-            if (!ok) break;
-            load_chunk(c + 1);
-          }
-        }
-        if (!ok) break;
-        ok = tc::mbar_wait(&bars[W_DA], (c * NG + NG - 1) & 1, abort);
-        if (!ok) break;
-        tc::tc_fence_after();
-        if (c + 1 == nch) {  // last chunk: the final colsum is issued here
-          const int gp = NG - 1;
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(m64_addr(tmem, T_GA, gp, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
+            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
                          tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, c > 0 || k0 > 0);
+          }
         }
-        for (int k0 = 0; k0 < a.LP; k0 += 16)
-          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
-                       id_dq, k0 > 0);
-        tc::mma_commit(&bars[W_OUT]);
       }
-      tc::mma_commit(&bars[W_FINAL]);
-      if (!tc::mbar_wait_drain(&bars[W_FINAL], 0)) atomicExch(a.err, 2);
+      if (leader && ok) {
+        for (int k0 = 0; k0 < a.LP; k0 += 16)
+          tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
+                       id_dq, k0 > 0);
+        tc::mma_commit(&bars[V1_OUT]);
+        if (c + 1 < nch) {
+          ok = tc::mbar_wait(&bars[V1_QK], (c + 1) & 1, abort);
+          if (ok) {
+            tc::tc_fence_after();
+            issue_proj(0);
+            // V and dO are free once every MMA issued so far has completed
+            tc::mma_commit(&bars[V1_TFREE]);
+            ok = tc::mbar_wait(&bars[V1_TFREE], c & 1, abort);
+            if (ok) load_vo(c + 1);
+          }
+        }
+      }
+    }
+    if (leader && nch > 0) {
+      tc::mma_commit(&bars[V1_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[V1_FINAL], 0)) atomicExch(a.err, 2);
     }
     __syncwarp();
   } else {
@@ -278,7 +335,6 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
     const int mrow = m64_row(q4, lane), mpar = lane >> 4;
     float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
-    float *const sA1 = reinterpret_cast<float *>(sm + P.a1);
     const float *st0 = a.fwd_state + ((size_t)n * a.nseg + seg) * E;
     // ---- prologue
     for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
@@ -312,49 +368,30 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
     tc::tmem_wait_st();
     tc::fence_async_smem();
     tc::tc_fence_before();
-    tc::named_bar_sync(1, NEPI_T);
-    tc::warp_arrive(&bars[W_INIT]);
+    tc::named_bar_sync(N1_INIT, NTHR);
 
     bool ok = true;
-    for (int c = 0; c < nch && ok; ++c) {
+    for (int c = 0; c < nch; ++c) {
       const int cg = c_begin + c, tok0 = cg * C;
       const int nt = min(C, a.T - tok0);
-      const float *Acur = (c & 1) ? sA1 : sA0;
       const uint32_t aCur = sbase + ((c & 1) ? P.a1 : P.a0), aNxt = sbase + ((c & 1) ? P.a0 : P.a1);
+      const float *Acur = reinterpret_cast<const float *>(sm + ((c & 1) ? P.a1 : P.a0));
       // the row-127 threads wrote this chunk's A during the previous one
-      ok = tc::warp_sync(&bars[W_ESYNC], c & 1, abort);
-      if (!ok) break;
-      // ---- P1m = tril-masked dO V^T ; chunk-start A to global
-      for (int s = threadIdx.x; s < S; s += NEPI_T) a.chunkA[((size_t)n * a.nchunks + cg) * S + s] = Acur[s];
-      ok = tc::warp_wait(&bars[W_P1], c & 1, abort);
-      if (!ok) break;
-      __syncwarp();
-      tc::tc_fence_after();
-      {
-        float v[32];
-        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * hq, v);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * hq + i > t) v[i] = 0.f;
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
+      tc::named_bar_sync(N1_ESYNC, NEPI_T);
+      if (ok) {
+        for (int s = threadIdx.x; s < S; s += NEPI_T) a.chunkA[((size_t)n * a.nchunks + cg) * S + s] = Acur[s];
       }
-      tc::fence_async_smem();
-      tc::tc_fence_before();
-      tc::warp_arrive(&bars[W_P1M]);
-      for (int g = 0; g < NG && ok; ++g) {
+      for (int g = 0; g < NG; ++g) {
         const int u = c * NG + g;
         float thQ[4], qQ[4], inv[16];  // this row's Q-side tanh and plane sigmoids of table 4g + hq
-        // ---- Pk, pq
-        ok = tc::warp_wait(&bars[W_PROJ], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        // ---- Pk ; chunk-start B state of this group -> smem bf16 + global
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_PROJ], u & 1, abort));
         tc::tc_fence_after();
-        {
-          float pk4[4], pr[16];
-          tc::tmem_ld4(tmem + lane_off + BT_R + 4 * hq, pk4);
-          tc::tmem_ld4(tmem + lane_off + BT_R + 16 + 4 * hq, thQ);
+        if (ok) {
+          float pk4[4], pr[16], bv[16];
+          tc::tmem_ld4(tmem + lane_off + B1_PJ + 4 * hq, pk4);
+          tc::tmem_ld4(tmem + lane_off + B1_PJ + 16 + 4 * hq, thQ);
+          tc::tmem_ld16(tmem + lane_off + T_BF + 64 * (g >> 1) + 16 * hq, bv);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -370,37 +407,6 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
           plane_sigmoids(thQ, a.scale, a.poly, qQ);
-          corner_probs(qQ, pr);
-          if (t >= nt) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pr[i] = 0.f;
-          }
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, pr + 8 * ch);
-        }
-        tc::fence_async_smem();
-        tc::tc_fence_before();
-        tc::warp_arrive(&bars[W_PK]);
-        // ---- inv, W ; chunk-start B state of this group -> smem bf16 + global
-        ok = tc::warp_wait(&bars[W_APREF], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
-        tc::tc_fence_after();
-        {
-          float ap[16], pq[16], bv[16];
-          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, ap);
-          tc::tmem_ld16(tmem + lane_off + T_BF + 64 * (g >> 1) + 16 * hq, bv);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::ld_row_chunk(sbase + P.w, t, 2 * hq + ch, pq + 8 * ch);
-          const int sb = g * GW + 16 * hq;
-          add_shared_row<16>(aCur + 4 * sb, ap);  // + (A + eps) at chunk start
-          if (t == C - 1) store_shared_row<16>(aNxt + 4 * sb, ap);
-          rcp_n<16>(ap, inv, a.batch_rcp);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) pq[i] *= inv[i];
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, pq + 8 * ch);
           if (mpar == (g & 1)) {
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst, mrow, 2 * hq + ch, bv + 8 * ch);
@@ -411,49 +417,73 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[W_W]);
-        // ---- G -> dpq (-> d proj_Q) and dA
-        ok = tc::warp_wait(&bars[W_G], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        tc::named_bar_arrive(N1_PK, NTHR);
+        if (g == 0) {
+          // ---- P1m = tril-masked dO V^T
+          if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_P1], c & 1, abort));
+          tc::tc_fence_after();
+          if (ok) {
+            float v[32];
+            tc::tmem_ld32(tmem + lane_off + B1_X + 32 * hq, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (32 * hq + i > t) v[i] = 0.f;
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
+          }
+          tc::fence_async_smem();
+          tc::tc_fence_before();
+          tc::named_bar_arrive(N1_P1M, NTHR);
+        }
+        // ---- inv from Apref (while G runs)
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_APREF], u & 1, abort));
         tc::tc_fence_after();
-        {
+        if (ok) {
+          float ap[16];
+          tc::tmem_ld16(tmem + lane_off + B1_R + 16 * hq, ap);
+          tc::tmem_wait_ld();
+          const int sb = g * GW + 16 * hq;
+          add_shared_row<16>(aCur + 4 * sb, ap);  // + (A + eps) at chunk start
+          if (t == C - 1) store_shared_row<16>(aNxt + 4 * sb, ap);
+          rcp_n<16>(ap, inv, a.batch_rcp);
+        }
+        // ---- G -> W, dpq (-> d proj_Q) and dA
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_G], u & 1, abort));
+        tc::tc_fence_after();
+        if (ok) {
           float G[16], pq[16], da[16];
-          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, G);
+          tc::tmem_ld16(tmem + lane_off + B1_X + 16 * hq, G);
           tc::tmem_wait_ld();
           corner_probs(qQ, pq);
+          const bool live = t < nt;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float gi = G[i] * inv[i];           // dpq
-            da[i] = -pq[i] * inv[i] * gi;              // dA
+            const float w = live ? pq[i] * inv[i] : 0.f;  // W
+            const float gi = live ? G[i] * inv[i] : 0.f;  // dpq
+            da[i] = -w * gi;                              // dA
             G[i] = gi;
-          }
-          if (t >= nt) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              da[i] = 0.f;
-              G[i] = 0.f;
-            }
+            inv[i] = w;
           }
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, da + 8 * ch);
+          for (int ch = 0; ch < 2; ++ch) {
+            tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, inv + 8 * ch);
+            tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, da + 8 * ch);
+          }
           float dp[4];
           table_probs_bwd(pq, G, thQ, a.scale, dp);
           tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[W_DA]);
+        tc::named_bar_arrive(N1_DA, NTHR);
       }
-      if (!ok) break;
       // ---- dQ, d in [16hq, 16hq+16)
-      ok = tc::warp_wait(&bars[W_OUT], c & 1, abort);
-      if (!ok) break;
-      __syncwarp();
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_OUT], c & 1, abort));
       tc::tc_fence_after();
-      {
+      if (ok) {
         float ov[16];
-        tc::tmem_ld16(tmem + lane_off + BT_X + 16 * hq, ov);
+        tc::tmem_ld16(tmem + lane_off + B1_X + 16 * hq, ov);
         tc::tmem_wait_ld();
         if (t < nt && a.dQ != nullptr) {
           __nv_bfloat16 *dst = a.dQ + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
@@ -462,11 +492,9 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
         }
       }
       tc::tc_fence_before();
-      tc::warp_arrive(&bars[W_OUTFREE]);
+      if (c + 1 < nch) tc::named_bar_arrive(N1_OUTFREE, NTHR);
     }
-    // ---- segment totals record (W_OUT of the last chunk covers every accumulation)
-    __syncwarp();
-    tc::tc_fence_after();
+    // ---- segment totals record (OUT of the last chunk covers every accumulation)
     if (ok && nch > 0) {
       float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
       for (int b = 0; b < nblk; ++b) {
