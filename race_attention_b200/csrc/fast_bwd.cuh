@@ -105,26 +105,10 @@ __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   m.dproj = o; o += TILE;
   m.a0 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
   m.a1 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
-  m.ga = o; o += GW * 4;
+  m.ga = o; o += 2 * GW * 4;  // two buffers (group parity)
   m.bars = o; o += 256;
   m.total = o + 1024;
   return m;
-}
-
-// TMEM columns: X (128) and R (64) scratch, then per-bucket M=64 state blocks
-constexpr uint32_t BT_X = 0, BT_R = 128, BT_ST = 192;
-
-enum { W_FULL = 0, W_INIT, W_P1, W_P1M, W_PROJ, W_PK, W_APREF, W_W, W_G, W_DA, W_DPK, W_Q2, W_DV, W_OUT, W_OUTFREE,
-       W_BST, W_FINAL, W_ESYNC, W_COUNT };
-
-// barriers all epilogue threads arrive on; the rest complete on one arrival
-__device__ __forceinline__ void bwd_init_bars(uint64_t *bars) {
-  for (int i = 0; i < W_COUNT; ++i) {
-    const bool epi = i == W_INIT || i == W_P1M || i == W_PK || i == W_W || i == W_DA || i == W_Q2 ||
-                     i == W_OUTFREE || i == W_ESYNC;
-    tc::mbar_init(&bars[i], epi ? NARR : 1);
-  }
-  tc::fence_mbar_init();
 }
 
 // row of an M=64 accumulator held by this thread's TMEM lane (lane quarter q, lane i):
@@ -527,6 +511,25 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
 
 // ===========================================================================
 // reverse walk of the backward pass
+//
+// TMEM: X [0,128) = P1 at chunk start, Q2 per group, dK at chunk end;
+// R [128,192) = Apref; GD [192,256) = G, then dpk; PJ [256,288) = proj of one
+// group; then GB, GA (M=64 suffix-state blocks) and DV [.., +64).
+// Schedule per group g ({X} named barrier, [X] mbarrier):
+//   control: {PK} Apref -> [APREF] ; {P1M, first group} ; [BST] G = dO Bst^T
+//            + P1m Pk -> [G] ; proj of the next group -> [PROJ] ;
+//            {W} Q2 = Pk W^T ; gB += W^T dO ; ([G] done: next group's Bst load) ;
+//            {DA} dpk = tril^T dA + V gBst^T + P1m^T W ; gA += dA^T 1 ;
+//            dV (+)= Pk gBst -> [DPK] ; {Q2} dV += Q2m dO ;
+//            chunk end: dK = dprojK planes -> [OUT] ; next chunk's proj(0) ;
+//            V/dO/Bst refill once every reader completed.
+//   epilogue: [PROJ] Pk, plane sigmoids, gBst and gA suffix copies {PK} ;
+//            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK, Q2m {Q2} ;
+//            chunk end: [OUT] dK, dV rows {OUTFREE}.
+enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_OUT, V3_TFREE, V3_FINAL, V3_COUNT };
+enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC };
+constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_PJ = 256, B3_ST = 288;
+
 __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                           const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV,
@@ -545,11 +548,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
   const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
   const int S = a.S, NG = a.ngroups, nblk = (NG + 1) / 2;
   const size_t E = (size_t)S + (size_t)S * HD;
-  const uint32_t T_GB = BT_ST, T_GA = BT_ST + 64 * nblk, T_DV = BT_ST + 80 * nblk;
+  const uint32_t T_GB = B3_ST, T_GA = B3_ST + 64 * nblk, T_DV = B3_ST + 80 * nblk;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    bwd_init_bars(bars);
+    for (int i = 0; i < V3_COUNT; ++i) tc::mbar_init(&bars[i], 1);
+    tc::fence_mbar_init();
   }
   if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
   tc::tc_fence_before();
@@ -559,140 +563,193 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
   volatile int *abort = &s_abort;
 
   if (warp == NEPI) {
-    if (lane == 0 && nch > 0) {
-      const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
-      const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
-      const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
-      const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
-      const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
-      const uint32_t id_mm = tc::idesc_bf16(C, GW, true, true);
-      const uint32_t id_q2 = tc::idesc_bf16(C, C, false, false);
-      const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
-      const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
-      const uint32_t id_dv = tc::idesc_bf16(C, HD, false, true);
-      const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o;
-      auto load_chunk = [=, &tmQ, &tmK, &tmV, &tmO](int c) {
-        const int t0 = (c_begin + c) * C;
-        tc::mbar_arrive_expect_tx(&bars[W_FULL], 4 * TILE);
-        tc::tma_load_3d(sm + oq, &tmQ, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + ok_, &tmK, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + ov, &tmV, &bars[W_FULL], 0, t0, n);
-        tc::tma_load_3d(sm + oo, &tmO, &bars[W_FULL], 0, t0, n);
-      };
-      const uint32_t obst = P.bst;
-      const int nchunks = a.nchunks;
-      auto load_bst = [=, &tmB](int c, int g) {
-        const int row = (int)(((size_t)n * nchunks + c_begin + c) * S + g * GW);
-        tc::mbar_arrive_expect_tx(&bars[W_BST], GW * 128);
-        tc::tma_load_2d(sm + obst, &tmB, &bars[W_BST], 0, row);
-      };
-      load_chunk(nch - 1);
+    // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
+    const bool leader = lane == 0;
+    const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
+    const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
+    const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
+    const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
+    const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
+    const uint32_t id_mm = tc::idesc_bf16(C, GW, true, true);
+    const uint32_t id_q2 = tc::idesc_bf16(C, C, false, false);
+    const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
+    const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
+    const uint32_t id_dv = tc::idesc_bf16(C, HD, false, true);
+    const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o, obst = P.bst;
+    const int nchunks = a.nchunks;
+    auto load_qk = [=, &tmQ, &tmK](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[V3_QK], 2 * TILE);
+      tc::tma_load_3d(sm + oq, &tmQ, &bars[V3_QK], 0, t0, n);
+      tc::tma_load_3d(sm + ok_, &tmK, &bars[V3_QK], 0, t0, n);
+    };
+    auto load_vo = [=, &tmV, &tmO](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[V3_VO], 2 * TILE);
+      tc::tma_load_3d(sm + ov, &tmV, &bars[V3_VO], 0, t0, n);
+      tc::tma_load_3d(sm + oo, &tmO, &bars[V3_VO], 0, t0, n);
+    };
+    auto load_bst = [=, &tmB](int c, int g) {
+      const int row = (int)(((size_t)n * nchunks + c_begin + c) * S + g * GW);
+      tc::mbar_arrive_expect_tx(&bars[V3_BST], GW * 128);
+      tc::tma_load_2d(sm + obst, &tmB, &bars[V3_BST], 0, row);
+    };
+    auto issue_proj = [=](int g) {
+      const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
+#pragma unroll
+      for (int k0 = 0; k0 < HD; k0 += 16) {
+        const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
+        tc::mma_bf16(tmem + B3_PJ, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
+        tc::mma_bf16(tmem + B3_PJ + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
+      }
+      tc::mma_commit(&bars[V3_PROJ]);
+    };
+    bool ok = true;
+    if (leader && nch > 0) {
+      load_qk(nch - 1);
+      load_vo(nch - 1);
       load_bst(nch - 1, 0);
-      bool ok = tc::mbar_wait(&bars[W_INIT], 0, abort);
-      for (int k = 0; k < nch && ok; ++k) {
-        const int c = nch - 1 - k;
-        ok = tc::mbar_wait(&bars[W_FULL], k & 1, abort);
-        if (ok && k > 0) ok = tc::mbar_wait(&bars[W_OUTFREE], (k - 1) & 1, abort);
-        if (!ok) break;
+    }
+    tc::named_bar_sync(N3_INIT, NTHR);  // planes, tril and suffix state are in place
+    if (leader && nch > 0) {
+      ok = tc::mbar_wait(&bars[V3_QK], 0, abort);
+      if (ok) {
         tc::tc_fence_after();
-        for (int k0 = 0; k0 < HD; k0 += 16)
-          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
-                       k0 > 0);
-        tc::mma_commit(&bars[W_P1]);
-        ok = tc::mbar_wait(&bars[W_P1M], k & 1, abort);
-        if (!ok) break;
-        for (int g = 0; g < NG && ok; ++g) {
-          const int u = k * NG + g;
-          if (u > 0) ok = tc::mbar_wait(&bars[W_Q2], (u - 1) & 1, abort);  // R and X free
-          if (!ok) break;
+        issue_proj(0);
+      }
+    }
+    for (int k = 0; k < nch; ++k) {
+      const int c = nch - 1 - k;
+      if (k > 0) tc::named_bar_sync(N3_OUTFREE, NTHR);  // dK and dV of the previous chunk are out
+      ok = ok && !*abort;
+      if (leader && ok) {
+        ok = tc::mbar_wait(&bars[V3_VO], k & 1, abort);
+        if (ok) {
           tc::tc_fence_after();
-          if (g > 0) {
-            // dV of the previous group of this chunk (its Q2m is in [w | da])
-            for (int k0 = 0; k0 < GW; k0 += 16)
-              tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
-                           id_dv, g > 1 || k0 > 0);
-            for (int k0 = 0; k0 < C; k0 += 16)
-              tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0),
-                           id_dv, true);
-            // no wait: the W_PROJ commit below completes only after these MMAs,
-            // and the epilogue rewrites Pk / w / da / gbst only after W_PROJ
-          }
-          const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
-          for (int k0 = 0; k0 < HD; k0 += 16) {
-            const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
-            tc::mma_bf16(tmem + BT_R + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
-          }
-          tc::mma_commit(&bars[W_PROJ]);
-          if (g > 0) load_bst(c, g);  // the previous group's G (the bst reader) completed before its W_Q2
-          ok = tc::mbar_wait(&bars[W_PK], u & 1, abort);
-          if (!ok) break;
-          tc::tc_fence_after();
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
-                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
-          tc::mma_commit(&bars[W_APREF]);
-          ok = tc::mbar_wait(&bars[W_W], u & 1, abort);
-          if (ok) ok = tc::mbar_wait(&bars[W_BST], u & 1, abort);
-          if (!ok) break;
-          tc::tc_fence_after();
+#pragma unroll
           for (int k0 = 0; k0 < HD; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
-                         id_gk, k0 > 0);
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.pk, k0, 0),
-                         id_gm, true);
-          tc::mma_commit(&bars[W_G]);
-          ok = tc::mbar_wait(&bars[W_DA], u & 1, abort);
-          if (!ok) break;
-          tc::tc_fence_after();
-          // dpk (in R) = tril^T dA + V gBst^T + P1m^T W
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_mnmajor(sbase + P.tril, k0, TILE), tc::desc_mnmajor(sbase + P.da, k0, 0),
-                         id_mm, k0 > 0);
-          for (int k0 = 0; k0 < HD; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gbst, k0, 0),
-                         id_gk, true);
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + BT_R, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
-                         id_mm, true);
-          // Q2 (in X) = Pk W^T
-          for (int k0 = 0; k0 < GW; k0 += 16)
-            tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
-                         id_q2, k0 > 0);
-          // suffix state: gB += W^T dO, gA += dA^T 1
-          for (int k0 = 0; k0 < C; k0 += 16) {
-            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
-                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
-            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
-                         tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, true);
-          }
-          tc::mma_commit(&bars[W_DPK]);
-        }
-        if (!ok) break;
-        // dV of the last group, then dK
-        ok = tc::mbar_wait(&bars[W_Q2], (k * NG + NG - 1) & 1, abort);
-        if (!ok) break;
-        tc::tc_fence_after();
-        for (int k0 = 0; k0 < GW; k0 += 16)
-          tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0), id_dv,
-                       NG > 1 || k0 > 0);
-        for (int k0 = 0; k0 < C; k0 += 16)
-          tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0), id_dv,
-                       true);
-        for (int k0 = 0; k0 < a.LP; k0 += 16)
-          tc::mma_bf16(tmem + BT_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
-                       id_dv, k0 > 0);
-        tc::mma_commit(&bars[W_OUT]);
-        if (k + 1 < nch) {
-          ok = tc::mbar_wait(&bars[W_OUT], k & 1, abort);  // all readers of the tiles and of bst done
-          if (!ok) break;
-          load_chunk(c - 1);
-          load_bst(c - 1, 0);
+            tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
+                         k0 > 0);
+          tc::mma_commit(&bars[V3_P1]);
         }
       }
-      tc::mma_commit(&bars[W_FINAL]);
-      if (!tc::mbar_wait_drain(&bars[W_FINAL], 0)) atomicExch(a.err, 2);
+      for (int g = 0; g < NG; ++g) {
+        const int u = k * NG + g;
+        tc::named_bar_sync(N3_PK, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + B3_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
+          tc::mma_commit(&bars[V3_APREF]);
+        }
+        if (g == 0) {
+          tc::named_bar_sync(N3_P1M, NTHR);
+          ok = ok && !*abort;
+        }
+        if (leader && ok) {
+          ok = tc::mbar_wait(&bars[V3_BST], u & 1, abort);
+          if (ok) {
+            tc::tc_fence_after();
+#pragma unroll
+            for (int k0 = 0; k0 < HD; k0 += 16)
+              tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
+                           id_gk, k0 > 0);
+#pragma unroll
+            for (int k0 = 0; k0 < C; k0 += 16)
+              tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.p1m, k0, TILE),
+                           tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, true);
+            tc::mma_commit(&bars[V3_G]);
+            if (g + 1 < NG) {
+              issue_proj(g + 1);
+            } else if (k + 1 < nch) {
+              load_qk(c - 1);  // the last proj of this chunk was consumed before {PK}
+            }
+          }
+        }
+        tc::named_bar_sync(N3_W, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+          // Q2 (in X) = Pk W^T ; suffix gB += W^T dO
+#pragma unroll
+          for (int k0 = 0; k0 < GW; k0 += 16)
+            tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
+                         id_q2, k0 > 0);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
+          // the Bst tile is free once G completed: next group's chunk-start state
+          if (g + 1 < NG) {
+            ok = tc::mbar_wait(&bars[V3_G], u & 1, abort);
+            if (ok) load_bst(c, g + 1);
+          }
+        }
+        tc::named_bar_sync(N3_DA, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+          // dpk (in GD) = tril^T dA + V gBst^T + P1m^T W ; gA += dA^T 1 ; dV (+)= Pk gBst
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + B3_GD, tc::desc_mnmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.da, k0, 0), id_mm, k0 > 0);
+#pragma unroll
+          for (int k0 = 0; k0 < HD; k0 += 16)
+            tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gbst, k0, 0),
+                         id_gk, true);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + B3_GD, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         id_mm, true);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
+                         tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, true);
+#pragma unroll
+          for (int k0 = 0; k0 < GW; k0 += 16)
+            tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
+                         id_dv, g > 0 || k0 > 0);
+          tc::mma_commit(&bars[V3_DPK]);
+        }
+        tc::named_bar_sync(N3_Q2, NTHR);
+        ok = ok && !*abort;
+        if (leader && ok) {
+          tc::tc_fence_after();
+          // dV += Q2m dO (Q2m is the two-block tile [w | da])
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0),
+                         id_dv, true);
+        }
+      }
+      if (leader && ok) {
+        for (int k0 = 0; k0 < a.LP; k0 += 16)
+          tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
+                       id_dv, k0 > 0);
+        tc::mma_commit(&bars[V3_OUT]);
+        if (k + 1 < nch) {
+          ok = tc::mbar_wait(&bars[V3_QK], (k + 1) & 1, abort);
+          if (ok) {
+            tc::tc_fence_after();
+            issue_proj(0);
+            // V, dO and the Bst tile are free once every MMA issued so far has completed
+            tc::mma_commit(&bars[V3_TFREE]);
+            ok = tc::mbar_wait(&bars[V3_TFREE], k & 1, abort);
+            if (ok) {
+              load_vo(c - 1);
+              load_bst(c - 1, 0);
+            }
+          }
+        }
+      }
+    }
+    if (leader && nch > 0) {
+      tc::mma_commit(&bars[V3_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[V3_FINAL], 0)) atomicExch(a.err, 2);
     }
     __syncwarp();
   } else {
@@ -737,23 +794,21 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     tc::tmem_wait_st();
     tc::fence_async_smem();
     tc::tc_fence_before();
-    tc::named_bar_sync(1, NEPI_T);
-    tc::warp_arrive(&bars[W_INIT]);
+    tc::named_bar_sync(N3_INIT, NTHR);
 
     bool ok = true;
-    uint32_t esync = 0;
-    for (int k = 0; k < nch && ok; ++k) {
+    for (int k = 0; k < nch; ++k) {
       const int c = nch - 1 - k, cg = c_begin + c, tok0 = cg * C;
       const int nt = min(C, a.T - tok0);
-      // chunk-start A (stored by the forward walk)
+      // chunk-start A + eps (stored by the forward walk)
       for (int s = threadIdx.x; s < S; s += NEPI_T) sA[s] = a.chunkA[((size_t)n * a.nchunks + cg) * S + s];
-      ok = tc::warp_wait(&bars[W_P1], k & 1, abort);
-      if (!ok) break;
-      __syncwarp();
+      tc::named_bar_sync(N3_ESYNC, NEPI_T);  // sA visible to all epilogue threads
+      // ---- P1m = tril-masked dO V^T
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_P1], k & 1, abort));
       tc::tc_fence_after();
-      {
+      if (ok) {
         float v[32];
-        tc::tmem_ld32(tmem + lane_off + BT_X + 32 * hq, v);
+        tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i)
@@ -763,20 +818,19 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
-      ok = tc::warp_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sA visible to all epilogue threads
-      if (!ok) break;
-      tc::warp_arrive(&bars[W_P1M]);
-      for (int g = 0; g < NG && ok; ++g) {
+      tc::named_bar_arrive(N3_P1M, NTHR);
+      for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
         float thK[4], qK[4], qQ[4], inv[16];  // K-side tanh, K and Q plane sigmoids of table 4g + hq
-        ok = tc::warp_wait(&bars[W_PROJ], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        // ---- Pk ; suffix gB (bf16) and gA copies of group g
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_PROJ], u & 1, abort));
         tc::tc_fence_after();
-        {
-          float pr[16];
-          tc::tmem_ld4(tmem + lane_off + BT_R + 4 * hq, thK);
-          tc::tmem_ld4(tmem + lane_off + BT_R + 16 + 4 * hq, qQ);
+        if (ok) {
+          float pr[16], bv[16], av;
+          tc::tmem_ld4(tmem + lane_off + B3_PJ + 4 * hq, thK);
+          tc::tmem_ld4(tmem + lane_off + B3_PJ + 16 + 4 * hq, qQ);
+          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
+          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -792,17 +846,24 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           }
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
+          if (mpar == (g & 1)) {
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 2 * hq + ch, bv + 8 * ch);
+            if (hq == 0) sGA[(g & 1) * GW + mrow] = av;
+          }
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[W_PK]);
-        ok = tc::warp_wait(&bars[W_APREF], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        tc::named_bar_arrive(N3_PK, NTHR);
+        // sGA (double-buffered by group parity: a warp may write the next group's
+        // copy while a slower one still reads this one) complete before any read
+        tc::named_bar_sync(N3_GSYNC, NEPI_T);
+        // ---- W = pq / (A + eps)
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_APREF], u & 1, abort));
         tc::tc_fence_after();
-        {
+        if (ok) {
           float ap[16], w[16];
-          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, ap);
+          tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, ap);
           tc::tmem_wait_ld();
           corner_probs(qQ, w);
           const int sb = g * GW + 16 * hq;
@@ -815,50 +876,38 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[W_W]);
-        ok = tc::warp_wait(&bars[W_G], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        tc::named_bar_arrive(N3_W, NTHR);
+        // ---- dA = -W G / (A + eps)
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_G], u & 1, abort));
         tc::tc_fence_after();
-        {
-          float G[16], pq[16], bv[16], av;
-          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, G);
-          // suffix state (after this chunk) of group g: bf16 copy for the MMAs, gA to smem
-          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
-          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
+        if (ok) {
+          float G[16], pq[16];
+          tc::tmem_ld16(tmem + lane_off + B3_GD + 16 * hq, G);
           tc::tmem_wait_ld();
           corner_probs(qQ, pq);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;  // dA
+          for (int i = 0; i < 16; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, G + 8 * ch);
-          if (mpar == (g & 1)) {
-#pragma unroll
-            for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 2 * hq + ch, bv + 8 * ch);
-            if (hq == 0) sGA[mrow] = av;
-          }
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        ok = tc::warp_sync(&bars[W_ESYNC], (esync++) & 1, abort);  // sGA complete (read after W_DPK)
-        if (!ok) break;
-        tc::warp_arrive(&bars[W_DA]);
-        ok = tc::warp_wait(&bars[W_DPK], u & 1, abort);
-        if (!ok) break;
-        __syncwarp();
+        tc::named_bar_arrive(N3_DA, NTHR);
+        // ---- dpk -> d proj_K ; Q2m
+        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_DPK], u & 1, abort));
         tc::tc_fence_after();
-        {
+        if (ok) {
           float dpk[16], pk[16], dp[4];
-          tc::tmem_ld16(tmem + lane_off + BT_R + 16 * hq, dpk);
+          tc::tmem_ld16(tmem + lane_off + B3_GD + 16 * hq, dpk);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) dpk[i] += sGA[16 * hq + i];
+          for (int i = 0; i < 16; ++i) dpk[i] += sGA[(g & 1) * GW + 16 * hq + i];
           corner_probs(qK, pk);
           table_probs_bwd(pk, dpk, thK, a.scale, dp);
           tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
           // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64)
           float v[32];
-          tc::tmem_ld32(tmem + lane_off + BT_X + 32 * hq, v);
+          tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i)
@@ -868,16 +917,14 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::warp_arrive(&bars[W_Q2]);
+        tc::named_bar_arrive(N3_Q2, NTHR);
       }
-      if (!ok) break;
-      ok = tc::warp_wait(&bars[W_OUT], k & 1, abort);
-      if (!ok) break;
-      __syncwarp();
+      // ---- dK, dV rows
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_OUT], k & 1, abort));
       tc::tc_fence_after();
-      {
+      if (ok) {
         float kv[16], vv[16];
-        tc::tmem_ld16(tmem + lane_off + BT_X + 16 * hq, kv);
+        tc::tmem_ld16(tmem + lane_off + B3_X + 16 * hq, kv);
         tc::tmem_ld16(tmem + lane_off + T_DV + 16 * hq, vv);
         tc::tmem_wait_ld();
         if (t < nt) {
@@ -891,7 +938,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
       }
       tc::tc_fence_before();
-      tc::warp_arrive(&bars[W_OUTFREE]);
+      if (k + 1 < nch) tc::named_bar_arrive(N3_OUTFREE, NTHR);
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }
