@@ -263,8 +263,10 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    n0 = rb._lib.load().race_launch_counter()
+    lib = rb._lib.load()
+    n0 = lib.race_launch_counter()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lib.race_kernel_timing(1)  # CUDA events around each tcgen05 launch, on its stream
     with ClockSampler(local) as clk:
         start.record()
         for _ in range(args.steps):
@@ -272,7 +274,9 @@ def run_ours(args, cfg):
         end.record()
         torch.cuda.synchronize()
     barrier()
-    launches = (rb._lib.load().race_launch_counter() - n0) // args.steps
+    launches = (lib.race_launch_counter() - n0) // args.steps
+    kernels = kernel_times(lib, args.steps)
+    lib.race_kernel_timing(0)
     ms = start.elapsed_time(end) / args.steps
     fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_fwd)
     bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in ev_bwd)
@@ -283,17 +287,7 @@ def run_ours(args, cfg):
     tokens = B * T * world
     value = tokens / (ms / 1e3)
 
-    # roofline of the dominant call (the fused backward, race_bwd_qkv): algorithmic bytes =
-    # read Q,K,V,dO + write dQ,dK,dV = 7*D*e per token-head
-    e = 2 if dtype == torch.bfloat16 else 4
-    hbm, tc, src = _peaks()
-    bwd_bytes = 7 * D * e * B * H * T
-    achieved = bwd_bytes / (bwd_ms / 1e3) / 1e9
-    layer_bytes = 11 * D * e * B * H * T
-    roof = {"bound": "hbm", "kernel": "race_bwd_qkv (fused backward call)", "achieved": achieved, "peak": hbm,
-            "unit": "GB/s", "frac": achieved / hbm, "traffic": None, "peak_source": src,
-            "step_achieved": layer_bytes / (ms / 1e3) / 1e9, "step_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
-            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms}
+    roof = roofline(kernels, cfg, ms, fwd_ms, bwd_ms)
 
     # e2e: same step through the public API with host (pinned) buffers, copies inside the timed region
     e2e = None
@@ -311,12 +305,97 @@ def run_ours(args, cfg):
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
                 "data": "synthetic (seeded randn, BASELINE shapes)", "config": config_dict(args, cfg),
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+                "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": int(launches),
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+# Algorithmic HBM bytes per token-head of each tcgen05 kernel (its own inputs and
+# outputs, D*e each; chunk-state records are implementation traffic and excluded),
+# and the MMA work it issues per 128-token chunk of one stream (fp32-accumulated
+# bf16 FMAs, from the kernels' MMA schedules for S = 16L buckets, D = 64).
+KERNEL_IO = {"fwd_totals_kernel": 2, "fwd_readout_kernel": 4, "bwd_fwd_kernel": 5, "bwd_rev_kernel": 6}
+
+
+def mma_fma_per_chunk(kernel, S, D=64, C=128):
+    LP = S // 4
+    if kernel == "fwd_totals_kernel":
+        return C * D * LP + (S // 128) * (128 * D * C + 128 * 16 * C)
+    if kernel == "fwd_readout_kernel":
+        return 2 * C * D * LP + (S // 128) * (C * 128 * C + C * C * 128 + C * D * 128 + C * D * C + 128 * D * C)
+    g = S // 64  # 64-bucket groups of the backward walks
+    proj = 2 * C * 16 * D
+    if kernel == "bwd_fwd_kernel":
+        per = proj + C * 64 * C + (C * 64 * D + C * 64 * C) + 64 * D * C + 64 * D * C + 64 * 16 * C
+        return C * C * D + g * per + C * D * LP
+    if kernel == "bwd_rev_kernel":
+        per = (proj + C * 64 * C + (C * 64 * D + C * 64 * C) + C * C * 64 + (C * 64 * D + C * 64 * C)
+               + 64 * D * C + C * 64 * C + 64 * 16 * C + C * D * 64 + C * D * C)
+        return C * C * D + g * per + C * D * LP
+    return 0
+
+
+def kernel_times(lib, steps):
+    import ctypes
+    from race_attention_b200 import _lib as L
+    out = {}
+    total = 0.0
+    for i, name in enumerate(L.KERNEL_NAMES):
+        ms, n = ctypes.c_double(0.0), ctypes.c_longlong(0)
+        if lib.race_kernel_time(i, ctypes.byref(ms), ctypes.byref(n)) != 0 or n.value == 0:
+            continue
+        out[name] = {"launches_per_step": n.value / steps, "ms_per_launch": ms.value / n.value,
+                     "ms_per_step": ms.value / steps}
+        total += ms.value / steps
+    for v in out.values():
+        v["share"] = v["ms_per_step"] / total if total else None
+    return out
+
+
+def _ncu_traffic(kernel, token_heads):
+    """DRAM bytes per launch from the committed ncu summary of this kernel (measured
+    on a smaller case: bytes per token-head x this launch's token-heads), else None."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_ncu.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_token_head:"):
+                    return float(line.split(":")[1]) * token_heads
+    except OSError:
+        pass
+    return None
+
+
+def roofline(kernels, cfg, ms, fwd_ms, bwd_ms):
+    """HBM roofline of the dominant kernel (largest device time per step) from its
+    live CUDA-event duration; the step-level figure uses the layer's 11*D*e bytes."""
+    B, H, T, D, L, P, dtype, scale = cfg
+    e = 2 if dtype == torch.bfloat16 else 4
+    S = L << P
+    hbm, tc, src = _peaks()
+    th = B * H * T  # token-heads per launch (all streams of this rank)
+    layer_bytes = 11 * D * e * th
+    roof = {"bound": "hbm", "unit": "GB/s", "peak": hbm, "peak_source": src,
+            "step_achieved": layer_bytes / (ms / 1e3) / 1e9, "step_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms}
+    fast = {k: v for k, v in kernels.items() if k in KERNEL_IO}
+    if not fast:
+        roof.update({"kernel": None, "achieved": None, "frac": None, "traffic": None})
+        return roof
+    k = max(fast, key=lambda n: fast[n]["ms_per_step"])
+    t = fast[k]["ms_per_launch"] / 1e3
+    achieved = KERNEL_IO[k] * D * e * th / t / 1e9
+    chunks = B * H * math.ceil(T / 128)
+    mma_tflops = 2 * mma_fma_per_chunk(k, S, D) * chunks / t / 1e12
+    roof.update({"kernel": k, "achieved": achieved, "frac": achieved / hbm,
+                 "algorithmic_bytes_per_launch": KERNEL_IO[k] * D * e * th,
+                 "traffic": _ncu_traffic(k, th), "ms_per_launch": fast[k]["ms_per_launch"],
+                 "mma_issued_tflops": mma_tflops, "mma_frac_of_bf16_peak": mma_tflops / tc})
+    return roof
 
 
 def run_e2e(layer, cfg, dev, world, barrier, args, planes):

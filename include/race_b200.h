@@ -68,6 +68,20 @@ const char *race_last_error(void);
  * process (host-side counter; used to report launches per benchmark step). */
 unsigned long long race_launch_counter(void);
 
+/* Diagnostic (no counterpart in the reference): device time of the tcgen05
+ * kernels.  While enabled, CUDA events are recorded on the launch stream
+ * around every launch of the kernels below; race_kernel_time() waits for the
+ * events recorded so far and returns the totals since the last enable.
+ * Enabling clears the totals.  Not for use inside stream capture. */
+#define RACE_KT_FWD_TOTALS 0   /* fused K-hash + segment totals          */
+#define RACE_KT_FWD_READOUT 1  /* forward readout                        */
+#define RACE_KT_BWD_FWD 2      /* backward, forward walk (dQ, grad totals) */
+#define RACE_KT_BWD_REV 3      /* backward, reverse walk (dK, dV)        */
+#define RACE_KT_SCAN 4         /* segment prefix / suffix scans          */
+#define RACE_KT_COUNT 5
+int race_kernel_timing(int enable);
+int race_kernel_time(int kernel, double *total_ms, long long *launches);
+
 /* Bytes of device workspace `op` needs for these sizes (pure host function).
  * chunk <= 0 selects the library default. */
 int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D,

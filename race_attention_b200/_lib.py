@@ -19,6 +19,8 @@ RACE_OK = 0
 RACE_F32 = 0
 RACE_BF16 = 1
 OP_FWD_PROBS, OP_BWD_PROBS, OP_FWD_QKV, OP_BWD_QKV, OP_STATE, OP_BWD_TOTALS = range(6)
+# kernel ids of race_kernel_time (include/race_b200.h RACE_KT_*)
+KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_fwd_kernel", "bwd_rev_kernel", "chunk_scan")
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -32,6 +34,8 @@ SIGNATURES = {
     "race_status_string": [_I],
     "race_last_error": [],
     "race_launch_counter": [],
+    "race_kernel_timing": [_I],
+    "race_kernel_time": [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)],
     "race_workspace_bytes": [_I, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I64, ctypes.POINTER(_SZ)],
     "race_fwd_probs": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _I64, _P, _SZ, _P],
     "race_bwd_probs": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _I64, _P, _SZ, _P],

@@ -513,20 +513,23 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant_
 // reverse walk of the backward pass
 //
 // TMEM: X [0,128) = P1 at chunk start, Q2 per group, dK at chunk end;
-// R [128,192) = Apref; GD [192,256) = G, then dpk; PJ [256,288) = proj of one
+// R [128,192) = Apref, then dpk; GD [192,256) = G; PJ [256,288) = proj of one
 // group; then GB, GA (M=64 suffix-state blocks) and DV [.., +64).
 // Schedule per group g ({X} named barrier, [X] mbarrier):
 //   control: {PK} Apref -> [APREF] ; {P1M, first group} ; [BST] G = dO Bst^T
-//            + P1m Pk -> [G] ; proj of the next group -> [PROJ] ;
-//            {W} Q2 = Pk W^T ; gB += W^T dO ; ([G] done: next group's Bst load) ;
-//            {DA} dpk = tril^T dA + V gBst^T + P1m^T W ; gA += dA^T 1 ;
-//            dV (+)= Pk gBst -> [DPK] ; {Q2} dV += Q2m dO ;
+//            + P1m Pk -> [G] ;
+//            {W} Q2 = Pk W^T ; dpk = V gBst^T + P1m^T W (in R) ; gB += W^T dO ;
+//            ([G] done: next group's Bst load) ;
+//            {DA} dpk += tril^T dA -> [DPK] ; gA += dA^T 1 ; dV (+)= Pk gBst -> [D2] ;
+//            proj of the next group -> [PROJ] ; {Q2} dV += Q2m dO ;
+// (critical MMAs first in each handoff: the tensor pipe runs them in order)
 //            chunk end: dK = dprojK planes -> [OUT] ; next chunk's proj(0) ;
 //            V/dO/Bst refill once every reader completed.
 //   epilogue: [PROJ] Pk, plane sigmoids, gBst and gA suffix copies {PK} ;
-//            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK, Q2m {Q2} ;
+//            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK, [D2] Q2m {Q2} ;
 //            chunk end: [OUT] dK, dV rows {OUTFREE}.
-enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_OUT, V3_TFREE, V3_FINAL, V3_COUNT };
+enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_D2, V3_OUT, V3_TFREE, V3_FINAL,
+       V3_COUNT };
 enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC };
 constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_PJ = 256, B3_ST = 288;
 
@@ -662,22 +665,27 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
               tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.p1m, k0, TILE),
                            tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, true);
             tc::mma_commit(&bars[V3_G]);
-            if (g + 1 < NG) {
-              issue_proj(g + 1);
-            } else if (k + 1 < nch) {
-              load_qk(c - 1);  // the last proj of this chunk was consumed before {PK}
-            }
+            if (g + 1 == NG && k + 1 < nch) load_qk(c - 1);  // the chunk's last proj was consumed before {PK}
           }
         }
         tc::named_bar_sync(N3_W, NTHR);
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
-          // Q2 (in X) = Pk W^T ; suffix gB += W^T dO
+          // Q2 (in X) = Pk W^T ; dpk (in R, Apref consumed) = V gBst^T + P1m^T W ;
+          // then, off the critical path, suffix gB += W^T dO
 #pragma unroll
           for (int k0 = 0; k0 < GW; k0 += 16)
             tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
                          id_q2, k0 > 0);
+#pragma unroll
+          for (int k0 = 0; k0 < HD; k0 += 16)
+            tc::mma_bf16(tmem + B3_R, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gbst, k0, 0),
+                         id_gk, k0 > 0);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         id_mm, true);
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
@@ -692,19 +700,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
-          // dpk (in GD) = tril^T dA + V gBst^T + P1m^T W ; gA += dA^T 1 ; dV (+)= Pk gBst
+          // dpk += tril^T dA -> [DPK] ; then gA += dA^T 1 ; dV (+)= Pk gBst -> [D2] ; next proj
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + B3_GD, tc::desc_mnmajor(sbase + P.tril, k0, TILE),
-                         tc::desc_mnmajor(sbase + P.da, k0, 0), id_mm, k0 > 0);
-#pragma unroll
-          for (int k0 = 0; k0 < HD; k0 += 16)
-            tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gbst, k0, 0),
-                         id_gk, true);
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + B3_GD, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
-                         id_mm, true);
+            tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.tril, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.da, k0, 0), id_mm, true);
+          tc::mma_commit(&bars[V3_DPK]);
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
@@ -713,7 +714,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           for (int k0 = 0; k0 < GW; k0 += 16)
             tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
                          id_dv, g > 0 || k0 > 0);
-          tc::mma_commit(&bars[V3_DPK]);
+          tc::mma_commit(&bars[V3_D2]);
+          if (g + 1 < NG) issue_proj(g + 1);
         }
         tc::named_bar_sync(N3_Q2, NTHR);
         ok = ok && !*abort;
@@ -898,22 +900,26 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         tc::tc_fence_after();
         if (ok) {
           float dpk[16], pk[16], dp[4];
-          tc::tmem_ld16(tmem + lane_off + B3_GD + 16 * hq, dpk);
+          tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, dpk);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) dpk[i] += sGA[(g & 1) * GW + 16 * hq + i];
           corner_probs(qK, pk);
           table_probs_bwd(pk, dpk, thK, a.scale, dp);
           tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
-          // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64)
+          // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64),
+          // written once gB, gA and the rest of dpk (readers of w and dA) completed
           float v[32];
           tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             if (32 * hq + i < t) v[i] = 0.f;
+          ok = tc::warp_all(tc::mbar_wait(&bars[V3_D2], u & 1, abort));
+          if (ok) {
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, v + 8 * ch);
+            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, v + 8 * ch);
+          }
         }
         tc::fence_async_smem();
         tc::tc_fence_before();

@@ -11,6 +11,9 @@
 #include <algorithm>
 #include <cstring>
 #include <initializer_list>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "decode.cuh"
@@ -45,6 +48,56 @@ int check_launch(const char *what) {
   if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return ok();
 }
+
+// Per-kernel device timing of the tcgen05 path (race_kernel_timing): an event
+// pair recorded on the launch stream around each launch while enabled.
+struct KernelTimer {
+  std::mutex mu;
+  bool on = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending[RACE_KT_COUNT];
+  double ms[RACE_KT_COUNT] = {};
+  long long launches[RACE_KT_COUNT] = {};
+};
+
+KernelTimer &ktimer() {
+  static KernelTimer t;
+  return t;
+}
+
+class KernelScope {
+ public:
+  KernelScope(int id, cudaStream_t s) : id_(id), s_(s) {
+    KernelTimer &t = ktimer();
+    std::lock_guard<std::mutex> g(t.mu);
+    if (!t.on) return;
+    if (cudaEventCreate(&e0_) != cudaSuccess || cudaEventCreate(&e1_) != cudaSuccess ||
+        cudaEventRecord(e0_, s_) != cudaSuccess) {
+      release();
+      cudaGetLastError();
+    }
+  }
+  ~KernelScope() { release(); }
+  void stop() {
+    if (!e0_) return;
+    if (cudaEventRecord(e1_, s_) == cudaSuccess) {
+      KernelTimer &t = ktimer();
+      std::lock_guard<std::mutex> g(t.mu);
+      t.pending[id_].push_back({e0_, e1_});
+      e0_ = e1_ = nullptr;
+    }
+    release();
+  }
+
+ private:
+  void release() {
+    if (e0_) cudaEventDestroy(e0_);
+    if (e1_) cudaEventDestroy(e1_);
+    e0_ = e1_ = nullptr;
+  }
+  int id_;
+  cudaStream_t s_;
+  cudaEvent_t e0_ = nullptr, e1_ = nullptr;
+};
 
 constexpr int64_t kMaxN = 65535;
 constexpr int64_t kMaxS = 1024;
@@ -361,11 +414,18 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
   if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   const fk::TotSmem ts = fk::tot_smem_plan(a.ngroups, a.LP);
   RACE_TRY(set_smem(fk::fwd_totals_kernel, ts.total));
-  fk::fwd_totals_kernel<<<(unsigned)(N * pl.nseg), fk::NTHR, ts.total, s>>>(mK, mV, a);
+  {
+    KernelScope ks(RACE_KT_FWD_TOTALS, s);
+    fk::fwd_totals_kernel<<<(unsigned)(N * pl.nseg), fk::NTHR, ts.total, s>>>(mK, mV, a);
+    ks.stop();
+  }
   RACE_TRY(check_launch("fast fwd_totals"));
   gen::Dims p = make_dims(N, T, S, fk::HD, eps);
   p.G = pl.nseg;
-  return launch_scan(at<float>(ws, pl.rec_off), A0, B0, Af, Bf, p, 0, s);
+  KernelScope ks(RACE_KT_SCAN, s);
+  const int rc = launch_scan(at<float>(ws, pl.rec_off), A0, B0, Af, Bf, p, 0, s);
+  ks.stop();
+  return rc;
 }
 
 int fast_forward(const void *Q, const void *K, const void *V, const float *planes_T, void *out, const float *A0,
@@ -379,7 +439,9 @@ int fast_forward(const void *Q, const void *K, const void *V, const float *plane
   a.out = static_cast<__nv_bfloat16 *>(out);
   const fk::FwdSmem fs = fk::fwd_smem_plan(a.ngroups, a.LP);
   RACE_TRY(set_smem(fk::fwd_readout_kernel, fs.total));
+  KernelScope ks(RACE_KT_FWD_READOUT, s);
   fk::fwd_readout_kernel<<<(unsigned)(N * a.nseg), fk::NTHR, fs.total, s>>>(mQ, mK, mV, a);
+  ks.stop();
   return check_launch("fast fwd_readout");
 }
 
@@ -425,15 +487,26 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   const fk::BwdSmem bs = fk::bwd_smem_plan(b.LP, b.S);
   const unsigned grid = (unsigned)(N * bp.p.nseg);
   RACE_TRY(set_smem(fk::bwd_fwd_kernel, bs.total));
-  fk::bwd_fwd_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, b);
+  {
+    KernelScope ks(RACE_KT_BWD_FWD, s);
+    fk::bwd_fwd_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, b);
+    ks.stop();
+  }
   RACE_TRY(check_launch("fast bwd_fwd"));
   gen::Dims p = make_dims(N, T, S, fk::HD, eps);
   p.G = bp.p.nseg;
-  RACE_TRY(launch_scan(at<float>(ws, bp.bwd_rec), totals_only ? nullptr : gA, totals_only ? nullptr : gB, dA0, dB0,
-                       p, 1, s));
+  {
+    KernelScope ks(RACE_KT_SCAN, s);
+    const int rc = launch_scan(at<float>(ws, bp.bwd_rec), totals_only ? nullptr : gA, totals_only ? nullptr : gB,
+                               dA0, dB0, p, 1, s);
+    ks.stop();
+    RACE_TRY(rc);
+  }
   if (totals_only) return RACE_OK;
   RACE_TRY(set_smem(fk::bwd_rev_kernel, bs.total));
+  KernelScope ks(RACE_KT_BWD_REV, s);
   fk::bwd_rev_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, mB, b);
+  ks.stop();
   return check_launch("fast bwd_rev");
 }
 
@@ -479,6 +552,47 @@ const char *race_status_string(int status) {
 const char *race_last_error(void) { return g_err; }
 
 unsigned long long race_launch_counter(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int race_kernel_timing(int enable) {
+  KernelTimer &t = ktimer();
+  std::lock_guard<std::mutex> g(t.mu);
+  for (int k = 0; k < RACE_KT_COUNT; ++k) {
+    for (auto &ev : t.pending[k]) {
+      cudaEventDestroy(ev.first);
+      cudaEventDestroy(ev.second);
+    }
+    t.pending[k].clear();
+    t.ms[k] = 0;
+    t.launches[k] = 0;
+  }
+  t.on = enable != 0;
+  return ok();
+}
+
+int race_kernel_time(int kernel, double *total_ms, long long *launches) {
+  RACE_NONNULL(total_ms);
+  RACE_NONNULL(launches);
+  if (kernel < 0 || kernel >= RACE_KT_COUNT) return fail(RACE_ERR_ARG, "kernel id %d out of range", kernel);
+  KernelTimer &t = ktimer();
+  std::lock_guard<std::mutex> g(t.mu);
+  for (auto &ev : t.pending[kernel]) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(ev.second);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, ev.first, ev.second);
+    cudaEventDestroy(ev.first);
+    cudaEventDestroy(ev.second);
+    if (e != cudaSuccess) {
+      t.pending[kernel].clear();
+      return fail(RACE_ERR_CUDA, "kernel timing events: %s", cudaGetErrorString(e));
+    }
+    t.ms[kernel] += ms;
+    t.launches[kernel] += 1;
+  }
+  t.pending[kernel].clear();
+  *total_ms = t.ms[kernel];
+  *launches = t.launches[kernel];
+  return ok();
+}
 
 int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int64_t L, int64_t P, int dtype,
                          int64_t chunk, size_t *bytes) {

@@ -89,3 +89,17 @@ def test_decode_validation():
     # group too large
     assert lib.race_decode_step(p, p, p, 0, p, p, p, p, 64, 2, 64, 8, 4, 1e-6, 0.125, None) == \
         codes["RACE_ERR_UNSUPPORTED"]
+
+
+def test_kernel_timing_host_side():
+    """The timing diagnostic toggles and reports zero launches with no GPU work,
+    and rejects an out-of-range kernel id."""
+    import ctypes
+    from race_attention_b200 import _lib
+    lib = _lib.load()
+    assert lib.race_kernel_timing(1) == 0
+    ms, n = ctypes.c_double(-1.0), ctypes.c_longlong(-1)
+    assert lib.race_kernel_time(3, ctypes.byref(ms), ctypes.byref(n)) == 0
+    assert ms.value == 0.0 and n.value == 0
+    assert lib.race_kernel_time(len(_lib.KERNEL_NAMES), ctypes.byref(ms), ctypes.byref(n)) != 0
+    assert lib.race_kernel_timing(0) == 0

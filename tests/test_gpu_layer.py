@@ -178,3 +178,23 @@ def test_fast_backward_segments(B, H, T, L):
     assert close(dQ, dQ_r, 2e-2, floor)[0], relerr(dQ, dQ_r)
     assert close(dK, dK_r, 2e-2, floor)[0], relerr(dK, dK_r)
     assert close(dV, dV_r, 2e-2, floor)[0], relerr(dV, dV_r)
+
+
+@pytest.mark.parametrize("logit_scale,eps", [(1.0, 1e-6), (0.125, 1e-9), (2.0, 1e-10)])
+def test_fast_path_general_scale_and_eps(logit_scale, eps):
+    """The tcgen05 kernels take the plane sigmoids from a series only when
+    2|logit_scale| <= 1/2 and batch the reciprocals of A + eps four at a time
+    only when eps >= 1e-8; these cases take the SFU exponential and/or one
+    reciprocal per bucket instead, forward and backward, against the oracle."""
+    import race_attention_b200 as rb
+    B, H, T, L = 1, 4, 700, 16
+    Q, K, V, dO = qkv(B, H, T, 64, seed=17, scale=1.0 / 8.0, dtype=torch.bfloat16)
+    planes, _ = rb.build_planes_protos(64, 4, L, 1, device="cpu", seed=0)
+    assert rb.ops.fast_path(torch.bfloat16, 64, L, 4)
+    args = (Q.cuda(), K.cuda(), V.cuda())
+    out = rb.ops.fwd_qkv(*args, planes.cuda(), L, 4, eps=eps, logit_scale=logit_scale)
+    dQ, dK, dV = rb.ops.bwd_qkv(*args, dO.cuda(), planes.cuda(), L, 4, eps=eps, logit_scale=logit_scale)
+    ref, _, _ = O.race_qkv_fwd(Q, K, V, planes, L, 4, eps=eps, logit_scale=logit_scale)
+    dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, L, 4, eps=eps, logit_scale=logit_scale)
+    assert relerr(out, ref) < 2e-2
+    assert relerr(dQ, dQ_r) < 2e-2 and relerr(dK, dK_r) < 2e-2 and relerr(dV, dV_r) < 2e-2
