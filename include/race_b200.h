@@ -73,12 +73,13 @@ unsigned long long race_launch_counter(void);
  * around every launch of the kernels below; race_kernel_time() waits for the
  * events recorded so far and returns the totals since the last enable.
  * Enabling clears the totals.  Not for use inside stream capture. */
-#define RACE_KT_FWD_TOTALS 0   /* fused K-hash + segment totals          */
-#define RACE_KT_FWD_READOUT 1  /* forward readout                        */
-#define RACE_KT_BWD_FWD 2      /* backward, forward walk (dQ, grad totals) */
-#define RACE_KT_BWD_REV 3      /* backward, reverse walk (dK, dV)        */
-#define RACE_KT_SCAN 4         /* segment prefix / suffix scans          */
-#define RACE_KT_COUNT 5
+#define RACE_KT_FWD_TOTALS 0   /* fused K-hash + segment totals / chunk states */
+#define RACE_KT_FWD_READOUT 1  /* forward readout                              */
+#define RACE_KT_BWD_FWD 2      /* backward forward walk (gradient totals only) */
+#define RACE_KT_BWD_REV 3      /* backward reverse walk (segment-local dK, dV) */
+#define RACE_KT_SCAN 4         /* segment prefix / suffix scans                */
+#define RACE_KT_BWD_FIX 5      /* backward suffix fix-up (dK, dV, dQ)          */
+#define RACE_KT_COUNT 6
 int race_kernel_timing(int enable);
 int race_kernel_time(int kernel, double *total_ms, long long *launches);
 
@@ -150,6 +151,28 @@ int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO,
                  int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
                  float eps, float logit_scale,
                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* Forward that also keeps what the backward needs, and the backward that uses it
+ * (no counterpart in the reference; the reference's autograd saves probsK/probsQ
+ * instead, scaling/race_causal_cuda.py:57).  For the tcgen05 configurations
+ * race_saved_bytes() gives the size of the caller-owned `saved` buffer (16-byte
+ * aligned): the layer's state at every 128-token chunk start, A + eps fp32
+ * [N, ceil(T/128), S] then B bf16 [N, ceil(T/128), S, D]; race_bwd_qkv_saved()
+ * then skips the two passes that rebuild those states.  Pass the same
+ * Q, K, V, planes, A0, B0, eps and logit_scale to both.  Elsewhere the size is 0
+ * and the two calls are race_fwd_qkv / race_bwd_qkv. */
+int race_saved_bytes(int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, int dtype, size_t *bytes);
+int race_fwd_qkv_save(const void *Q, const void *K, const void *V, int dtype,
+                      const float *planes_T, void *out, const float *A0, const float *B0,
+                      float *A_final, float *B_final, void *saved, size_t saved_bytes,
+                      int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
+                      float logit_scale, void *workspace, size_t workspace_bytes, void *stream);
+int race_bwd_qkv_saved(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                       const float *planes_T, const void *saved, size_t saved_bytes,
+                       void *dQ, void *dK, void *dV, const float *A0, const float *B0,
+                       const float *gA_in, const float *gB_in, float *dA0, float *dB0,
+                       int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
+                       float logit_scale, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- state / decode (no reference counterpart: the reference's KV-cache
  * branch raises NotImplementedError, chat/nanochat/gpt.py:143-146) ---------- */

@@ -20,7 +20,8 @@ RACE_F32 = 0
 RACE_BF16 = 1
 OP_FWD_PROBS, OP_BWD_PROBS, OP_FWD_QKV, OP_BWD_QKV, OP_STATE, OP_BWD_TOTALS = range(6)
 # kernel ids of race_kernel_time (include/race_b200.h RACE_KT_*)
-KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_fwd_kernel", "bwd_rev_kernel", "chunk_scan")
+KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_fwd_kernel", "bwd_rev_kernel", "chunk_scan",
+                "bwd_fix_kernel")
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -50,6 +51,11 @@ SIGNATURES = {
     "race_fwd_probs_noalloc": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
     "race_bwd_sharded_phaseA": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F,
                                 _P, _SZ, _P],
+    "race_saved_bytes": [_I64, _I64, _I64, _I64, _I64, _I, ctypes.POINTER(_SZ)],
+    "race_fwd_qkv_save": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _F, _F, _P,
+                          _SZ, _P],
+    "race_bwd_qkv_saved": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                           _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
 }
 _RESTYPES = {"race_status_string": ctypes.c_char_p, "race_last_error": ctypes.c_char_p,
              "race_launch_counter": ctypes.c_ulonglong}

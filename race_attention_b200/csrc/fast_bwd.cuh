@@ -48,6 +48,8 @@ struct BwdArgs {
   float *chunkA;            // [N, nchunks, S]        fp32 A at chunk start
   __nv_bfloat16 *chunkB;    // [N, nchunks, S, 64]    bf16 B at chunk start
   __nv_bfloat16 *dQ, *dK, *dV;  // [N, T, 64]
+  __nv_bfloat16 *dprojQ;        // [N, T, 64] d proj_Q (columns >= LP unused), reverse walk -> fix-up
+  float *dprojK;                // [N, T, 64] segment-local d proj_K (fp32), reverse walk -> fix-up
   int *err;
 };
 
@@ -73,6 +75,9 @@ __device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g
   }
 }
 
+// x rounded to bf16 (round to nearest even, as the tile stores) and back
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
 __device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float *v) {
   uint4 w;
   w.x = tc::pack_bf16(v[0], v[1]);
@@ -84,10 +89,13 @@ __device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float
 
 // --------------------------------------------------------------------------
 struct BwdSmem {
-  uint32_t q, k, v, o, p1m, tril, planes, pk, w, da, bst, gbst, dproj, a0, a1, ga, bars, total;
+  uint32_t q, k, v, o, p1m, tril, planes, plo, pk, w, da, bst, gbst, diag, dproj, a0, a1, ga, bars, total;
 };
 
-__host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
+// rev: the reverse walk keeps the bf16 residuals of the planes (planes - bf16(planes)), so
+// that its projections are exact to ~2^-17, and the fp32 diagonal of P1 = dO V^T; it writes
+// d proj_K to global memory (no dproj tile) and needs no second A array.
+__host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S, bool rev = false) {
   BwdSmem m;
   uint32_t o = 0;
   m.q = o; o += TILE;
@@ -97,14 +105,16 @@ __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   m.p1m = o; o += 2 * TILE;
   m.tril = o; o += 2 * TILE;
   m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.plo = o; if (rev) o += (uint32_t)align_up((size_t)LP * 128, 1024);
   m.pk = o; o += TILE;
   m.w = o; o += TILE;
   m.da = o; o += TILE;  // must follow w: [w | da] is the 2-block Q2m tile of the reverse walk
   m.bst = o; o += GW * 128;
   m.gbst = o; o += GW * 128;
-  m.dproj = o; o += TILE;
+  m.diag = o; if (rev) o += C * 4;
+  m.dproj = o; if (!rev) o += TILE;
   m.a0 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
-  m.a1 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
+  m.a1 = o; if (!rev) o += (uint32_t)align_up((size_t)S * 4, 128);
   m.ga = o; o += 2 * GW * 4;  // two buffers (group parity)
   m.bars = o; o += 256;
   m.total = o + 1024;
@@ -540,10 +550,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap tmB, BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
-  const BwdSmem P = bwd_smem_plan(a.LP, a.S);
+  const BwdSmem P = bwd_smem_plan(a.LP, a.S, true);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
-  __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
+  // no static shared memory (it would cost a 1 KB aligned block): the TMEM base
+  // and the abort flag live after the barriers
+  uint32_t &s_tmem = *reinterpret_cast<uint32_t *>(sm + P.bars + 8 * V3_COUNT);
+  int &s_abort = *reinterpret_cast<int *>(sm + P.bars + 8 * V3_COUNT + 4);
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
@@ -597,13 +609,16 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       tc::mbar_arrive_expect_tx(&bars[V3_BST], GW * 128);
       tc::tma_load_2d(sm + obst, &tmB, &bars[V3_BST], 0, row);
     };
-    auto issue_proj = [=](int g) {
-      const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
+    auto issue_proj = [=](int g) {  // x (planes_hi + planes_lo): the projections to ~2^-17
 #pragma unroll
-      for (int k0 = 0; k0 < HD; k0 += 16) {
-        const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
-        tc::mma_bf16(tmem + B3_PJ, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
-        tc::mma_bf16(tmem + B3_PJ + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
+      for (int part = 0; part < 2; ++part) {
+        const uint32_t pl = sbase + (part ? P.plo : P.planes) + (uint32_t)g * 16 * 128;
+#pragma unroll
+        for (int k0 = 0; k0 < HD; k0 += 16) {
+          const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
+          tc::mma_bf16(tmem + B3_PJ, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, part > 0 || k0 > 0);
+          tc::mma_bf16(tmem + B3_PJ + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, part > 0 || k0 > 0);
+        }
       }
       tc::mma_commit(&bars[V3_PROJ]);
     };
@@ -729,10 +744,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         }
       }
       if (leader && ok) {
-        for (int k0 = 0; k0 < a.LP; k0 += 16)
-          tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
-                       id_dv, k0 > 0);
-        tc::mma_commit(&bars[V3_OUT]);
+        tc::mma_commit(&bars[V3_OUT]);  // dV of the chunk complete
         if (k + 1 < nch) {
           ok = tc::mbar_wait(&bars[V3_QK], (k + 1) & 1, abort);
           if (ok) {
@@ -765,11 +777,15 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     const int mrow = m64_row(q4, lane), mpar = lane >> 4;
     float *sA = reinterpret_cast<float *>(sm + P.a0);
     float *sGA = reinterpret_cast<float *>(sm + P.ga);
-    const float *sst = a.suf_state + ((size_t)n * a.nseg + seg) * E;
-    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
+    float *sDiag = reinterpret_cast<float *>(sm + P.diag);
+    const float *sst = a.suf_state ? a.suf_state + ((size_t)n * a.nseg + seg) * E : nullptr;
+    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {  // planes = hi + lo, both bf16
       const int j = i / HD, d = i % HD;
-      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(j, d >> 3) + (d & 7) * 2) =
-          __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
+      const float pv = a.planes[(size_t)d * a.LP + j];
+      const __nv_bfloat16 hi = __float2bfloat16(pv);
+      const uint32_t off = tc::sw128_off(j, d >> 3) + (d & 7) * 2;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + off) = hi;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.plo + off) = __float2bfloat16(pv - __bfloat162float(hi));
     }
     {
       float v[8];
@@ -779,10 +795,10 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
-    for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end -> TMEM, d in [16hq, +16)
+    for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end (zero: segment-local walk) -> TMEM
       const int g = 2 * b + mpar;
       float v[16];
-      if (g < NG) {
+      if (g < NG && sst != nullptr) {
         const float *src = sst + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = src[i];
@@ -791,7 +807,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
       }
       tc::tmem_st16(tmem + lane_off + T_GB + 64 * b + 16 * hq, v);
-      if (hq == 0) tc::tmem_st1(tmem + lane_off + T_GA + 16 * b, g < NG ? sst[g * GW + mrow] : 0.f);
+      if (hq == 0) tc::tmem_st1(tmem + lane_off + T_GA + 16 * b, g < NG && sst != nullptr ? sst[g * GW + mrow] : 0.f);
     }
     tc::tmem_wait_st();
     tc::fence_async_smem();
@@ -812,6 +828,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         float v[32];
         tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
         tc::tmem_wait_ld();
+        if (hq == q4) {  // fp32 diagonal P1[t][t] (the exact-diagonal corrections below)
+          float dg = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
+          sDiag[t] = dg;
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i)
           if (32 * hq + i > t) v[i] = 0.f;
@@ -823,24 +845,24 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       tc::named_bar_arrive(N3_P1M, NTHR);
       for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
-        float thK[4], qK[4], qQ[4], inv[16];  // K-side tanh, K and Q plane sigmoids of table 4g + hq
+        float thK[4], thQ[4], qK[4], qQ[4], inv[16];  // tanh and plane sigmoids of table 4g + hq
         // ---- Pk ; suffix gB (bf16) and gA copies of group g
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_PROJ], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
           float pr[16], bv[16], av;
           tc::tmem_ld4(tmem + lane_off + B3_PJ + 4 * hq, thK);
-          tc::tmem_ld4(tmem + lane_off + B3_PJ + 16 + 4 * hq, qQ);
+          tc::tmem_ld4(tmem + lane_off + B3_PJ + 16 + 4 * hq, thQ);
           tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
           tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             thK[i] = tanh_fast(thK[i]);
-            qQ[i] = tanh_fast(qQ[i]);
+            thQ[i] = tanh_fast(thQ[i]);
           }
           plane_sigmoids(thK, a.scale, a.poly, qK);
-          plane_sigmoids(qQ, a.scale, a.poly, qQ);
+          plane_sigmoids(thQ, a.scale, a.poly, qQ);
           corner_probs(qK, pr);
           if (t >= nt) {
 #pragma unroll
@@ -867,6 +889,14 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           float ap[16], w[16];
           tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, ap);
           tc::tmem_wait_ld();
+          {  // the MMA summed bf16(pk_t) on the diagonal: use pk_t itself there
+            float pk[16];
+            corner_probs(qK, pk);
+            if (t < nt) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) ap[i] += pk[i] - bf16r(pk[i]);
+            }
+          }
           corner_probs(qQ, w);
           const int sb = g * GW + 16 * hq;
           add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
@@ -883,14 +913,39 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_G], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
-          float G[16], pq[16];
+          float G[16], pq[16], pk[16], corr[16];
           tc::tmem_ld16(tmem + lane_off + B3_GD + 16 * hq, G);
           tc::tmem_wait_ld();
           corner_probs(qQ, pq);
+          corner_probs(qK, pk);
+          const bool live = t < nt;
+          // Exact diagonal (tau = t).  Its share of G is P1[t][t] pk_t and of dpk it is
+          // dA_t + P1[t][t] W_t = W_t (P1[t][t] - dpq_t), which cancels exactly at the first
+          // tokens; the MMAs used bf16 roundings of each factor, so swap them for fp32 ones
+          // (G here, dpk through corr in the dpk phase).
+          const float p1 = sDiag[t], p1b = bf16r(p1);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) G[i] = t < nt ? -pq[i] * inv[i] * inv[i] * G[i] : 0.f;
+          for (int i = 0; i < 16; ++i) {
+            const float g = G[i] + p1 * pk[i] - p1b * bf16r(pk[i]);
+            const float w = live ? pq[i] * inv[i] : 0.f;
+            const float dpq = live ? g * inv[i] : 0.f;
+            const float da = -w * dpq;
+            G[i] = da;
+            corr[i] = live ? (da - bf16r(da)) + (p1 * w - p1b * bf16r(w)) : 0.f;
+            inv[i] = dpq;
+          }
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, G + 8 * ch);
+          if (a.dprojQ != nullptr && live) {  // d proj_Q of table 4g + hq -> the fix-up's dQ
+            float dp[4];
+            table_probs_bwd(pq, inv, thQ, a.scale, dp);
+            uint2 w2;
+            w2.x = tc::pack_bf16(dp[0], dp[1]);
+            w2.y = tc::pack_bf16(dp[2], dp[3]);
+            *reinterpret_cast<uint2 *>(a.dprojQ + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * hq) = w2;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) inv[i] = corr[i];  // carried to the dpk phase
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -903,10 +958,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, dpk);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) dpk[i] += sGA[(g & 1) * GW + 16 * hq + i];
+          for (int i = 0; i < 16; ++i) dpk[i] += sGA[(g & 1) * GW + 16 * hq + i] + inv[i];  // + diagonal correction
           corner_probs(qK, pk);
           table_probs_bwd(pk, dpk, thK, a.scale, dp);
-          tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
+          if (t < nt)  // segment-local d proj_K of table 4g + hq, fp32, to the fix-up
+            *reinterpret_cast<float4 *>(a.dprojK + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * hq) =
+                make_float4(dp[0], dp[1], dp[2], dp[3]);
           // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64),
           // written once gB, gA and the rest of dpk (readers of w and dA) completed
           float v[32];
@@ -929,22 +986,355 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_OUT], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
-        float kv[16], vv[16];
-        tc::tmem_ld16(tmem + lane_off + B3_X + 16 * hq, kv);
+        float vv[16];
         tc::tmem_ld16(tmem + lane_off + T_DV + 16 * hq, vv);
         tc::tmem_wait_ld();
         if (t < nt) {
-          __nv_bfloat16 *dk = a.dK + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
           __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            st_bf16x8_global(dk + 8 * ch, kv + 8 * ch);
-            st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
-          }
+          for (int ch = 0; ch < 2; ++ch) st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
         }
       }
       tc::tc_fence_before();
       if (k + 1 < nch) tc::named_bar_arrive(N3_OUTFREE, NTHR);
+    }
+    // ---- segment-local gradient totals (suffix state at the segment start; OUT of the last
+    // chunk covers every accumulation)
+    if (a.tot != nullptr) {
+      float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
+      if (ok && nch > 0) {
+        for (int b = 0; b < nblk; ++b) {
+          const int g = 2 * b + mpar;
+          float bv[16], av;
+          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * b + 16 * hq, bv);
+          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * b, av);
+          tc::tmem_wait_ld();
+          if (g < NG) {
+            float *dst = rec + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) dst[i] = bv[i];
+            if (hq == 0) rec[g * GW + mrow] = av;
+          }
+        }
+      } else if (nch == 0) {
+        for (int i = threadIdx.x; i < (int)E; i += NEPI_T) rec[i] = 0.f;
+      }
+    }
+    if (!ok && lane == 0) atomicExch(a.err, 1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == NEPI) {
+    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// Suffix fix-up of the backward.  The reverse walk runs each segment with a
+// zero suffix state at its end (segment-local gradient states); the true
+// suffix of a segment, gA_in / gB_in (later segments + the carried-in state,
+// from the reverse chunk_scan of the walks' totals), enters the gradients
+// linearly:
+//   dpk_t[s] += gA_in[s] + V_t . gB_in[s]   (d proj_K: softmax backward of it, plus
+//                                            the walk's local d proj_K, fp32)
+//   dV_t     += sum_s pk_t[s] gB_in[s]
+// then dK = d proj_K planes, dQ = d proj_Q planes (planes and d proj_K as
+// bf16 hi + lo pairs).  No chunk depends on
+// another, so one CTA per (stream, segment) loops over its chunks with the
+// segment's gB_in held in shared memory (bf16, the MMA operand for both
+// products).
+//   control: [KV] proj = K (planes_hi + planes_lo) -> [PROJ] ; Dfix = V gB_in^T -> [DPK] ;
+//            {OUTFREE} dQ = dprojQ planes ; {PK} dV = Pk gB_in ; {DP} dK = dproj planes -> [OUT]
+//   epilogue: [PROJ] Pk {PK} ; [DPK] dproj = softmax bwd of (Dfix + gA_in) {DP} ;
+//             [OUT] dK += , dV += , dQ = {OUTFREE}
+enum { VF_KV = 0, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_FINAL, VF_COUNT };
+enum { NF_INIT = 1, NF_PK, NF_DP, NF_OUTFREE };
+
+struct FixSmem {
+  uint32_t k, v, dq, pk, gb, dp, dplo, planes, plo, ga, bars, total;
+};
+
+__host__ __device__ __forceinline__ FixSmem fix_smem_plan(int LP, int S) {
+  FixSmem m;
+  uint32_t o = 0;
+  m.k = o; o += TILE;
+  m.v = o; o += TILE;
+  m.dq = o; o += TILE;
+  m.pk = o; o += (uint32_t)(S / 64) * TILE;  // [128 t x S] K-major, 64-column blocks
+  m.gb = o; o += (uint32_t)S * 128;          // [S rows x 64 d] bf16
+  m.dp = o; o += TILE;                       // d proj_K = hi + lo, bf16 tiles
+  m.dplo = o; o += TILE;
+  m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.plo = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.ga = o; o += (uint32_t)align_up((size_t)S * 4, 128);
+  m.bars = o; o += 256;
+  m.total = o + 1024;
+  return m;
+}
+
+// TMEM: projK [0,64) ; Dfix [64, 64+S) ; dQ, dK, dV 64 columns each after it
+constexpr uint32_t FX_PJ = 0, FX_D = 64;
+
+__global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                          const __grid_constant__ CUtensorMap tmV,
+                                                          const __grid_constant__ CUtensorMap tmDQ, BwdArgs a) {
+  extern __shared__ __align__(1024) unsigned char smraw[];
+  unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  const FixSmem P = fix_smem_plan(a.LP, a.S);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int c_begin = seg * a.seg_chunks;
+  const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
+  const int S = a.S, LP = a.LP;
+  const size_t E = (size_t)S + (size_t)S * HD;
+  const uint32_t T_DQ = FX_D + S, T_DK = T_DQ + 64, T_DV = T_DK + 64;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < VF_COUNT; ++i) tc::mbar_init(&bars[i], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  volatile int *abort = &s_abort;
+
+  if (warp == NEPI) {
+    // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
+    const bool leader = lane == 0;
+    const uint32_t id_proj = tc::idesc_bf16(C, LP, false, false);
+    const uint32_t id_vg = tc::idesc_bf16(C, S, false, false);
+    const uint32_t id_d = tc::idesc_bf16(C, HD, false, true);
+    const uint32_t ok_ = P.k, ov = P.v, oq = P.dq;
+    auto load = [=, &tmK, &tmV, &tmDQ](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[VF_KV], 3 * TILE);
+      tc::tma_load_3d(sm + ok_, &tmK, &bars[VF_KV], 0, t0, n);
+      tc::tma_load_3d(sm + ov, &tmV, &bars[VF_KV], 0, t0, n);
+      tc::tma_load_3d(sm + oq, &tmDQ, &bars[VF_KV], 0, t0, n);
+    };
+    // proj = K planes and Dfix = V gB_in^T for the chunk in the tiles
+    auto issue_front = [=]() {
+#pragma unroll
+      for (int part = 0; part < 2; ++part)
+#pragma unroll
+        for (int k0 = 0; k0 < HD; k0 += 16)
+          tc::mma_bf16(tmem + FX_PJ, tc::desc_kmajor(sbase + P.k, k0, 0),
+                       tc::desc_kmajor(sbase + (part ? P.plo : P.planes), k0, 0), id_proj, part > 0 || k0 > 0);
+      tc::mma_commit(&bars[VF_PROJ]);
+#pragma unroll
+      for (int k0 = 0; k0 < HD; k0 += 16)
+        tc::mma_bf16(tmem + FX_D, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gb, k0, 0), id_vg,
+                     k0 > 0);
+      tc::mma_commit(&bars[VF_DPK]);
+    };
+    // D = A (planes_hi + planes_lo) [+ A_lo planes_hi]
+    auto issue_planes = [=](uint32_t d_col, uint32_t a_tile, uint32_t a_lo) {
+      for (int part = 0; part < 3; ++part) {
+        if (part == 2 && a_lo == 0) break;
+        for (int k0 = 0; k0 < LP; k0 += 16)
+          tc::mma_bf16(tmem + d_col, tc::desc_kmajor(sbase + (part == 2 ? a_lo : a_tile), k0, 0),
+                       tc::desc_mnmajor(sbase + (part == 1 ? P.plo : P.planes), k0, 0), id_d, part > 0 || k0 > 0);
+      }
+    };
+    bool ok = true;
+    if (leader && nch > 0) load(0);
+    tc::named_bar_sync(NF_INIT, NTHR);  // planes, gB_in, gA_in in shared memory
+    if (leader && nch > 0) {
+      ok = tc::mbar_wait(&bars[VF_KV], 0, abort);
+      if (ok) {
+        tc::tc_fence_after();
+        issue_front();
+      }
+    }
+    for (int c = 0; c < nch; ++c) {
+      if (c > 0) tc::named_bar_sync(NF_OUTFREE, NTHR);  // dQ, dK, dV of the previous chunk are out
+      ok = ok && !*abort;
+      if (leader && ok) {
+        tc::tc_fence_after();
+        issue_planes(T_DQ, P.dq, 0);
+        tc::mma_commit(&bars[VF_TFREE]);  // every reader of the K, V, dprojQ tiles issued
+      }
+      tc::named_bar_sync(NF_PK, NTHR);
+      ok = ok && !*abort;
+      if (leader && ok) {
+        ok = tc::mbar_wait(&bars[VF_TFREE], c & 1, abort);
+        if (ok && c + 1 < nch) load(c + 1);
+        tc::tc_fence_after();
+        for (int k0 = 0; k0 < S; k0 += 16)
+          tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, TILE), tc::desc_mnmajor(sbase + P.gb, k0, 0),
+                       id_d, k0 > 0);
+      }
+      tc::named_bar_sync(NF_DP, NTHR);
+      ok = ok && !*abort;
+      if (leader && ok) {
+        tc::tc_fence_after();
+        issue_planes(T_DK, P.dp, P.dplo);
+        tc::mma_commit(&bars[VF_OUT]);
+        if (c + 1 < nch) {
+          ok = tc::mbar_wait(&bars[VF_KV], (c + 1) & 1, abort);
+          if (ok) {
+            tc::tc_fence_after();
+            issue_front();
+          }
+        }
+      }
+    }
+    if (leader && nch > 0) {
+      tc::mma_commit(&bars[VF_FINAL]);
+      if (!tc::mbar_wait_drain(&bars[VF_FINAL], 0)) atomicExch(a.err, 2);
+    }
+    __syncwarp();
+  } else {
+    // ============================== epilogue warps: row t, column quarter hq
+    // (quarter hq owns the tables [tq*hq, tq*hq + tq), tq = L/4: buckets [16 tq hq, +16 tq))
+    const int q4 = warp & 3, hq = warp >> 2;
+    const int t = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int tq = a.L / 4;
+    const float *sin = a.suf_state + ((size_t)n * a.nseg + seg) * E;
+    float *sGA = reinterpret_cast<float *>(sm + P.ga);
+    for (int i = threadIdx.x; i < LP * HD; i += NEPI_T) {  // planes = hi + lo, both bf16
+      const int j = i / HD, d = i % HD;
+      const float pv = a.planes[(size_t)d * LP + j];
+      const __nv_bfloat16 hi = __float2bfloat16(pv);
+      const uint32_t off = tc::sw128_off(j, d >> 3) + (d & 7) * 2;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + off) = hi;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.plo + off) = __float2bfloat16(pv - __bfloat162float(hi));
+    }
+    for (int i = threadIdx.x; i < S * 8; i += NEPI_T) {  // gB_in (bf16 rows s), 8 values per step
+      const int sr = i >> 3, ch = i & 7;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = sin[S + (size_t)sr * HD + ch * 8 + e];
+      tc::st_row_chunk(sbase + P.gb, sr, ch, v);
+    }
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sGA[s] = sin[s];
+    tc::fence_async_smem();
+    tc::named_bar_sync(NF_INIT, NTHR);
+
+    bool ok = true;
+    for (int c = 0; c < nch; ++c) {
+      const int tok0 = (c_begin + c) * C;
+      const int nt = min(C, a.T - tok0);
+      float thK[16], qK[16];  // tanh and plane sigmoids of this quarter's tables (up to 4)
+      // ---- Pk of this quarter's buckets
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_PROJ], c & 1, abort));
+      tc::tc_fence_after();
+      if (ok) {
+        if (tq == 4) {
+          float pj[16];
+          tc::tmem_ld16(tmem + lane_off + FX_PJ + 16 * hq, pj);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) thK[i] = tanh_fast(pj[i]);
+        } else {
+          float pj[8];
+          tc::tmem_ld8(tmem + lane_off + FX_PJ + 8 * hq, pj);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) thK[i] = tanh_fast(pj[i]);
+#pragma unroll
+          for (int i = 8; i < 16; ++i) thK[i] = 0.f;
+        }
+#pragma unroll
+        for (int tb = 0; tb < 4; ++tb) {
+          if (tb < tq) {
+            plane_sigmoids(thK + 4 * tb, a.scale, a.poly, qK + 4 * tb);
+            float pr[16];
+            corner_probs(qK + 4 * tb, pr);
+            if (t >= nt) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) pr[i] = 0.f;
+            }
+            const int b0 = 16 * (tq * hq + tb);  // first bucket of the table
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+              tc::st_row_chunk(sbase + P.pk + (uint32_t)(b0 >> 6) * TILE, t, ((b0 & 63) >> 3) + ch, pr + 8 * ch);
+          }
+        }
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NF_PK, NTHR);
+      // ---- dproj_fix = softmax bwd of (V gB_in^T + gA_in) + the walk's segment-local d proj_K
+      const bool live = t < nt;
+      const size_t row = ((size_t)n * a.T + tok0 + (live ? t : 0)) * HD;
+      float4 loc[4];  // issued before the wait: the loads are in flight meanwhile
+#pragma unroll
+      for (int tb = 0; tb < 4; ++tb)
+        loc[tb] = tb < tq && live ? *reinterpret_cast<const float4 *>(a.dprojK + row + 4 * (tq * hq + tb))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_DPK], c & 1, abort));
+      tc::tc_fence_after();
+      if (ok) {
+#pragma unroll
+        for (int tb = 0; tb < 4; ++tb) {
+          if (tb < tq) {
+            const int b0 = 16 * (tq * hq + tb);
+            float g16[16], p16[16], dp[4];
+            tc::tmem_ld16(tmem + lane_off + FX_D + b0, g16);
+            tc::tmem_wait_ld();
+            add_shared_row<16>(sbase + P.ga + 4 * b0, g16);
+            corner_probs(qK + 4 * tb, p16);
+            table_probs_bwd(p16, g16, thK + 4 * tb, a.scale, dp);
+            const int j = 4 * (tq * hq + tb);  // first projection column of the table
+            // then hi + lo bf16 for the dK MMA
+            dp[0] += loc[tb].x;
+            dp[1] += loc[tb].y;
+            dp[2] += loc[tb].z;
+            dp[3] += loc[tb].w;
+            float lo[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) lo[i] = dp[i] - __bfloat162float(__float2bfloat16(dp[i]));
+            tc::st_row_half(sbase + P.dp, t, j >> 3, (j >> 2) & 1, dp);
+            tc::st_row_half(sbase + P.dplo, t, j >> 3, (j >> 2) & 1, lo);
+          }
+        }
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(NF_DP, NTHR);
+      // ---- dK, dV += dV_fix, dQ (row t, d in [16hq, 16hq+16))
+      uint4 dvl[2];  // the walk's dV rows, loaded before the wait
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch)
+        dvl[ch] = live ? *reinterpret_cast<const uint4 *>(a.dV + row + 16 * hq + 8 * ch) : make_uint4(0, 0, 0, 0);
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_OUT], c & 1, abort));
+      tc::tc_fence_after();
+      if (ok) {
+        float vq[16], vk[16], vv[16];
+        tc::tmem_ld16(tmem + lane_off + T_DQ + 16 * hq, vq);
+        tc::tmem_ld16(tmem + lane_off + T_DK + 16 * hq, vk);
+        tc::tmem_ld16(tmem + lane_off + T_DV + 16 * hq, vv);
+        tc::tmem_wait_ld();
+        if (live) {
+          const size_t orow = row + 16 * hq;
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            const uint4 v4 = dvl[ch];
+            const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              vv[8 * ch + 2 * e] += __uint_as_float(vw[e] << 16);
+              vv[8 * ch + 2 * e + 1] += __uint_as_float(vw[e] & 0xFFFF0000u);
+            }
+            st_bf16x8_global(a.dK + orow + 8 * ch, vk + 8 * ch);
+            st_bf16x8_global(a.dV + orow + 8 * ch, vv + 8 * ch);
+            if (a.dQ != nullptr) st_bf16x8_global(a.dQ + orow + 8 * ch, vq + 8 * ch);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      if (c + 1 < nch) tc::named_bar_arrive(NF_OUTFREE, NTHR);
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }

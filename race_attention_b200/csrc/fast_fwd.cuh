@@ -53,6 +53,9 @@ struct FwdArgs {
   const float *seg_state;  // [N, nseg, S + S*64]  (A part, then B part) exclusive segment prefixes
   float *seg_tot;          // totals kernel output, same layout
   __nv_bfloat16 *out;      // [N, T, 64]
+  float *chunkA;           // states pass of the totals kernel, or a forward that saves them for the
+  __nv_bfloat16 *chunkB;   // backward: [N, nchunks, S] A + eps and [N, nchunks, S, 64] bf16 B at each
+                           // chunk start (nullptr: not wanted)
   int *err;
 };
 
@@ -361,6 +364,20 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
     const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
     float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
+    // chunk-start state for the backward (when saving): B of group gr at chunk cc, this
+    // thread's bucket row and d in [16hq, 16hq+16), bf16
+    auto save_b = [=](int cc, int gr, const float *v16) {
+      __nv_bfloat16 *dst = a.chunkB + (((size_t)n * a.nchunks + cc) * S + gr * GB + t) * HD + 16 * hq;
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        uint4 w4;
+        w4.x = tc::pack_bf16(v16[8 * ch + 0], v16[8 * ch + 1]);
+        w4.y = tc::pack_bf16(v16[8 * ch + 2], v16[8 * ch + 3]);
+        w4.z = tc::pack_bf16(v16[8 * ch + 4], v16[8 * ch + 5]);
+        w4.w = tc::pack_bf16(v16[8 * ch + 6], v16[8 * ch + 7]);
+        reinterpret_cast<uint4 *>(dst)[ch] = w4;
+      }
+    };
     // ---- prologue: planes (bf16, K-major rows j), tril, A_start, Bstate
     for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
       const int j = i / HD, d = i % HD;
@@ -386,6 +403,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       tc::tmem_st16(tmem + lane_off + T_B + 64 * g + 16 * hq, v);
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 2 * hq + ch, v + 8 * ch);
+      if (a.chunkB != nullptr && nch > 0) save_b(c_begin, g, v);
     }
     tc::tmem_wait_st();
     tc::fence_async_smem();
@@ -394,12 +412,14 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
 
     // bf16 copy of Bstate_gr (lane t = bucket t), d in [16hq, 16hq+16), for the
     // next chunk's W x Bstate
-    auto refresh = [=](int gr) {
+    // (cc: the chunk this is the start state of; saved for the backward when asked)
+    auto refresh = [=](int gr, int cc) {
       float bv[16];
       tc::tmem_ld16(tmem + lane_off + T_B + 64 * gr + 16 * hq, bv);
       tc::tmem_wait_ld();
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + gr * TILE, t, 2 * hq + ch, bv + 8 * ch);
+      if (a.chunkB != nullptr && cc < nch) save_b(c_begin + cc, gr, bv);
       tc::fence_async_smem();
       tc::tc_fence_before();
     };
@@ -411,6 +431,10 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       const uint32_t aCur = sbase + ((c & 1) ? P.a1 : P.a0), aNxt = sbase + ((c & 1) ? P.a0 : P.a1);
       // the row-127 threads wrote this chunk's A during the previous one
       tc::named_bar_sync(NB_ESYNC, NEPI_T);
+      if (a.chunkA != nullptr) {  // A + eps at chunk start, for the backward
+        const float *ac = reinterpret_cast<const float *>(sm + ((c & 1) ? P.a1 : P.a0));
+        for (int s = threadIdx.x; s < S; s += NEPI_T) a.chunkA[((size_t)n * a.nchunks + c_begin + c) * S + s] = ac[s];
+      }
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[B_PROJ], c & 1, abort));
       tc::tc_fence_after();
       for (int g = 0; g < NG; ++g) {
@@ -463,7 +487,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         tc::named_bar_arrive(NB_W, NTHR);
         // ---- previous group's state refresh while Smat runs (with one group per
         // chunk the refresh follows Smask instead: the next Bupd is this group's)
-        if (ok && NG > 1 && u > 0) refresh(g > 0 ? g - 1 : NG - 1);
+        if (ok && NG > 1 && u > 0) refresh(g > 0 ? g - 1 : NG - 1, g > 0 ? c + 1 : c);
         // ---- Smask = tril(Smat), columns tau in [32hq, 32hq+32)
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[B_SMAT], u & 1, abort));
         tc::tc_fence_after();
@@ -488,7 +512,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::named_bar_arrive(NB_SMASK, NTHR);
-        if (ok && NG == 1) refresh(0);
+        if (ok && NG == 1) refresh(0, c + 1);
       }
       // ---- out rows, d in [16hq, 16hq+16), after the chunk's last Smask V
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[B_GDONE], (c * NG + NG - 1) & 1, abort));
@@ -527,6 +551,10 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
 // Segment totals: A_tot[s] = sum_t pk[t,s], B_tot[s,:] = sum_t pk[t,s] V[t,:]
 // over one (stream, segment), written as a record of the chunk_scan layout.
 // Same warp roles; A_tot comes from an MMA against a ones column.
+// States pass (a.chunkA != nullptr): the same walk started from the segment's
+// exclusive prefix (a.seg_state) stores the state at every chunk start --
+// A + eps in fp32 and B in bf16, the operands of the backward's reverse walk --
+// and writes no record.
 struct TotSmem {
   uint32_t k, v, pk, ones, planes, bars, total;  // k, v: 2 stages of TILE bytes each
 };
@@ -564,6 +592,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
   const int S = a.S;
   const size_t E = (size_t)S + (size_t)S * HD;
   float *rec = a.seg_tot + ((size_t)n * a.nseg + seg) * E;
+  const bool states = a.chunkA != nullptr;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -613,9 +642,9 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           for (int k0 = 0; k0 < C; k0 += 16) {
             const uint64_t ap = tc::desc_mnmajor(pk, k0, TILE);
             tc::mma_bf16(tmem + 64 + 64 * g, ap, tc::desc_mnmajor(sbase + P.v + st * TILE, k0, TILE), id_bupd,
-                         c > 0 || k0 > 0);
+                         states || c > 0 || k0 > 0);
             tc::mma_bf16(tmem + 192 + 16 * g, ap, tc::desc_mnmajor(sbase + P.ones, k0, TILE), id_ones,
-                         c > 0 || k0 > 0);
+                         states || c > 0 || k0 > 0);
           }
         }
         tc::mma_commit(&bars[TB_DONE]);
@@ -648,7 +677,20 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
         tc::st_row_chunk(sbase + P.ones, t, ch, v);
       }
     }
+    if (states) {  // segment-start state into the accumulators (lane t = bucket t of group g)
+      const float *st0 = a.seg_state + ((size_t)n * a.nseg + seg) * E;
+      for (int g = 0; g < a.ngroups; ++g) {
+        float v[16];
+        const float *src = st0 + S + (size_t)(g * GB + t) * HD + 16 * hq;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = src[i];
+        tc::tmem_st16(tmem + lane_off + 64 + 64 * g + 16 * hq, v);
+        if (hq == 0) tc::tmem_st1(tmem + lane_off + 192 + 16 * g, st0[g * GB + t]);
+      }
+      tc::tmem_wait_st();
+    }
     tc::fence_async_smem();
+    tc::tc_fence_before();
     tc::warp_arrive(&bars[TB_INIT]);
     bool ok = true;
     for (int c = 0; c < nch && ok; ++c) {
@@ -658,6 +700,26 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
+      if (states) {  // the accumulators hold this chunk's start state until its MMAs are issued
+        const int cg = c_begin + c;
+        for (int g = 0; g < a.ngroups; ++g) {
+          float bv[16], av;
+          tc::tmem_ld16(tmem + lane_off + 64 + 64 * g + 16 * hq, bv);
+          tc::tmem_ld1(tmem + lane_off + 192 + 16 * g, av);
+          tc::tmem_wait_ld();
+          const size_t row = ((size_t)n * a.nchunks + cg) * S + g * GB + t;
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch) {
+            uint4 w4;
+            w4.x = tc::pack_bf16(bv[8 * ch + 0], bv[8 * ch + 1]);
+            w4.y = tc::pack_bf16(bv[8 * ch + 2], bv[8 * ch + 3]);
+            w4.z = tc::pack_bf16(bv[8 * ch + 4], bv[8 * ch + 5]);
+            w4.w = tc::pack_bf16(bv[8 * ch + 6], bv[8 * ch + 7]);
+            *reinterpret_cast<uint4 *>(a.chunkB + row * HD + 16 * hq + 8 * ch) = w4;
+          }
+          if (hq == 0) a.chunkA[row] = av + a.eps;
+        }
+      }
       for (int g = 0; g < a.ngroups; ++g) {
         const int j0 = (g * 8 + hq * 2) * 4;
         float pj[8], pr[32];
@@ -681,7 +743,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     if (ok && nch > 0) ok = tc::warp_wait(&bars[TB_DONE], (nch - 1) & 1, abort);
     __syncwarp();
     tc::tc_fence_after();
-    if (ok) {
+    if (ok && !states) {
       for (int g = 0; g < a.ngroups; ++g) {
         float bv[16], av;
         tc::tmem_ld16(tmem + lane_off + 64 + 64 * g + 16 * hq, bv);
@@ -693,7 +755,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
         if (hq == 0) rec[g * GB + t] = av;
       }
     }
-    if (nch == 0) {  // empty segment: zero record
+    if (nch == 0 && !states) {  // empty segment: zero record
       for (int i = threadIdx.x; i < (int)E; i += NEPI_T) rec[i] = 0.f;
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);

@@ -113,10 +113,11 @@ inline bool make_map(CUtensorMap *m, const void *base, int64_t N, int64_t T) {
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Backward workspace: status | forward segment records | backward segment
-// records | per-chunk start state (A fp32, B bf16) written by the forward walk.
+// records | per-chunk start state (A + eps fp32, B bf16) | d proj_Q [N, T, 64] bf16
+// and segment-local d proj_K [N, T, 64] fp32 (reverse walk -> fix-up).
 struct BwdPlan {
   Plan p;
-  size_t fwd_rec, bwd_rec, chunkA, chunkB, total;
+  size_t fwd_rec, bwd_rec, chunkA, chunkB, dprojQ, dprojK, total;
 };
 
 inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms) {
@@ -128,11 +129,28 @@ inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms) {
   b.bwd_rec = b.fwd_rec + rec;
   b.chunkA = b.bwd_rec + rec;
   b.chunkB = b.chunkA + align_up(sizeof(float) * (size_t)N * b.p.nchunks * S, 256);
-  b.total = b.chunkB + align_up(sizeof(uint16_t) * (size_t)N * b.p.nchunks * S * fk::HD, 256);
+  b.dprojQ = b.chunkB + align_up(sizeof(uint16_t) * (size_t)N * b.p.nchunks * S * fk::HD, 256);
+  b.dprojK = b.dprojQ + align_up(sizeof(uint16_t) * (size_t)N * T * fk::HD, 256);
+  b.total = b.dprojK + align_up(sizeof(float) * (size_t)N * T * fk::HD, 256);
   return b;
 }
 
 inline size_t bwd_workspace_bytes(int64_t N, int64_t T, int64_t S) { return bwd_plan(N, T, S, 256).total; }
+
+// What a saving forward keeps for the backward: A + eps [N, nchunks, S] fp32 and
+// B [N, nchunks, S, 64] bf16 at every 128-token chunk start (independent of the segment plan).
+struct SavedPlan {
+  size_t chunkA, chunkB, total;
+};
+
+inline SavedPlan saved_plan(int64_t N, int64_t T, int64_t S) {
+  SavedPlan v;
+  const int64_t nchunks = (T + fk::C - 1) / fk::C;
+  v.chunkA = 0;
+  v.chunkB = align_up(sizeof(float) * (size_t)N * nchunks * S, 256);
+  v.total = v.chunkB + align_up(sizeof(uint16_t) * (size_t)N * nchunks * S * fk::HD, 256);
+  return v;
+}
 
 // 2-D map over the per-chunk B states viewed as [rows][64] bf16, box [64 x 64].
 inline bool make_rows_map(CUtensorMap *m, const void *base, int64_t rows) {

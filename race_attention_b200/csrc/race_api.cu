@@ -392,6 +392,8 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
   a.seg_state = at<float>(ws, pl.rec_off);
   a.seg_tot = at<float>(ws, pl.rec_off);
   a.out = nullptr;
+  a.chunkA = nullptr;
+  a.chunkB = nullptr;
   a.err = at<int>(ws, pl.status_off);
   return RACE_OK;
 }
@@ -430,13 +432,18 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
 
 int fast_forward(const void *Q, const void *K, const void *V, const float *planes_T, void *out, const float *A0,
                  const float *B0, float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale,
-                 void *ws, cudaStream_t s) {
+                 void *ws, cudaStream_t s, void *saved = nullptr) {
   fk::FwdArgs a;
   CUtensorMap mQ, mK, mV;
   RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV));
   if (!fh::make_map(&mQ, Q, N, T))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(Q) failed: CUresult %d", fh::last_encode_status());
   a.out = static_cast<__nv_bfloat16 *>(out);
+  if (saved != nullptr) {
+    const fh::SavedPlan sp = fh::saved_plan(N, T, 16 * L);
+    a.chunkA = at<float>(saved, sp.chunkA);
+    a.chunkB = at<__nv_bfloat16>(saved, sp.chunkB);
+  }
   const fk::FwdSmem fs = fk::fwd_smem_plan(a.ngroups, a.LP);
   RACE_TRY(set_smem(fk::fwd_readout_kernel, fs.total));
   KernelScope ks(RACE_KT_FWD_READOUT, s);
@@ -448,16 +455,30 @@ int fast_forward(const void *Q, const void *K, const void *V, const float *plane
 int fast_backward(const void *Q, const void *K, const void *V, const void *dO, const float *planes_T, void *dQ,
                   void *dK, void *dV, const float *A0, const float *B0, const float *gA, const float *gB, float *dA0,
                   float *dB0, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws, cudaStream_t s,
-                  bool totals_only) {
+                  bool totals_only, const void *saved = nullptr) {
   const int64_t S = 16 * L;
   const fh::BwdPlan bp = fh::bwd_plan(N, T, S, fh::sm_count());
   fk::FwdArgs fa;
-  CUtensorMap mQ, mK, mV, mO, mB;
-  // forward segment prefixes (exclusive, seeded with the carried-in state)
-  RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, nullptr, nullptr, N, T, L, eps, scale, ws, s, fa, mK, mV,
-                                bp.fwd_rec));
+  CUtensorMap mQ, mK, mV, mO, mB, mP;
+  // chunk-start states: saved by the forward, or recomputed below
+  const fh::SavedPlan sp = fh::saved_plan(N, T, S);
+  float *chunkA = saved ? at<float>(const_cast<void *>(saved), sp.chunkA) : at<float>(ws, bp.chunkA);
+  __nv_bfloat16 *chunkB =
+      saved ? at<__nv_bfloat16>(const_cast<void *>(saved), sp.chunkB) : at<__nv_bfloat16>(ws, bp.chunkB);
+  if (saved == nullptr) {
+    // forward segment prefixes (exclusive, seeded with the carried-in state)
+    RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, nullptr, nullptr, N, T, L, eps, scale, ws, s, fa, mK, mV,
+                                  bp.fwd_rec));
+  } else {
+    if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
+    if (!fh::make_map(&mK, K, N, T) || !fh::make_map(&mV, V, N, T))
+      return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(K/V) failed: CUresult %d", fh::last_encode_status());
+    cudaError_t e = cudaMemsetAsync(at<int>(ws, 0), 0, sizeof(int), s);
+    if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  }
   if (!fh::make_map(&mQ, Q, N, T) || !fh::make_map(&mO, dO, N, T) ||
-      !fh::make_rows_map(&mB, at<void>(ws, bp.chunkB), N * (int64_t)bp.p.nchunks * S))
+      !fh::make_map(&mP, at<void>(ws, bp.dprojQ), N, T) ||
+      !fh::make_rows_map(&mB, chunkB, N * (int64_t)bp.p.nchunks * S))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed in the backward: CUresult %d",
                 fh::last_encode_status());
   fk::BwdArgs b;
@@ -477,37 +498,72 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   b.planes = planes_T;
   b.fwd_state = at<float>(ws, bp.fwd_rec);
   b.tot = at<float>(ws, bp.bwd_rec);
-  b.suf_state = at<float>(ws, bp.bwd_rec);
-  b.chunkA = at<float>(ws, bp.chunkA);
-  b.chunkB = at<__nv_bfloat16>(ws, bp.chunkB);
-  b.dQ = totals_only ? nullptr : static_cast<__nv_bfloat16 *>(dQ);
+  b.suf_state = nullptr;
+  b.chunkA = chunkA;
+  b.chunkB = chunkB;
+  b.dQ = nullptr;
   b.dK = static_cast<__nv_bfloat16 *>(dK);
   b.dV = static_cast<__nv_bfloat16 *>(dV);
+  b.dprojQ = at<__nv_bfloat16>(ws, bp.dprojQ);
+  b.dprojK = at<float>(ws, bp.dprojK);
   b.err = at<int>(ws, 0);
-  const fk::BwdSmem bs = fk::bwd_smem_plan(b.LP, b.S);
   const unsigned grid = (unsigned)(N * bp.p.nseg);
-  RACE_TRY(set_smem(fk::bwd_fwd_kernel, bs.total));
-  {
-    KernelScope ks(RACE_KT_BWD_FWD, s);
-    fk::bwd_fwd_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, b);
-    ks.stop();
-  }
-  RACE_TRY(check_launch("fast bwd_fwd"));
   gen::Dims p = make_dims(N, T, S, fk::HD, eps);
   p.G = bp.p.nseg;
+  if (totals_only) {
+    // gradient totals only (sequence-sharded phase A): the forward walk
+    const fk::BwdSmem bs = fk::bwd_smem_plan(b.LP, b.S);
+    RACE_TRY(set_smem(fk::bwd_fwd_kernel, bs.total));
+    {
+      KernelScope ks(RACE_KT_BWD_FWD, s);
+      fk::bwd_fwd_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, b);
+      ks.stop();
+    }
+    RACE_TRY(check_launch("fast bwd_fwd"));
+    KernelScope ks(RACE_KT_SCAN, s);
+    const int rc = launch_scan(at<float>(ws, bp.bwd_rec), nullptr, nullptr, dA0, dB0, p, 1, s);
+    ks.stop();
+    return rc;
+  }
+  // 1. chunk-start forward states (A + eps, bf16 B) from the segment prefixes, unless saved
+  if (saved == nullptr) {
+    fa.chunkA = b.chunkA;
+    fa.chunkB = b.chunkB;
+    fa.seg_state = b.fwd_state;
+    {
+      const fk::TotSmem ts = fk::tot_smem_plan(fa.ngroups, fa.LP);
+      KernelScope ks(RACE_KT_FWD_TOTALS, s);
+      fk::fwd_totals_kernel<<<grid, fk::NTHR, ts.total, s>>>(mK, mV, fa);
+      ks.stop();
+    }
+    RACE_TRY(check_launch("fast chunk states"));
+  }
+  // 2. segment-local reverse walk: dV and d proj_K without the later segments' suffix, d proj_Q,
+  //    local totals
+  const fk::BwdSmem rs = fk::bwd_smem_plan(b.LP, b.S, true);
+  RACE_TRY(set_smem(fk::bwd_rev_kernel, rs.total));
+  {
+    KernelScope ks(RACE_KT_BWD_REV, s);
+    fk::bwd_rev_kernel<<<grid, fk::NTHR, rs.total, s>>>(mQ, mK, mV, mO, mB, b);
+    ks.stop();
+  }
+  RACE_TRY(check_launch("fast bwd_rev"));
+  // 3. suffix over segments (seeded with the carried-in gradient state); its totals are dA0, dB0
   {
     KernelScope ks(RACE_KT_SCAN, s);
-    const int rc = launch_scan(at<float>(ws, bp.bwd_rec), totals_only ? nullptr : gA, totals_only ? nullptr : gB,
-                               dA0, dB0, p, 1, s);
+    const int rc = launch_scan(at<float>(ws, bp.bwd_rec), gA, gB, dA0, dB0, p, 1, s);
     ks.stop();
     RACE_TRY(rc);
   }
-  if (totals_only) return RACE_OK;
-  RACE_TRY(set_smem(fk::bwd_rev_kernel, bs.total));
-  KernelScope ks(RACE_KT_BWD_REV, s);
-  fk::bwd_rev_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, mB, b);
+  // 4. fix-up: the suffix's linear contribution to dV and d proj_K; dK, dQ from d proj_K, d proj_Q
+  b.suf_state = at<float>(ws, bp.bwd_rec);
+  b.dQ = static_cast<__nv_bfloat16 *>(dQ);
+  const fk::FixSmem xs = fk::fix_smem_plan(b.LP, b.S);
+  RACE_TRY(set_smem(fk::bwd_fix_kernel, xs.total));
+  KernelScope ks(RACE_KT_BWD_FIX, s);
+  fk::bwd_fix_kernel<<<grid, fk::NTHR, xs.total, s>>>(mK, mV, mP, b);
   ks.stop();
-  return check_launch("fast bwd_rev");
+  return check_launch("fast bwd_fix");
 }
 
 int check_fast_ptrs(std::initializer_list<const void *> ptrs) {
@@ -706,10 +762,10 @@ int race_soft_hash_bwd(const void *X, int dtype, const float *planes_T, const fl
   return ok();
 }
 
-int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
-                 const float *A0, const float *B0, float *A_final, float *B_final, int64_t N, int64_t T, int64_t D,
-                 int64_t L, int64_t P, float eps, float logit_scale, void *workspace, size_t workspace_bytes,
-                 void *stream) {
+static int fwd_qkv_impl(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
+                        const float *A0, const float *B0, float *A_final, float *B_final, void *saved,
+                        size_t saved_bytes, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
+                        float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
   RACE_NONNULL(Q);
   RACE_NONNULL(K);
   RACE_NONNULL(V);
@@ -723,7 +779,14 @@ int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype, const f
   if (fh::eligible(dtype, D, L, P)) {
     RACE_TRY(check_ws(workspace, workspace_bytes, fh::fwd_workspace_bytes(N, T, S)));
     RACE_TRY(check_fast_ptrs({Q, K, V, out}));
-    RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, A_final, B_final, N, T, L, eps, logit_scale, workspace, s));
+    if (saved != nullptr) {
+      if (saved_bytes < fh::saved_plan(N, T, S).total)
+        return fail(RACE_ERR_WORKSPACE, "saved-state buffer too small: %zu < %zu bytes", saved_bytes,
+                    fh::saved_plan(N, T, S).total);
+      if (!fh::aligned16(saved)) return fail(RACE_ERR_ALIGN, "saved-state buffer must be 16-byte aligned");
+    }
+    RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, A_final, B_final, N, T, L, eps, logit_scale, workspace, s,
+                          saved));
     return ok();
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total));
@@ -737,10 +800,11 @@ int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype, const f
   return ok();
 }
 
-int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
-                 void *dQ, void *dK, void *dV, const float *A0, const float *B0, const float *gA_in,
-                 const float *gB_in, float *dA0, float *dB0, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
-                 float eps, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+static int bwd_qkv_impl(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                        const float *planes_T, const void *saved, size_t saved_bytes, void *dQ, void *dK, void *dV,
+                        const float *A0, const float *B0, const float *gA_in, const float *gB_in, float *dA0,
+                        float *dB0, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
+                        float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
   RACE_NONNULL(Q);
   RACE_NONNULL(K);
   RACE_NONNULL(V);
@@ -757,8 +821,14 @@ int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, in
   if (fh::eligible(dtype, D, L, P)) {
     RACE_TRY(check_ws(workspace, workspace_bytes, fh::bwd_workspace_bytes(N, T, S)));
     RACE_TRY(check_fast_ptrs({Q, K, V, dO, dQ, dK, dV}));
+    if (saved != nullptr) {
+      if (saved_bytes < fh::saved_plan(N, T, S).total)
+        return fail(RACE_ERR_WORKSPACE, "saved-state buffer too small: %zu < %zu bytes", saved_bytes,
+                    fh::saved_plan(N, T, S).total);
+      if (!fh::aligned16(saved)) return fail(RACE_ERR_ALIGN, "saved-state buffer must be 16-byte aligned");
+    }
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, L, eps,
-                           logit_scale, workspace, s, false));
+                           logit_scale, workspace, s, false, saved));
     return ok();
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
@@ -772,6 +842,50 @@ int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, in
         planes_T, (__nv_bfloat16 *)dQ, (__nv_bfloat16 *)dK, (__nv_bfloat16 *)dV, A0, B0, gA_in, gB_in, dA0, dB0, N,
         T, D, L, P, eps, logit_scale, workspace, s));
   return ok();
+}
+
+int race_fwd_qkv(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
+                 const float *A0, const float *B0, float *A_final, float *B_final, int64_t N, int64_t T, int64_t D,
+                 int64_t L, int64_t P, float eps, float logit_scale, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+  return fwd_qkv_impl(Q, K, V, dtype, planes_T, out, A0, B0, A_final, B_final, nullptr, 0, N, T, D, L, P, eps,
+                      logit_scale, workspace, workspace_bytes, stream);
+}
+
+int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                 void *dQ, void *dK, void *dV, const float *A0, const float *B0, const float *gA_in,
+                 const float *gB_in, float *dA0, float *dB0, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                 float eps, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+  return bwd_qkv_impl(Q, K, V, dO, dtype, planes_T, nullptr, 0, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, D,
+                      L, P, eps, logit_scale, workspace, workspace_bytes, stream);
+}
+
+int race_saved_bytes(int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, int dtype, size_t *bytes) {
+  RACE_NONNULL(bytes);
+  *bytes = 0;
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  if (fh::eligible(dtype, D, L, P)) *bytes = fh::saved_plan(N, T, S).total;
+  return ok();
+}
+
+int race_fwd_qkv_save(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
+                      const float *A0, const float *B0, float *A_final, float *B_final, void *saved,
+                      size_t saved_bytes, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
+                      float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+  return fwd_qkv_impl(Q, K, V, dtype, planes_T, out, A0, B0, A_final, B_final, saved_bytes ? saved : nullptr,
+                      saved_bytes, N, T, D, L, P, eps, logit_scale, workspace, workspace_bytes, stream);
+}
+
+int race_bwd_qkv_saved(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                       const void *saved, size_t saved_bytes, void *dQ, void *dK, void *dV, const float *A0,
+                       const float *B0, const float *gA_in, const float *gB_in, float *dA0, float *dB0, int64_t N,
+                       int64_t T, int64_t D, int64_t L, int64_t P, float eps, float logit_scale, void *workspace,
+                       size_t workspace_bytes, void *stream) {
+  return bwd_qkv_impl(Q, K, V, dO, dtype, planes_T, saved_bytes ? saved : nullptr, saved_bytes, dQ, dK, dV, A0, B0,
+                      gA_in, gB_in, dA0, dB0, N, T, D, L, P, eps, logit_scale, workspace, workspace_bytes, stream);
 }
 
 int race_state_from_prefill(const void *K, const void *V, int dtype, const float *planes_T, const float *A0,

@@ -48,6 +48,13 @@ def _dtype_code(t):
         raise RuntimeError(f"unsupported dtype {t.dtype} (float32 or bfloat16)") from None
 
 
+def _dtype_code_of(dtype):
+    try:
+        return _DT[dtype]
+    except KeyError:
+        raise RuntimeError(f"unsupported dtype {dtype} (float32 or bfloat16)") from None
+
+
 def _workspace(op, N, T, S, D, L, P, dtype, dev):
     lib = _lib.load()
     nbytes = ctypes.c_size_t(0)
@@ -208,27 +215,45 @@ def _qkv_common(Q, K, V, planes_T, L, P, logit_scale):
     return dev, Q, K, V, planes_T, N, T, D, L << P, scale
 
 
-def fwd_qkv(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None, return_state=False):
-    """Fused soft hash + causal scan + readout; out has Q's dtype and [N,T,D] shape."""
+def saved_bytes(N, T, D, L, P, dtype) -> int:
+    """Size of the chunk-state buffer a saving forward keeps for the backward (0: not used)."""
+    nb = ctypes.c_size_t(0)
+    _lib.check(_lib.load().race_saved_bytes(N, T, D, L, P, _dtype_code_of(dtype), ctypes.byref(nb)),
+               "race_saved_bytes")
+    return int(nb.value)
+
+
+def fwd_qkv(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None, return_state=False,
+            save=False):
+    """Fused soft hash + causal scan + readout; out has Q's dtype and [N,T,D] shape.
+    save=True also returns the chunk-state buffer for bwd_qkv(saved=...) (None when unused)."""
     dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
     A0, B0 = _opt_state(A0, B0, N, S, D, dev)
     out = torch.empty_like(Q)
     Af = torch.empty((N, S), dtype=torch.float32, device=dev) if return_state else None
     Bf = torch.empty((N, S, D), dtype=torch.float32, device=dev) if return_state else None
     lib = _lib.load()
+    saved = None
     with torch.cuda.device(dev):
         ws, nb = _workspace(_lib.OP_FWD_QKV, N, T, S, D, L, P, _dtype_code(Q), dev)
-        _lib.check(lib.race_fwd_qkv(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out), _ptr(A0),
-                                    _ptr(B0), _ptr(Af), _ptr(Bf), N, T, D, L, P, float(eps), scale, _ptr(ws), nb,
-                                    _stream(dev)), "race_fwd_qkv")
+        sb = saved_bytes(N, T, D, L, P, Q.dtype) if save else 0
+        if sb:
+            saved = torch.empty(sb, dtype=torch.uint8, device=dev)
+        _lib.check(lib.race_fwd_qkv_save(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out),
+                                         _ptr(A0), _ptr(B0), _ptr(Af), _ptr(Bf), _ptr(saved), sb, N, T, D, L, P,
+                                         float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_fwd_qkv")
         if fast_path(Q.dtype, D, L, P):
             _check_status(ws, "race_fwd_qkv")
-    return (out, Af, Bf) if return_state else out
+    res = (out, Af, Bf) if return_state else (out,)
+    if save:
+        res = res + (saved,)
+    return res if len(res) > 1 else res[0]
 
 
 def bwd_qkv(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None, gA=None, gB=None,
-            return_state_grad=False):
-    """(dQ, dK, dV[, dA0, dB0]) of the fused layer."""
+            return_state_grad=False, saved=None):
+    """(dQ, dK, dV[, dA0, dB0]) of the fused layer.  saved: the buffer of fwd_qkv(save=True) on the
+    same inputs (skips rebuilding the forward's chunk states)."""
     dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
     dO = _as_ntd(dO, "dO").to(Q.dtype)
     A0, B0 = _opt_state(A0, B0, N, S, D, dev)
@@ -239,9 +264,11 @@ def bwd_qkv(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0
     lib = _lib.load()
     with torch.cuda.device(dev):
         ws, nb = _workspace(_lib.OP_BWD_QKV, N, T, S, D, L, P, _dtype_code(Q), dev)
-        _lib.check(lib.race_bwd_qkv(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T), _ptr(dQ),
-                                    _ptr(dK), _ptr(dV), _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), _ptr(dA0), _ptr(dB0),
-                                    N, T, D, L, P, float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_bwd_qkv")
+        sb = saved.numel() if saved is not None else 0
+        _lib.check(lib.race_bwd_qkv_saved(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T),
+                                          _ptr(saved), sb, _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(A0), _ptr(B0),
+                                          _ptr(gA), _ptr(gB), _ptr(dA0), _ptr(dB0), N, T, D, L, P, float(eps), scale,
+                                          _ptr(ws), nb, _stream(dev)), "race_bwd_qkv")
         if fast_path(Q.dtype, D, L, P):
             _check_status(ws, "race_bwd_qkv")
     return (dQ, dK, dV, dA0, dB0) if return_state_grad else (dQ, dK, dV)

@@ -67,16 +67,17 @@ class RaceQKVFn(Function):
     @staticmethod
     def forward(ctx, Q, K, V, planes_T, L, P, eps, logit_scale):
         shape = Q.shape
-        out = ops.fwd_qkv(Q, K, V, planes_T, L, P, eps, logit_scale)
-        ctx.save_for_backward(Q, K, V, planes_T)
+        # the tcgen05 path keeps its chunk-start states for the backward (None elsewhere)
+        out, saved = ops.fwd_qkv(Q, K, V, planes_T, L, P, eps, logit_scale, save=True)
+        ctx.save_for_backward(Q, K, V, planes_T, saved)
         ctx.cfg = (L, P, eps, logit_scale, shape)
         return out.view(shape)
 
     @staticmethod
     def backward(ctx, dO):
-        Q, K, V, planes_T = ctx.saved_tensors
+        Q, K, V, planes_T, saved = ctx.saved_tensors
         L, P, eps, scale, shape = ctx.cfg
-        dQ, dK, dV = ops.bwd_qkv(Q, K, V, dO, planes_T, L, P, eps, scale)
+        dQ, dK, dV = ops.bwd_qkv(Q, K, V, dO, planes_T, L, P, eps, scale, saved=saved)
         return dQ.view(shape), dK.view(shape), dV.view(shape), None, None, None, None, None
 
 

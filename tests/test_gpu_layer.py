@@ -158,10 +158,10 @@ def test_fast_forward_segments(B, H, T, L):
 @pytest.mark.parametrize("B,H,T,L", [(2, 16, 4000, 16), (4, 8, 3000, 8), (1, 2, 129, 16), (1, 3, 128, 8),
                                      (1, 2, 1, 16)])
 def test_fast_backward_segments(B, H, T, L):
-    """tcgen05 backward (two walks + reverse segment scan): multi-chunk segments,
-    partial last chunk, two and four bucket groups; grads vs the oracle and the
-    launch count proves the fused path ran (forward totals + scan, forward walk,
-    reverse scan, reverse walk)."""
+    """tcgen05 backward: multi-chunk segments, partial last chunk, two and four
+    bucket groups; grads vs the oracle, and the launch count proves the fused
+    path ran (forward totals + prefix scan, chunk states, segment-local reverse
+    walk, suffix scan, suffix fix-up)."""
     import race_attention_b200 as rb
     Q, K, V, dO = qkv(B, H, T, 64, seed=3 * T + L, scale=1.0 / 8.0, dtype=torch.bfloat16)
     planes, _ = rb.build_planes_protos(64, 4, L, 1, device="cpu", seed=0)
@@ -169,7 +169,7 @@ def test_fast_backward_segments(B, H, T, L):
     n0 = lib.race_launch_counter()
     dQ, dK, dV = rb.ops.bwd_qkv(Q.cuda(), K.cuda(), V.cuda(), dO.cuda(), planes.cuda(), L, 4)
     torch.cuda.synchronize()
-    assert lib.race_launch_counter() - n0 == 5
+    assert lib.race_launch_counter() - n0 == 6
     dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, L, 4)
     # T=1: the exact dK is a cancellation (dpk = -pq/pk (dO.V) + pq/pk (V.dO) = 0);
     # only an absolute floor at the bf16 resolution of the O(10) cancelling terms
@@ -198,3 +198,31 @@ def test_fast_path_general_scale_and_eps(logit_scale, eps):
     dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, L, 4, eps=eps, logit_scale=logit_scale)
     assert relerr(out, ref) < 2e-2
     assert relerr(dQ, dQ_r) < 2e-2 and relerr(dK, dK_r) < 2e-2 and relerr(dV, dV_r) < 2e-2
+
+
+@pytest.mark.parametrize("B,H,T,L", [(2, 16, 4000, 16), (1, 3, 129, 8)])
+def test_saved_states_backward(B, H, T, L):
+    """fwd_qkv(save=True) keeps the chunk-start states; bwd_qkv(saved=...) skips the
+    two passes that rebuild them (3 launches: reverse walk, suffix scan, fix-up) and
+    gives the same gradients as the rebuilding backward and the oracle."""
+    import race_attention_b200 as rb
+    Q, K, V, dO = qkv(B, H, T, 64, seed=5 * T + L, scale=1.0 / 8.0, dtype=torch.bfloat16)
+    planes, _ = rb.build_planes_protos(64, 4, L, 1, device="cpu", seed=0)
+    args = (Q.cuda(), K.cuda(), V.cuda())
+    pc = planes.cuda()
+    out, saved = rb.ops.fwd_qkv(*args, pc, L, 4, save=True)
+    assert saved is not None and saved.numel() == rb.ops.saved_bytes(B * H, T, 64, L, 4, torch.bfloat16)
+    lib = rb._lib.load()
+    n0 = lib.race_launch_counter()
+    g_saved = rb.ops.bwd_qkv(*args, dO.cuda(), pc, L, 4, saved=saved)
+    torch.cuda.synchronize()
+    assert lib.race_launch_counter() - n0 == 3
+    g_full = rb.ops.bwd_qkv(*args, dO.cuda(), pc, L, 4)
+    ref = O.race_qkv_bwd(Q, K, V, dO, planes, L, 4)[:3]
+    for gs, gf, r in zip(g_saved, g_full, ref):
+        assert relerr(gs, gf) < 2e-3
+        assert relerr(gs, r) < 2e-2
+    # the autograd path uses the saved states
+    q, k, v = (x.clone().requires_grad_(True) for x in args)
+    rb.race_causal(q, k, v, pc, L, 4).backward(dO.cuda())
+    assert relerr(q.grad, g_saved[0]) < 1e-6 and relerr(k.grad, g_saved[1]) < 1e-6
