@@ -54,7 +54,7 @@ extern "C" {
 #define RACE_OP_FWD_QKV 2
 #define RACE_OP_BWD_QKV 3
 #define RACE_OP_STATE 4
-#define RACE_OP_BWD_TOTALS 5
+#define RACE_OP_BWD_SPLIT 5  /* race_bwd_local + race_bwd_finish (one workspace) */
 
 /* Library ABI version (bumped on any signature change). */
 int race_abi_version(void);
@@ -75,11 +75,10 @@ unsigned long long race_launch_counter(void);
  * Enabling clears the totals.  Not for use inside stream capture. */
 #define RACE_KT_FWD_TOTALS 0   /* fused K-hash + segment totals / chunk states */
 #define RACE_KT_FWD_READOUT 1  /* forward readout                              */
-#define RACE_KT_BWD_FWD 2      /* backward forward walk (gradient totals only) */
-#define RACE_KT_BWD_REV 3      /* backward reverse walk (segment-local dK, dV) */
-#define RACE_KT_SCAN 4         /* segment prefix / suffix scans                */
-#define RACE_KT_BWD_FIX 5      /* backward suffix fix-up (dK, dV, dQ)          */
-#define RACE_KT_COUNT 6
+#define RACE_KT_BWD_REV 2      /* backward reverse walk (segment-local grads)  */
+#define RACE_KT_SCAN 3         /* segment prefix / suffix scans                */
+#define RACE_KT_BWD_FIX 4      /* backward suffix fix-up (dK, dV, dQ)          */
+#define RACE_KT_COUNT 5
 int race_kernel_timing(int enable);
 int race_kernel_time(int kernel, double *total_ms, long long *launches);
 
@@ -209,19 +208,28 @@ int race_fwd_sharded_phaseA(const void *K, const void *V, int dtype,
                             float logit_scale,
                             void *workspace, size_t workspace_bytes, void *stream);
 
-/* Backward phase A: this shard's gradient totals for its final state
+/* Backward of a shard in two calls on ONE workspace (RACE_OP_BWD_SPLIT size):
+ * race_bwd_local writes this shard's gradient totals for its start state
  *   gA_tot[N,S]   = sum_t -pq[t,s] * G_t[s] / (A_t[s] + eps)^2,
  *                   G_t[s] = dO_t . B_t[s,:]
  *   gB_tot[N,S,D] = sum_t pq[t,s] * dO_t / (A_t[s] + eps)
- * given the carried-in forward prefix A0/B0.  Backward phase B is
- * race_bwd_qkv with gA_in/gB_in = the sum of the totals of all later shards. */
-int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V,
-                            const void *dO, int dtype, const float *planes_T,
-                            const float *A0, const float *B0,
-                            float *gA_tot, float *gB_tot,
-                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
-                            float eps, float logit_scale,
-                            void *workspace, size_t workspace_bytes, void *stream);
+ * given the carried-in forward prefix A0/B0 (and optionally the `saved`
+ * chunk states of race_fwd_qkv_save), and keeps its local gradients in the
+ * workspace; race_bwd_finish then writes dQ, dK, dV given gA_in/gB_in = the
+ * sum of the totals of all later shards.  Same inputs to both calls. */
+int race_bwd_local(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                   const float *planes_T, const void *saved, size_t saved_bytes,
+                   const float *A0, const float *B0, float *gA_tot, float *gB_tot,
+                   int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                   float eps, float logit_scale,
+                   void *workspace, size_t workspace_bytes, void *stream);
+int race_bwd_finish(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                    const float *planes_T, const void *saved, size_t saved_bytes,
+                    const float *A0, const float *B0, const float *gA_in, const float *gB_in,
+                    void *dQ, void *dK, void *dV,
+                    int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                    float eps, float logit_scale,
+                    void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- allocation-free variant ----------------------------------------------
  * No counterpart in the reference.  Same math and outputs as race_fwd_probs

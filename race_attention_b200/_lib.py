@@ -18,10 +18,9 @@ _lib = None
 RACE_OK = 0
 RACE_F32 = 0
 RACE_BF16 = 1
-OP_FWD_PROBS, OP_BWD_PROBS, OP_FWD_QKV, OP_BWD_QKV, OP_STATE, OP_BWD_TOTALS = range(6)
+OP_FWD_PROBS, OP_BWD_PROBS, OP_FWD_QKV, OP_BWD_QKV, OP_STATE, OP_BWD_SPLIT = range(6)
 # kernel ids of race_kernel_time (include/race_b200.h RACE_KT_*)
-KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_fwd_kernel", "bwd_rev_kernel", "chunk_scan",
-                "bwd_fix_kernel")
+KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_rev_kernel", "chunk_scan", "bwd_fix_kernel")
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -49,8 +48,10 @@ SIGNATURES = {
     "race_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P],
     "race_fwd_sharded_phaseA": [_P, _P, _I, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
     "race_fwd_probs_noalloc": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
-    "race_bwd_sharded_phaseA": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F,
-                                _P, _SZ, _P],
+    "race_bwd_local": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F,
+                       _P, _SZ, _P],
+    "race_bwd_finish": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                        _I64, _F, _F, _P, _SZ, _P],
     "race_saved_bytes": [_I64, _I64, _I64, _I64, _I64, _I, ctypes.POINTER(_SZ)],
     "race_fwd_qkv_save": [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _F, _F, _P,
                           _SZ, _P],

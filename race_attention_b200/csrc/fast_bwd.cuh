@@ -6,22 +6,20 @@
 //   dA_t[s] = -W_t[s] G_t[s] / (A_t[s]+eps)
 //   gA_t    = sum_{t'>=t} dA_t'   gB_t = sum_{t'>=t} W_t' (x) dO_t'   (suffix states)
 //   dpk     = gA_t + V_t . gB_t   dV_t = sum_s pk[t,s] gB_t[s]
-// Two walks per (stream, segment) of 128-token chunks, with buckets handled in
-// groups of 64 (4 tables).  Per-bucket state accumulators are M=64 tcgen05
-// tiles, two groups sharing a TMEM column block (lane offsets 0 and 16).
+// Per (stream, segment) of 128-token chunks, with buckets in groups of 64
+// (4 tables); per-bucket state accumulators are M=64 tcgen05 tiles, two groups
+// sharing a TMEM column block (lane offsets 0 and 16):
 //
-//   bwd_fwd_kernel (forward walk, exact forward state carried in TMEM):
-//     P1 = dO V^T (masked t>=tau) ; per group: Pk, Apref = tril Pk, W, inv,
-//     G = dO Bst^T + P1m Pk, dA, dpq -> d proj_Q ; totals gB += W^T dO,
-//     gA += dA^T 1 ; Bstate += Pk^T V ; then dQ = dprojQ planes.
-//     Stores each chunk's start state (A fp32, B bf16) for the reverse walk.
-//   bwd_rev_kernel (reverse walk, suffix state carried in TMEM):
-//     per group: W, inv, G, dA as above from the stored chunk state;
-//     dpk = tril^T dA + V gBst^T + P1m^T W + gA_suffix -> d proj_K ;
-//     Q2 = Pk W^T (masked t>=tau) ; dV += Pk gBst + Q2m dO ;
-//     gB += W^T dO ; gA += dA^T 1 ; then dK = dprojK planes.
-// The segment-level suffix states come from a reverse chunk_scan of the first
-// walk's totals.  All waits are bounded (see fast_fwd.cuh).
+//   bwd_rev_kernel (reverse walk from a zero suffix state at the segment end,
+//     i.e. segment-local gradient states, forward state from the stored chunk
+//     starts): per group Pk, Apref = tril Pk, W, G = dO Bst^T + P1m Pk, dA,
+//     dpq -> d proj_Q ; dpk = tril^T dA + V gBst^T + P1m^T W + gA -> d proj_K ;
+//     Q2 = Pk W^T (masked t' >= tau) ; dV = Pk gBst + Q2m dO ; gB += W^T dO,
+//     gA += dA^T 1 ; the segment's local totals at the end.
+//   chunk_scan (reverse): the suffix of later segments for each segment.
+//   bwd_fix_kernel (chunks independent): that suffix's linear share of dpk and
+//     dV, dK = d proj_K planes, dQ = d proj_Q planes.
+// All waits are bounded (see fast_fwd.cuh).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -50,6 +48,8 @@ struct BwdArgs {
   __nv_bfloat16 *dQ, *dK, *dV;  // [N, T, 64]
   __nv_bfloat16 *dprojQ;        // [N, T, 64] d proj_Q (columns >= LP unused), reverse walk -> fix-up
   float *dprojK;                // [N, T, 64] segment-local d proj_K (fp32), reverse walk -> fix-up
+  const float *seedA, *seedB;   // fix-up: suffix of later shards added to every segment's ([N,S], [N,S,64])
+  const __nv_bfloat16 *dVloc;   // fix-up: the walk's dV when it is not in dV itself (split backward)
   int *err;
 };
 
@@ -89,13 +89,12 @@ __device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float
 
 // --------------------------------------------------------------------------
 struct BwdSmem {
-  uint32_t q, k, v, o, p1m, tril, planes, plo, pk, w, da, bst, gbst, diag, dproj, a0, a1, ga, bars, total;
+  uint32_t q, k, v, o, p1m, tril, planes, plo, pk, w, da, bst, gbst, diag, a0, ga, bars, total;
 };
 
-// rev: the reverse walk keeps the bf16 residuals of the planes (planes - bf16(planes)), so
-// that its projections are exact to ~2^-17, and the fp32 diagonal of P1 = dO V^T; it writes
-// d proj_K to global memory (no dproj tile) and needs no second A array.
-__host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S, bool rev = false) {
+// planes and plo: bf16 planes and their residuals planes - bf16(planes), so that the
+// projections are exact to ~2^-17; diag: the fp32 diagonal of P1 = dO V^T.
+__host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   BwdSmem m;
   uint32_t o = 0;
   m.q = o; o += TILE;
@@ -105,16 +104,14 @@ __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S, bool re
   m.p1m = o; o += 2 * TILE;
   m.tril = o; o += 2 * TILE;
   m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
-  m.plo = o; if (rev) o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.plo = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
   m.pk = o; o += TILE;
   m.w = o; o += TILE;
-  m.da = o; o += TILE;  // must follow w: [w | da] is the 2-block Q2m tile of the reverse walk
+  m.da = o; o += TILE;  // must follow w: [w | da] is the 2-block Q2m tile
   m.bst = o; o += GW * 128;
   m.gbst = o; o += GW * 128;
-  m.diag = o; if (rev) o += C * 4;
-  m.dproj = o; if (!rev) o += TILE;
+  m.diag = o; o += C * 4;
   m.a0 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
-  m.a1 = o; if (!rev) o += (uint32_t)align_up((size_t)S * 4, 128);
   m.ga = o; o += 2 * GW * 4;  // two buffers (group parity)
   m.bars = o; o += 256;
   m.total = o + 1024;
@@ -130,399 +127,9 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 }
 
 // ===========================================================================
-// forward walk of the backward pass
-//
-// TMEM: X [0,128) = P1 at chunk start, G during the group loop ([0,64)), dQ at
-// chunk end ([0,64)); R [128,192) = Apref; PJ [192,224) = proj of one group
-// (K in 16 columns, Q in 16); then the M=64 state blocks BF (forward B state),
-// GB (gradient B totals), GA (gradient A totals).
-// Schedule (u = chunk * ngroups + group); {X} named barrier (epilogue arrives,
-// control syncs), [X] mbarrier (tcgen05.commit / TMA):
-//   control, per chunk: [VO] P1 = dO V^T -> [P1]
-//            per group: {PK} Apref -> [APREF] ; {P1M, first group}
-//                       Bfwd += Pk^T V ; G = dO Bst^T + P1m Pk -> [G] ;
-//                       proj of the next group -> [PROJ] (after the last: Q/K refill)
-//                       {DA} gB += W^T dO ; gA += dA^T 1
-//            chunk end: dQ = dprojQ planes -> [OUT] ; next chunk's proj(0) ;
-//                       V/dO refill once every reader completed
-//   epilogue, per group: [PROJ] Pk, plane sigmoids, Bst refresh {PK} ;
-//                        (first group: [P1] P1m {P1M}) ;
-//                        [APREF] inv ; [G] W, dA, dpq -> dprojQ {DA}
-//            chunk end:  [OUT] dQ rows {OUTFREE}
-// Abort: as in the forward readout, every thread keeps taking every
-// named-barrier step after a bounded wait gave up.
-enum { V1_QK = 0, V1_VO, V1_P1, V1_PROJ, V1_APREF, V1_G, V1_OUT, V1_TFREE, V1_FINAL, V1_COUNT };
-enum { N1_INIT = 1, N1_PK, N1_P1M, N1_DA, N1_OUTFREE, N1_ESYNC };
-constexpr uint32_t B1_X = 0, B1_R = 128, B1_PJ = 192, B1_ST = 224;
-
-__global__ void __launch_bounds__(NTHR, 1) bwd_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
-                                                          const __grid_constant__ CUtensorMap tmK,
-                                                          const __grid_constant__ CUtensorMap tmV,
-                                                          const __grid_constant__ CUtensorMap tmO, BwdArgs a) {
-  extern __shared__ __align__(1024) unsigned char smraw[];
-  unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
-  const BwdSmem P = bwd_smem_plan(a.LP, a.S);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
-  __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
-  const uint32_t sbase = tc::smem_u32(sm);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
-  const int c_begin = seg * a.seg_chunks;
-  const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
-  const int S = a.S, NG = a.ngroups, nblk = (NG + 1) / 2;
-  const size_t E = (size_t)S + (size_t)S * HD;
-  const uint32_t T_BF = B1_ST, T_GB = B1_ST + 64 * nblk, T_GA = B1_ST + 128 * nblk;
-
-  if (threadIdx.x == 0) {
-    s_abort = 0;
-    for (int i = 0; i < V1_COUNT; ++i) tc::mbar_init(&bars[i], 1);
-    tc::fence_mbar_init();
-  }
-  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
-  tc::tc_fence_before();
-  __syncthreads();
-  tc::tc_fence_after();
-  const uint32_t tmem = s_tmem;
-  volatile int *abort = &s_abort;
-
-  if (warp == NEPI) {
-    // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
-    const bool leader = lane == 0;
-    const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
-    const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
-    const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
-    const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
-    const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
-    const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
-    const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
-    const uint32_t id_dq = tc::idesc_bf16(C, HD, false, true);
-    const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o;
-    auto load_qk = [=, &tmQ, &tmK](int c) {
-      const int t0 = (c_begin + c) * C;
-      tc::mbar_arrive_expect_tx(&bars[V1_QK], 2 * TILE);
-      tc::tma_load_3d(sm + oq, &tmQ, &bars[V1_QK], 0, t0, n);
-      tc::tma_load_3d(sm + ok_, &tmK, &bars[V1_QK], 0, t0, n);
-    };
-    auto load_vo = [=, &tmV, &tmO](int c) {
-      const int t0 = (c_begin + c) * C;
-      tc::mbar_arrive_expect_tx(&bars[V1_VO], 2 * TILE);
-      tc::tma_load_3d(sm + ov, &tmV, &bars[V1_VO], 0, t0, n);
-      tc::tma_load_3d(sm + oo, &tmO, &bars[V1_VO], 0, t0, n);
-    };
-    auto issue_proj = [=](int g) {
-      const uint32_t pl = sbase + P.planes + (uint32_t)g * 16 * 128;
-#pragma unroll
-      for (int k0 = 0; k0 < HD; k0 += 16) {
-        const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
-        tc::mma_bf16(tmem + B1_PJ, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
-        tc::mma_bf16(tmem + B1_PJ + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
-      }
-      tc::mma_commit(&bars[V1_PROJ]);
-    };
-    bool ok = true;
-    if (leader && nch > 0) {
-      load_qk(0);
-      load_vo(0);
-    }
-    tc::named_bar_sync(N1_INIT, NTHR);  // planes, tril, A and B state are in place
-    if (leader && nch > 0) {
-      ok = tc::mbar_wait(&bars[V1_QK], 0, abort);
-      if (ok) {
-        tc::tc_fence_after();
-        issue_proj(0);
-      }
-    }
-    for (int c = 0; c < nch; ++c) {
-      if (c > 0) tc::named_bar_sync(N1_OUTFREE, NTHR);  // the previous dQ is out of X
-      ok = ok && !*abort;
-      if (leader && ok) {
-        ok = tc::mbar_wait(&bars[V1_VO], c & 1, abort);
-        if (ok) {
-          tc::tc_fence_after();
-#pragma unroll
-          for (int k0 = 0; k0 < HD; k0 += 16)
-            tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.v, k0, 0), id_p1,
-                         k0 > 0);
-          tc::mma_commit(&bars[V1_P1]);
-        }
-      }
-      for (int g = 0; g < NG; ++g) {
-        tc::named_bar_sync(N1_PK, NTHR);
-        ok = ok && !*abort;
-        if (leader && ok) {
-          tc::tc_fence_after();
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + B1_R, tc::desc_kmajor(sbase + P.tril, k0, TILE),
-                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_apref, k0 > 0);
-          tc::mma_commit(&bars[V1_APREF]);
-        }
-        if (g == 0) {
-          tc::named_bar_sync(N1_P1M, NTHR);
-          ok = ok && !*abort;
-        }
-        if (leader && ok) {
-          tc::tc_fence_after();
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(m64_addr(tmem, T_BF, g, 64), tc::desc_mnmajor(sbase + P.pk, k0, 0),
-                         tc::desc_mnmajor(sbase + P.v, k0, 0), id_st, true);
-#pragma unroll
-          for (int k0 = 0; k0 < HD; k0 += 16)
-            tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
-                         id_gk, k0 > 0);
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.pk, k0, 0),
-                         id_gm, true);
-          tc::mma_commit(&bars[V1_G]);
-          if (g + 1 < NG) {
-            issue_proj(g + 1);
-          } else if (c + 1 < nch) {
-            load_qk(c + 1);  // the last proj of this chunk was consumed before {PK}
-          }
-        }
-        tc::named_bar_sync(N1_DA, NTHR);
-        ok = ok && !*abort;
-        if (leader && ok) {
-          tc::tc_fence_after();
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16) {
-            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
-                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, c > 0 || k0 > 0);
-            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
-                         tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, c > 0 || k0 > 0);
-          }
-        }
-      }
-      if (leader && ok) {
-        for (int k0 = 0; k0 < a.LP; k0 += 16)
-          tc::mma_bf16(tmem + B1_X, tc::desc_kmajor(sbase + P.dproj, k0, 0), tc::desc_mnmajor(sbase + P.planes, k0, 0),
-                       id_dq, k0 > 0);
-        tc::mma_commit(&bars[V1_OUT]);
-        if (c + 1 < nch) {
-          ok = tc::mbar_wait(&bars[V1_QK], (c + 1) & 1, abort);
-          if (ok) {
-            tc::tc_fence_after();
-            issue_proj(0);
-            // V and dO are free once every MMA issued so far has completed
-            tc::mma_commit(&bars[V1_TFREE]);
-            ok = tc::mbar_wait(&bars[V1_TFREE], c & 1, abort);
-            if (ok) load_vo(c + 1);
-          }
-        }
-      }
-    }
-    if (leader && nch > 0) {
-      tc::mma_commit(&bars[V1_FINAL]);
-      if (!tc::mbar_wait_drain(&bars[V1_FINAL], 0)) atomicExch(a.err, 2);
-    }
-    __syncwarp();
-  } else {
-    // ============================== epilogue warps: row t, column quarter hq
-    // (in a 64-bucket group, quarter hq owns table 4g + hq: buckets [16hq, 16hq+16))
-    const int q4 = warp & 3, hq = warp >> 2;
-    const int t = q4 * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
-    const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
-    const int mrow = m64_row(q4, lane), mpar = lane >> 4;
-    float *const sA0 = reinterpret_cast<float *>(sm + P.a0);
-    const float *st0 = a.fwd_state + ((size_t)n * a.nseg + seg) * E;
-    // ---- prologue
-    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {
-      const int j = i / HD, d = i % HD;
-      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(j, d >> 3) + (d & 7) * 2) =
-          __float2bfloat16(a.planes[(size_t)d * a.LP + j]);
-    }
-    {
-      float v[8];
-      for (int ch = 0; ch < 4; ++ch) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) <= t ? 1.f : 0.f;
-        tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
-      }
-    }
-    // the A arrays (and the per-chunk A records) hold A + eps
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = st0[s] + a.eps;
-    for (int b = 0; b < nblk; ++b) {  // forward state -> TMEM (M=64 layout), this lane's row, d in [16hq, +16)
-      const int g = 2 * b + mpar;
-      float v[16];
-      if (g < NG) {
-        const float *src = st0 + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = src[i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      }
-      tc::tmem_st16(tmem + lane_off + T_BF + 64 * b + 16 * hq, v);
-    }
-    tc::tmem_wait_st();
-    tc::fence_async_smem();
-    tc::tc_fence_before();
-    tc::named_bar_sync(N1_INIT, NTHR);
-
-    bool ok = true;
-    for (int c = 0; c < nch; ++c) {
-      const int cg = c_begin + c, tok0 = cg * C;
-      const int nt = min(C, a.T - tok0);
-      const uint32_t aCur = sbase + ((c & 1) ? P.a1 : P.a0), aNxt = sbase + ((c & 1) ? P.a0 : P.a1);
-      const float *Acur = reinterpret_cast<const float *>(sm + ((c & 1) ? P.a1 : P.a0));
-      // the row-127 threads wrote this chunk's A during the previous one
-      tc::named_bar_sync(N1_ESYNC, NEPI_T);
-      if (ok) {
-        for (int s = threadIdx.x; s < S; s += NEPI_T) a.chunkA[((size_t)n * a.nchunks + cg) * S + s] = Acur[s];
-      }
-      for (int g = 0; g < NG; ++g) {
-        const int u = c * NG + g;
-        float thQ[4], qQ[4], inv[16];  // this row's Q-side tanh and plane sigmoids of table 4g + hq
-        // ---- Pk ; chunk-start B state of this group -> smem bf16 + global
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_PROJ], u & 1, abort));
-        tc::tc_fence_after();
-        if (ok) {
-          float pk4[4], pr[16], bv[16];
-          tc::tmem_ld4(tmem + lane_off + B1_PJ + 4 * hq, pk4);
-          tc::tmem_ld4(tmem + lane_off + B1_PJ + 16 + 4 * hq, thQ);
-          tc::tmem_ld16(tmem + lane_off + T_BF + 64 * (g >> 1) + 16 * hq, bv);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            pk4[i] = tanh_fast(pk4[i]);
-            thQ[i] = tanh_fast(thQ[i]);
-          }
-          plane_sigmoids(pk4, a.scale, a.poly, pk4);
-          corner_probs(pk4, pr);
-          if (t >= nt) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pr[i] = 0.f;
-          }
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
-          plane_sigmoids(thQ, a.scale, a.poly, qQ);
-          if (mpar == (g & 1)) {
-#pragma unroll
-            for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst, mrow, 2 * hq + ch, bv + 8 * ch);
-            __nv_bfloat16 *dst = a.chunkB + (((size_t)n * a.nchunks + cg) * S + g * GW + mrow) * HD + 16 * hq;
-#pragma unroll
-            for (int ch = 0; ch < 2; ++ch) st_bf16x8_global(dst + 8 * ch, bv + 8 * ch);
-          }
-        }
-        tc::fence_async_smem();
-        tc::tc_fence_before();
-        tc::named_bar_arrive(N1_PK, NTHR);
-        if (g == 0) {
-          // ---- P1m = tril-masked dO V^T
-          if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_P1], c & 1, abort));
-          tc::tc_fence_after();
-          if (ok) {
-            float v[32];
-            tc::tmem_ld32(tmem + lane_off + B1_X + 32 * hq, v);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (32 * hq + i > t) v[i] = 0.f;
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
-          }
-          tc::fence_async_smem();
-          tc::tc_fence_before();
-          tc::named_bar_arrive(N1_P1M, NTHR);
-        }
-        // ---- inv from Apref (while G runs)
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_APREF], u & 1, abort));
-        tc::tc_fence_after();
-        if (ok) {
-          float ap[16];
-          tc::tmem_ld16(tmem + lane_off + B1_R + 16 * hq, ap);
-          tc::tmem_wait_ld();
-          const int sb = g * GW + 16 * hq;
-          add_shared_row<16>(aCur + 4 * sb, ap);  // + (A + eps) at chunk start
-          if (t == C - 1) store_shared_row<16>(aNxt + 4 * sb, ap);
-          rcp_n<16>(ap, inv, a.batch_rcp);
-        }
-        // ---- G -> W, dpq (-> d proj_Q) and dA
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_G], u & 1, abort));
-        tc::tc_fence_after();
-        if (ok) {
-          float G[16], pq[16], da[16];
-          tc::tmem_ld16(tmem + lane_off + B1_X + 16 * hq, G);
-          tc::tmem_wait_ld();
-          corner_probs(qQ, pq);
-          const bool live = t < nt;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float w = live ? pq[i] * inv[i] : 0.f;  // W
-            const float gi = live ? G[i] * inv[i] : 0.f;  // dpq
-            da[i] = -w * gi;                              // dA
-            G[i] = gi;
-            inv[i] = w;
-          }
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, inv + 8 * ch);
-            tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, da + 8 * ch);
-          }
-          float dp[4];
-          table_probs_bwd(pq, G, thQ, a.scale, dp);
-          tc::st_row_half(sbase + P.dproj, t, 2 * g + (hq >> 1), hq & 1, dp);
-        }
-        tc::fence_async_smem();
-        tc::tc_fence_before();
-        tc::named_bar_arrive(N1_DA, NTHR);
-      }
-      // ---- dQ, d in [16hq, 16hq+16)
-      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V1_OUT], c & 1, abort));
-      tc::tc_fence_after();
-      if (ok) {
-        float ov[16];
-        tc::tmem_ld16(tmem + lane_off + B1_X + 16 * hq, ov);
-        tc::tmem_wait_ld();
-        if (t < nt && a.dQ != nullptr) {
-          __nv_bfloat16 *dst = a.dQ + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) st_bf16x8_global(dst + 8 * ch, ov + 8 * ch);
-        }
-      }
-      tc::tc_fence_before();
-      if (c + 1 < nch) tc::named_bar_arrive(N1_OUTFREE, NTHR);
-    }
-    // ---- segment totals record (OUT of the last chunk covers every accumulation)
-    if (ok && nch > 0) {
-      float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
-      for (int b = 0; b < nblk; ++b) {
-        const int g = 2 * b + mpar;
-        float bv[16], av;
-        tc::tmem_ld16(tmem + lane_off + T_GB + 64 * b + 16 * hq, bv);
-        tc::tmem_ld1(tmem + lane_off + T_GA + 16 * b, av);
-        tc::tmem_wait_ld();
-        if (g < NG) {
-          float *dst = rec + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) dst[i] = bv[i];
-          if (hq == 0) rec[g * GW + mrow] = av;
-        }
-      }
-    } else if (nch == 0) {
-      float *rec = a.tot + ((size_t)n * a.nseg + seg) * E;
-      for (int i = threadIdx.x; i < (int)E; i += NEPI_T) rec[i] = 0.f;
-    }
-    if (!ok && lane == 0) atomicExch(a.err, 1);
-  }
-  tc::tc_fence_before();
-  __syncthreads();
-  if (warp == NEPI) {
-    if (s_abort && lane == 0) atomicExch(a.err, 1);
-    tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, 512);
-  }
-}
-
-// ===========================================================================
 // reverse walk of the backward pass
 //
-// TMEM: X [0,128) = P1 at chunk start, Q2 per group, dK at chunk end;
+// TMEM: X [0,128) = P1 at chunk start, then Q2 per group;
 // R [128,192) = Apref, then dpk; GD [192,256) = G; PJ [256,288) = proj of one
 // group; then GB, GA (M=64 suffix-state blocks) and DV [.., +64).
 // Schedule per group g ({X} named barrier, [X] mbarrier):
@@ -550,7 +157,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap tmB, BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
-  const BwdSmem P = bwd_smem_plan(a.LP, a.S, true);
+  const BwdSmem P = bwd_smem_plan(a.LP, a.S);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
   // no static shared memory (it would cost a 1 KB aligned block): the TMEM base
   // and the abort flag live after the barriers
@@ -1210,14 +817,17 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + off) = hi;
       *reinterpret_cast<__nv_bfloat16 *>(sm + P.plo + off) = __float2bfloat16(pv - __bfloat162float(hi));
     }
+    const float *seedB = a.seedB ? a.seedB + (size_t)n * S * HD : nullptr;
+    const float *seedA = a.seedA ? a.seedA + (size_t)n * S : nullptr;
     for (int i = threadIdx.x; i < S * 8; i += NEPI_T) {  // gB_in (bf16 rows s), 8 values per step
       const int sr = i >> 3, ch = i & 7;
       float v[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = sin[S + (size_t)sr * HD + ch * 8 + e];
+      for (int e = 0; e < 8; ++e)
+        v[e] = sin[S + (size_t)sr * HD + ch * 8 + e] + (seedB ? seedB[(size_t)sr * HD + ch * 8 + e] : 0.f);
       tc::st_row_chunk(sbase + P.gb, sr, ch, v);
     }
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sGA[s] = sin[s];
+    for (int s = threadIdx.x; s < S; s += NEPI_T) sGA[s] = sin[s] + (seedA ? seedA[s] : 0.f);
     tc::fence_async_smem();
     tc::named_bar_sync(NF_INIT, NTHR);
 
@@ -1305,9 +915,10 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       tc::named_bar_arrive(NF_DP, NTHR);
       // ---- dK, dV += dV_fix, dQ (row t, d in [16hq, 16hq+16))
       uint4 dvl[2];  // the walk's dV rows, loaded before the wait
+      const __nv_bfloat16 *dvsrc = a.dVloc ? a.dVloc : a.dV;
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch)
-        dvl[ch] = live ? *reinterpret_cast<const uint4 *>(a.dV + row + 16 * hq + 8 * ch) : make_uint4(0, 0, 0, 0);
+        dvl[ch] = live ? *reinterpret_cast<const uint4 *>(dvsrc + row + 16 * hq + 8 * ch) : make_uint4(0, 0, 0, 0);
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_OUT], c & 1, abort));
       tc::tc_fence_after();
       if (ok) {

@@ -114,13 +114,15 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Backward workspace: status | forward segment records | backward segment
 // records | per-chunk start state (A + eps fp32, B bf16) | d proj_Q [N, T, 64] bf16
-// and segment-local d proj_K [N, T, 64] fp32 (reverse walk -> fix-up).
+// and segment-local d proj_K [N, T, 64] fp32 (reverse walk -> fix-up) | for the
+// split backward, the walk's dV [N, T, 64] bf16.
 struct BwdPlan {
   Plan p;
-  size_t fwd_rec, bwd_rec, chunkA, chunkB, dprojQ, dprojK, total;
+  size_t fwd_rec, bwd_rec, chunkA, chunkB, dprojQ, dprojK, dVloc, total;
 };
 
-inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms) {
+// split: room for the walk's dV between race_bwd_local and race_bwd_finish
+inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms, bool split = false) {
   BwdPlan b;
   b.p = plan(N, T, S, sms);
   const size_t E = (size_t)S + (size_t)S * fk::HD;
@@ -131,11 +133,14 @@ inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms) {
   b.chunkB = b.chunkA + align_up(sizeof(float) * (size_t)N * b.p.nchunks * S, 256);
   b.dprojQ = b.chunkB + align_up(sizeof(uint16_t) * (size_t)N * b.p.nchunks * S * fk::HD, 256);
   b.dprojK = b.dprojQ + align_up(sizeof(uint16_t) * (size_t)N * T * fk::HD, 256);
-  b.total = b.dprojK + align_up(sizeof(float) * (size_t)N * T * fk::HD, 256);
+  b.dVloc = b.dprojK + align_up(sizeof(float) * (size_t)N * T * fk::HD, 256);
+  b.total = b.dVloc + (split ? align_up(sizeof(uint16_t) * (size_t)N * T * fk::HD, 256) : 0);
   return b;
 }
 
-inline size_t bwd_workspace_bytes(int64_t N, int64_t T, int64_t S) { return bwd_plan(N, T, S, 256).total; }
+inline size_t bwd_workspace_bytes(int64_t N, int64_t T, int64_t S, bool split = false) {
+  return bwd_plan(N, T, S, 256, split).total;
+}
 
 // What a saving forward keeps for the backward: A + eps [N, nchunks, S] fp32 and
 // B [N, nchunks, S, 64] bf16 at every 128-token chunk start (independent of the segment plan).

@@ -4,6 +4,9 @@
 // Nothing here allocates device memory; launches go on the caller's stream.
 #include "race_b200.h"
 
+// the generic path's layout for the gradient-totals half of the split backward
+#define RACE_OP_BWD_TOTALS RACE_OP_BWD_SPLIT
+
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -452,20 +455,28 @@ int fast_forward(const void *Q, const void *K, const void *V, const float *plane
   return check_launch("fast fwd_readout");
 }
 
+// Backward of the tcgen05 path.  FULL: everything in one call.  LOCAL (first half of
+// the split backward of a sequence shard): the walk and the suffix scan over this
+// shard's segments; dA0/dB0 receive the shard's gradient totals and the workspace
+// keeps the rest.  FINISH: the fix-up with the later shards' suffix (seedA/seedB)
+// added to every segment's, on the workspace LOCAL left.
+enum BwdMode { BWD_FULL = 0, BWD_LOCAL, BWD_FINISH };
+
 int fast_backward(const void *Q, const void *K, const void *V, const void *dO, const float *planes_T, void *dQ,
                   void *dK, void *dV, const float *A0, const float *B0, const float *gA, const float *gB, float *dA0,
                   float *dB0, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws, cudaStream_t s,
-                  bool totals_only, const void *saved = nullptr) {
+                  BwdMode mode, const void *saved = nullptr) {
   const int64_t S = 16 * L;
-  const fh::BwdPlan bp = fh::bwd_plan(N, T, S, fh::sm_count());
+  const fh::BwdPlan bp = fh::bwd_plan(N, T, S, fh::sm_count(), mode != BWD_FULL);
   fk::FwdArgs fa;
   CUtensorMap mQ, mK, mV, mO, mB, mP;
-  // chunk-start states: saved by the forward, or recomputed below
+  // chunk-start states: saved by the forward, or rebuilt below
   const fh::SavedPlan sp = fh::saved_plan(N, T, S);
   float *chunkA = saved ? at<float>(const_cast<void *>(saved), sp.chunkA) : at<float>(ws, bp.chunkA);
   __nv_bfloat16 *chunkB =
       saved ? at<__nv_bfloat16>(const_cast<void *>(saved), sp.chunkB) : at<__nv_bfloat16>(ws, bp.chunkB);
-  if (saved == nullptr) {
+  const bool rebuild = saved == nullptr && mode != BWD_FINISH;
+  if (rebuild) {
     // forward segment prefixes (exclusive, seeded with the carried-in state)
     RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, nullptr, nullptr, N, T, L, eps, scale, ws, s, fa, mK, mV,
                                   bp.fwd_rec));
@@ -473,12 +484,14 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
     if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
     if (!fh::make_map(&mK, K, N, T) || !fh::make_map(&mV, V, N, T))
       return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(K/V) failed: CUresult %d", fh::last_encode_status());
-    cudaError_t e = cudaMemsetAsync(at<int>(ws, 0), 0, sizeof(int), s);
-    if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    if (mode != BWD_FINISH) {
+      cudaError_t e = cudaMemsetAsync(at<int>(ws, 0), 0, sizeof(int), s);
+      if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
   }
-  if (!fh::make_map(&mQ, Q, N, T) || !fh::make_map(&mO, dO, N, T) ||
-      !fh::make_map(&mP, at<void>(ws, bp.dprojQ), N, T) ||
-      !fh::make_rows_map(&mB, chunkB, N * (int64_t)bp.p.nchunks * S))
+  if (!fh::make_map(&mP, at<void>(ws, bp.dprojQ), N, T) ||
+      (mode != BWD_FINISH && (!fh::make_map(&mQ, Q, N, T) || !fh::make_map(&mO, dO, N, T) ||
+                              !fh::make_rows_map(&mB, chunkB, N * (int64_t)bp.p.nchunks * S))))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed in the backward: CUresult %d",
                 fh::last_encode_status());
   fk::BwdArgs b;
@@ -503,61 +516,58 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   b.chunkB = chunkB;
   b.dQ = nullptr;
   b.dK = static_cast<__nv_bfloat16 *>(dK);
-  b.dV = static_cast<__nv_bfloat16 *>(dV);
+  b.dV = mode == BWD_FULL ? static_cast<__nv_bfloat16 *>(dV) : at<__nv_bfloat16>(ws, bp.dVloc);
   b.dprojQ = at<__nv_bfloat16>(ws, bp.dprojQ);
   b.dprojK = at<float>(ws, bp.dprojK);
+  b.seedA = b.seedB = nullptr;
+  b.dVloc = nullptr;
   b.err = at<int>(ws, 0);
   const unsigned grid = (unsigned)(N * bp.p.nseg);
   gen::Dims p = make_dims(N, T, S, fk::HD, eps);
   p.G = bp.p.nseg;
-  if (totals_only) {
-    // gradient totals only (sequence-sharded phase A): the forward walk
-    const fk::BwdSmem bs = fk::bwd_smem_plan(b.LP, b.S);
-    RACE_TRY(set_smem(fk::bwd_fwd_kernel, bs.total));
+  if (mode != BWD_FINISH) {
+    // 1. chunk-start forward states (A + eps, bf16 B) from the segment prefixes, unless saved
+    if (rebuild) {
+      fa.chunkA = b.chunkA;
+      fa.chunkB = b.chunkB;
+      fa.seg_state = b.fwd_state;
+      {
+        const fk::TotSmem ts = fk::tot_smem_plan(fa.ngroups, fa.LP);
+        KernelScope ks(RACE_KT_FWD_TOTALS, s);
+        fk::fwd_totals_kernel<<<grid, fk::NTHR, ts.total, s>>>(mK, mV, fa);
+        ks.stop();
+      }
+      RACE_TRY(check_launch("fast chunk states"));
+    }
+    // 2. segment-local reverse walk: dV and d proj_K without the later segments' suffix,
+    //    d proj_Q, the segments' local totals
+    const fk::BwdSmem rs = fk::bwd_smem_plan(b.LP, b.S);
+    RACE_TRY(set_smem(fk::bwd_rev_kernel, rs.total));
     {
-      KernelScope ks(RACE_KT_BWD_FWD, s);
-      fk::bwd_fwd_kernel<<<grid, fk::NTHR, bs.total, s>>>(mQ, mK, mV, mO, b);
+      KernelScope ks(RACE_KT_BWD_REV, s);
+      fk::bwd_rev_kernel<<<grid, fk::NTHR, rs.total, s>>>(mQ, mK, mV, mO, mB, b);
       ks.stop();
     }
-    RACE_TRY(check_launch("fast bwd_fwd"));
-    KernelScope ks(RACE_KT_SCAN, s);
-    const int rc = launch_scan(at<float>(ws, bp.bwd_rec), nullptr, nullptr, dA0, dB0, p, 1, s);
-    ks.stop();
-    return rc;
-  }
-  // 1. chunk-start forward states (A + eps, bf16 B) from the segment prefixes, unless saved
-  if (saved == nullptr) {
-    fa.chunkA = b.chunkA;
-    fa.chunkB = b.chunkB;
-    fa.seg_state = b.fwd_state;
+    RACE_TRY(check_launch("fast bwd_rev"));
+    // 3. suffix over segments (seeded with the carried-in gradient state); its totals are dA0, dB0
     {
-      const fk::TotSmem ts = fk::tot_smem_plan(fa.ngroups, fa.LP);
-      KernelScope ks(RACE_KT_FWD_TOTALS, s);
-      fk::fwd_totals_kernel<<<grid, fk::NTHR, ts.total, s>>>(mK, mV, fa);
+      KernelScope ks(RACE_KT_SCAN, s);
+      const int rc = launch_scan(at<float>(ws, bp.bwd_rec), mode == BWD_FULL ? gA : nullptr,
+                                 mode == BWD_FULL ? gB : nullptr, dA0, dB0, p, 1, s);
       ks.stop();
+      RACE_TRY(rc);
     }
-    RACE_TRY(check_launch("fast chunk states"));
+    if (mode == BWD_LOCAL) return RACE_OK;
   }
-  // 2. segment-local reverse walk: dV and d proj_K without the later segments' suffix, d proj_Q,
-  //    local totals
-  const fk::BwdSmem rs = fk::bwd_smem_plan(b.LP, b.S, true);
-  RACE_TRY(set_smem(fk::bwd_rev_kernel, rs.total));
-  {
-    KernelScope ks(RACE_KT_BWD_REV, s);
-    fk::bwd_rev_kernel<<<grid, fk::NTHR, rs.total, s>>>(mQ, mK, mV, mO, mB, b);
-    ks.stop();
-  }
-  RACE_TRY(check_launch("fast bwd_rev"));
-  // 3. suffix over segments (seeded with the carried-in gradient state); its totals are dA0, dB0
-  {
-    KernelScope ks(RACE_KT_SCAN, s);
-    const int rc = launch_scan(at<float>(ws, bp.bwd_rec), gA, gB, dA0, dB0, p, 1, s);
-    ks.stop();
-    RACE_TRY(rc);
-  }
-  // 4. fix-up: the suffix's linear contribution to dV and d proj_K; dK, dQ from d proj_K, d proj_Q
+  // 4. fix-up: the suffix's linear share of dV and d proj_K; dK, dQ from d proj_K, d proj_Q
   b.suf_state = at<float>(ws, bp.bwd_rec);
   b.dQ = static_cast<__nv_bfloat16 *>(dQ);
+  b.dV = static_cast<__nv_bfloat16 *>(dV);
+  if (mode == BWD_FINISH) {
+    b.seedA = gA;
+    b.seedB = gB;
+    b.dVloc = at<__nv_bfloat16>(ws, bp.dVloc);
+  }
   const fk::FixSmem xs = fk::fix_smem_plan(b.LP, b.S);
   RACE_TRY(set_smem(fk::bwd_fix_kernel, xs.total));
   KernelScope ks(RACE_KT_BWD_FIX, s);
@@ -664,8 +674,13 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int
   RACE_TRY(check_nts(N, T, S, D));
   if ((op == RACE_OP_FWD_QKV || op == RACE_OP_STATE) && fh::eligible(dtype, D, L, P))
     *bytes = fh::fwd_workspace_bytes(N, T, S);
-  else if ((op == RACE_OP_BWD_QKV || op == RACE_OP_BWD_TOTALS) && fh::eligible(dtype, D, L, P))
+  else if (op == RACE_OP_BWD_QKV && fh::eligible(dtype, D, L, P))
     *bytes = fh::bwd_workspace_bytes(N, T, S);
+  else if (op == RACE_OP_BWD_SPLIT && fh::eligible(dtype, D, L, P))
+    *bytes = fh::bwd_workspace_bytes(N, T, S, true);
+  else if (op == RACE_OP_BWD_SPLIT)
+    *bytes = std::max(generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total,
+                      generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total);
   else
     *bytes = generic_layout(op, N, T, S, D).total;
   return ok();
@@ -828,7 +843,7 @@ static int bwd_qkv_impl(const void *Q, const void *K, const void *V, const void 
       if (!fh::aligned16(saved)) return fail(RACE_ERR_ALIGN, "saved-state buffer must be 16-byte aligned");
     }
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, L, eps,
-                           logit_scale, workspace, s, false, saved));
+                           logit_scale, workspace, s, BWD_FULL, saved));
     return ok();
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
@@ -927,10 +942,10 @@ int race_fwd_sharded_phaseA(const void *K, const void *V, int dtype, const float
                                  workspace, workspace_bytes, stream);
 }
 
-int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V, const void *dO, int dtype,
-                            const float *planes_T, const float *A0, const float *B0, float *gA_tot, float *gB_tot,
-                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps, float logit_scale,
-                            void *workspace, size_t workspace_bytes, void *stream) {
+int race_bwd_local(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                   const void *saved, size_t saved_bytes, const float *A0, const float *B0, float *gA_tot,
+                   float *gB_tot, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
+                   float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
   RACE_NONNULL(Q);
   RACE_NONNULL(K);
   RACE_NONNULL(V);
@@ -944,10 +959,13 @@ int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V, const v
   RACE_TRY(check_nts(N, T, S, D));
   cudaStream_t s = as_stream(stream);
   if (fh::eligible(dtype, D, L, P)) {
-    RACE_TRY(check_ws(workspace, workspace_bytes, fh::bwd_workspace_bytes(N, T, S)));
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::bwd_workspace_bytes(N, T, S, true)));
     RACE_TRY(check_fast_ptrs({Q, K, V, dO}));
+    if (saved_bytes && saved_bytes < fh::saved_plan(N, T, S).total)
+      return fail(RACE_ERR_WORKSPACE, "saved-state buffer too small");
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, nullptr, nullptr, nullptr, A0, B0, nullptr, nullptr, gA_tot,
-                           gB_tot, N, T, L, eps, logit_scale, workspace, s, true));
+                           gB_tot, N, T, L, eps, logit_scale, workspace, s, BWD_LOCAL,
+                           saved_bytes ? saved : nullptr));
     return ok();
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total));
@@ -960,6 +978,35 @@ int race_bwd_sharded_phaseA(const void *Q, const void *K, const void *V, const v
                                                (const __nv_bfloat16 *)V, (const __nv_bfloat16 *)dO, planes_T, A0, B0,
                                                gA_tot, gB_tot, N, T, D, L, P, eps, logit_scale, workspace, s));
   return ok();
+}
+
+int race_bwd_finish(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                    const void *saved, size_t saved_bytes, const float *A0, const float *B0, const float *gA_in,
+                    const float *gB_in, void *dQ, void *dK, void *dV, int64_t N, int64_t T, int64_t D, int64_t L,
+                    int64_t P, float eps, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(dO);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(dQ);
+  RACE_NONNULL(dK);
+  RACE_NONNULL(dV);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  cudaStream_t s = as_stream(stream);
+  if (fh::eligible(dtype, D, L, P)) {
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::bwd_workspace_bytes(N, T, S, true)));
+    RACE_TRY(check_fast_ptrs({K, V, dQ, dK, dV}));
+    RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, nullptr, nullptr, N, T, L, eps,
+                           logit_scale, workspace, s, BWD_FINISH, saved_bytes ? saved : nullptr));
+    return ok();
+  }
+  // generic path: the whole backward again, with the later shards' suffix
+  return race_bwd_qkv(Q, K, V, dO, dtype, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, nullptr, nullptr, N, T, D, L,
+                      P, eps, logit_scale, workspace, workspace_bytes, stream);
 }
 
 int race_decode_step(const void *q, const void *k, const void *v, int dtype, const float *planes_T, float *A,

@@ -291,8 +291,16 @@ def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None)
     return A, B
 
 
-def bwd_totals(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None):
-    """(gA_tot[N,S], gB_tot[N,S,D]): this shard's final-state gradient totals."""
+class BwdSplit:
+    """What race_bwd_local leaves for race_bwd_finish: the inputs and the workspace."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def bwd_local(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=None, saved=None):
+    """First half of a shard's backward: (gA_tot[N,S], gB_tot[N,S,D], handle) -- this shard's
+    gradient totals for its start state; the handle goes to bwd_finish."""
     dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
     dO = _as_ntd(dO, "dO").to(Q.dtype)
     A0, B0 = _opt_state(A0, B0, N, S, D, dev)
@@ -300,13 +308,34 @@ def bwd_totals(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None,
     gB = torch.empty((N, S, D), dtype=torch.float32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
-        ws, nb = _workspace(_lib.OP_BWD_TOTALS, N, T, S, D, L, P, _dtype_code(Q), dev)
-        _lib.check(lib.race_bwd_sharded_phaseA(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T),
-                                               _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), N, T, D, L, P, float(eps),
-                                               scale, _ptr(ws), nb, _stream(dev)), "race_bwd_sharded_phaseA")
+        ws, nb = _workspace(_lib.OP_BWD_SPLIT, N, T, S, D, L, P, _dtype_code(Q), dev)
+        sb = saved.numel() if saved is not None else 0
+        _lib.check(lib.race_bwd_local(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T),
+                                      _ptr(saved), sb, _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), N, T, D, L, P,
+                                      float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_bwd_local")
         if fast_path(Q.dtype, D, L, P):
-            _check_status(ws, "race_bwd_sharded_phaseA")
-    return gA, gB
+            _check_status(ws, "race_bwd_local")
+    h = BwdSplit(Q=Q, K=K, V=V, dO=dO, planes_T=planes_T, L=L, P=P, eps=eps, scale=scale, A0=A0, B0=B0,
+                 saved=saved, ws=ws, nb=nb, dev=dev)
+    return gA, gB, h
+
+
+def bwd_finish(h, gA=None, gB=None):
+    """Second half: (dQ, dK, dV) given gA/gB = the sum of the totals of all later shards."""
+    N, T, D = h.Q.shape
+    S = h.L << h.P
+    gA, gB = _opt_state(gA, gB, N, S, D, h.dev)
+    dQ, dK, dV = torch.empty_like(h.Q), torch.empty_like(h.K), torch.empty_like(h.V)
+    lib = _lib.load()
+    with torch.cuda.device(h.dev):
+        sb = h.saved.numel() if h.saved is not None else 0
+        _lib.check(lib.race_bwd_finish(_ptr(h.Q), _ptr(h.K), _ptr(h.V), _ptr(h.dO), _dtype_code(h.Q),
+                                       _ptr(h.planes_T), _ptr(h.saved), sb, _ptr(h.A0), _ptr(h.B0), _ptr(gA),
+                                       _ptr(gB), _ptr(dQ), _ptr(dK), _ptr(dV), N, T, D, h.L, h.P, float(h.eps),
+                                       h.scale, _ptr(h.ws), h.nb, _stream(h.dev)), "race_bwd_finish")
+        if fast_path(h.Q.dtype, D, h.L, h.P):
+            _check_status(h.ws, "race_bwd_finish")
+    return dQ, dK, dV
 
 
 def decode_step(q, k, v, planes_T, A, B, L, P, eps=1e-6, logit_scale=None):

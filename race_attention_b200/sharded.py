@@ -7,9 +7,10 @@ readout must start from the exact prefix of all earlier ranks:
 forward   A. local totals (A_tot [N,S], B_tot [N,S,D]) of this slice
           -> all_gather -> prefix = sum of ranks < r (fixed order, float64)
           B. fused readout of the slice starting from that prefix
-backward  A. local final-state gradient totals (gA_tot, gB_tot) given the prefix
+backward  A. the slice's gradients with a zero suffix at its end, and their
+             start-state totals (gA_tot, gB_tot), given the prefix
           -> all_gather -> suffix = sum of ranks > r
-          B. fused backward of the slice with that suffix as incoming gradient
+          B. that suffix's (linear) share added to the gradients
 
 The exchange is one all_gather of N*(S + S*D) float32 per rank and direction
 (266 KB at N=8, S=128, D=64).  The compute backend defaults to the CUDA
@@ -29,13 +30,15 @@ class CudaShardBackend:
         return ops.state_from_prefill(K, V, planes_T, L, P, scale)
 
     def fwd(self, Q, K, V, planes_T, L, P, eps, scale, A0, B0):
-        return ops.fwd_qkv(Q, K, V, planes_T, L, P, eps, scale, A0, B0)
+        """(out, saved): saved = chunk states kept for the backward (None when unused)."""
+        return ops.fwd_qkv(Q, K, V, planes_T, L, P, eps, scale, A0, B0, save=True)
 
-    def bwd_totals(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0):
-        return ops.bwd_totals(Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0)
+    def bwd_local(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, saved):
+        """(gA_tot, gB_tot, handle) of this shard."""
+        return ops.bwd_local(Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, saved)
 
-    def bwd(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, gA, gB):
-        return ops.bwd_qkv(Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, gA, gB)
+    def bwd_finish(self, handle, gA, gB):
+        return ops.bwd_finish(handle, gA, gB)
 
 
 def _pack(A, B):
@@ -71,19 +74,19 @@ class ShardedRaceFn(torch.autograd.Function):
         scale = ops.default_logit_scale(D) if logit_scale is None else float(logit_scale)
         A_tot, B_tot = backend.fwd_totals(Kn, Vn, planes_T, L, P, scale)
         A0, B0 = exchange(A_tot, B_tot, group, "prefix")
-        out = backend.fwd(Qn, Kn, Vn, planes_T, L, P, eps, scale, A0, B0)
-        ctx.save_for_backward(Qn, Kn, Vn, planes_T, A0, B0)
+        out, saved = backend.fwd(Qn, Kn, Vn, planes_T, L, P, eps, scale, A0, B0)
+        ctx.save_for_backward(Qn, Kn, Vn, planes_T, A0, B0, saved)
         ctx.cfg = (L, P, eps, scale, group, backend, shape)
         return out.reshape(shape)
 
     @staticmethod
     def backward(ctx, dO):
-        Qn, Kn, Vn, planes_T, A0, B0 = ctx.saved_tensors
+        Qn, Kn, Vn, planes_T, A0, B0, saved = ctx.saved_tensors
         L, P, eps, scale, group, backend, shape = ctx.cfg
         dOn = dO.reshape(Qn.shape).contiguous()
-        gA_tot, gB_tot = backend.bwd_totals(Qn, Kn, Vn, dOn, planes_T, L, P, eps, scale, A0, B0)
+        gA_tot, gB_tot, handle = backend.bwd_local(Qn, Kn, Vn, dOn, planes_T, L, P, eps, scale, A0, B0, saved)
         gA, gB = exchange(gA_tot, gB_tot, group, "suffix")
-        dQ, dK, dV = backend.bwd(Qn, Kn, Vn, dOn, planes_T, L, P, eps, scale, A0, B0, gA, gB)
+        dQ, dK, dV = backend.bwd_finish(handle, gA, gB)
         return dQ.reshape(shape), dK.reshape(shape), dV.reshape(shape), None, None, None, None, None, None, None
 
 

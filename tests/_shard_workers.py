@@ -16,7 +16,7 @@ from oracle import oracle as O
 
 
 class OracleShardBackend:
-    """Same four methods as sharded.CudaShardBackend, computed by the CPU oracle."""
+    """Same methods as sharded.CudaShardBackend, computed by the CPU oracle."""
 
     @staticmethod
     def _t(x):
@@ -29,14 +29,14 @@ class OracleShardBackend:
 
     def fwd(self, Q, K, V, planes_T, L, P, eps, scale, A0, B0):
         out, _, _ = O.race_qkv_fwd(Q, K, V, planes_T, L, P, eps, scale, A0, B0)
-        return self._t(out)
+        return self._t(out), None
 
-    def bwd_totals(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0):
+    def bwd_local(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, saved):
         _, _, _, gA, gB = O.race_qkv_bwd(Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0)
-        return self._t(gA), self._t(gB)
+        return self._t(gA), self._t(gB), (Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0)
 
-    def bwd(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, gA, gB):
-        dQ, dK, dV, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, gA, gB)
+    def bwd_finish(self, handle, gA, gB):
+        dQ, dK, dV, _, _ = O.race_qkv_bwd(*handle, gA, gB)
         return self._t(dQ), self._t(dK), self._t(dV)
 
 

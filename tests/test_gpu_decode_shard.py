@@ -50,8 +50,9 @@ def test_state_from_prefill_with_initial_state():
 @pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
 def test_sequence_shard_phases_emulated(world, dtype, tol):
-    """W ranks emulated on one GPU: phase A totals -> host prefix/suffix sums ->
-    phase B; the concatenation equals the single-run result (oracle)."""
+    """W ranks emulated on one GPU: forward phase A totals -> host prefix sums ->
+    forward phase B (keeping chunk states) ; backward local half -> host suffix sums
+    -> finishing half; the concatenation equals the single-run result (oracle)."""
     import race_attention_b200 as rb
     N, T, D, L, P = 4, 333, 64, 8, 4
     g = torch.Generator().manual_seed(world)
@@ -67,15 +68,16 @@ def test_sequence_shard_phases_emulated(world, dtype, tol):
         A = sum((tots[i][0].double() for i in range(r)), torch.zeros_like(tots[0][0], dtype=torch.float64))
         B = sum((tots[i][1].double() for i in range(r)), torch.zeros_like(tots[0][1], dtype=torch.float64))
         pref.append((A.float(), B.float()))
-    outs = [rb.ops.fwd_qkv(c(Q, r), c(K, r), c(V, r), pc, L, P, A0=pref[r][0], B0=pref[r][1]) for r in range(world)]
-    gt = [rb.ops.bwd_totals(c(Q, r), c(K, r), c(V, r), c(dO, r), pc, L, P, A0=pref[r][0], B0=pref[r][1])
+    fw = [rb.ops.fwd_qkv(c(Q, r), c(K, r), c(V, r), pc, L, P, A0=pref[r][0], B0=pref[r][1], save=True)
           for r in range(world)]
+    outs = [f[0] for f in fw]
+    gt = [rb.ops.bwd_local(c(Q, r), c(K, r), c(V, r), c(dO, r), pc, L, P, A0=pref[r][0], B0=pref[r][1],
+                           saved=fw[r][1]) for r in range(world)]
     grads = []
     for r in range(world):
         gA = sum((gt[i][0].double() for i in range(r + 1, world)), torch.zeros_like(gt[0][0], dtype=torch.float64))
         gB = sum((gt[i][1].double() for i in range(r + 1, world)), torch.zeros_like(gt[0][1], dtype=torch.float64))
-        grads.append(rb.ops.bwd_qkv(c(Q, r), c(K, r), c(V, r), c(dO, r), pc, L, P, A0=pref[r][0], B0=pref[r][1],
-                                    gA=gA.float(), gB=gB.float()))
+        grads.append(rb.ops.bwd_finish(gt[r][2], gA.float(), gB.float()))
     out_r, _, _ = O.race_qkv_fwd(Q, K, V, planes, L, P)
     dQ_r, dK_r, dV_r, _, _ = O.race_qkv_bwd(Q, K, V, dO, planes, L, P)
     cat = lambda xs: torch.cat([x.float().cpu() for x in xs], 1)  # noqa: E731
