@@ -55,6 +55,7 @@ extern "C" {
 #define RACE_OP_BWD_QKV 3
 #define RACE_OP_STATE 4
 #define RACE_OP_BWD_SPLIT 5  /* race_bwd_local + race_bwd_finish (one workspace) */
+#define RACE_OP_FWD_SPLIT 6  /* race_fwd_local + race_fwd_finish (one workspace) */
 
 /* Library ABI version (bumped on any signature change). */
 int race_abi_version(void);
@@ -199,14 +200,25 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype,
 
 /* ---- sequence-sharded phases (one rank's contiguous slice of T) ---------- */
 
-/* Forward phase A: this shard's state totals (== race_state_from_prefill with
- * A0 = B0 = NULL).  Forward phase B is race_fwd_qkv with A0/B0 = the sum of
- * the totals of all earlier shards. */
-int race_fwd_sharded_phaseA(const void *K, const void *V, int dtype,
-                            const float *planes_T, float *A_tot, float *B_tot,
-                            int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
-                            float logit_scale,
-                            void *workspace, size_t workspace_bytes, void *stream);
+/* Forward of a shard in two calls on ONE workspace (RACE_OP_FWD_SPLIT size):
+ * race_fwd_local writes this shard's state totals A_tot[N,S], B_tot[N,S,D]
+ * (what race_state_from_prefill with A0 = B0 = NULL writes) and keeps its
+ * segment prefixes in the workspace; race_fwd_finish then writes `out`
+ * given A0/B0 = the sum of the totals of all earlier shards (NULL: none),
+ * without recomputing them.  `saved` (optional, race_saved_bytes) receives
+ * the chunk states race_bwd_local/race_bwd_finish can reuse, as
+ * race_fwd_qkv_save does.  Same K/V (and workspace) to both calls. */
+int race_fwd_local(const void *K, const void *V, int dtype,
+                   const float *planes_T, float *A_tot, float *B_tot,
+                   int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                   float logit_scale,
+                   void *workspace, size_t workspace_bytes, void *stream);
+int race_fwd_finish(const void *Q, const void *K, const void *V, int dtype,
+                    const float *planes_T, void *out, void *saved, size_t saved_bytes,
+                    const float *A0, const float *B0,
+                    int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                    float eps, float logit_scale,
+                    void *workspace, size_t workspace_bytes, void *stream);
 
 /* Backward of a shard in two calls on ONE workspace (RACE_OP_BWD_SPLIT size):
  * race_bwd_local writes this shard's gradient totals for its start state

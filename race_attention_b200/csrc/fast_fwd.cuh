@@ -56,6 +56,8 @@ struct FwdArgs {
   float *chunkA;           // states pass of the totals kernel, or a forward that saves them for the
   __nv_bfloat16 *chunkB;   // backward: [N, nchunks, S] A + eps and [N, nchunks, S, 64] bf16 B at each
                            // chunk start (nullptr: not wanted)
+  const float *seedA;      // readout of a sequence shard: the earlier shards' state ([N,S], [N,S,64])
+  const float *seedB;      // added to every segment's prefix (nullptr: none)
   int *err;
 };
 
@@ -394,12 +396,18 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       }
     }
     // the A arrays hold A + eps (the chunk recurrence adds counts, so the offset carries)
-    for (int s = threadIdx.x; s < S; s += NEPI_T) sA0[s] = state0[s] + a.eps;
+    for (int s = threadIdx.x; s < S; s += NEPI_T)
+      sA0[s] = state0[s] + a.eps + (a.seedA != nullptr ? a.seedA[(size_t)n * S + s] : 0.f);
     for (int g = 0; g < NG; ++g) {
       float v[16];
       const float *src = state0 + S + (size_t)(g * GB + t) * HD + 16 * hq;
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = src[i];
+      if (a.seedB != nullptr) {
+        const float *sd = a.seedB + ((size_t)n * S + g * GB + t) * HD + 16 * hq;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] += sd[i];
+      }
       tc::tmem_st16(tmem + lane_off + T_B + 64 * g + 16 * hq, v);
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.bst + g * TILE, t, 2 * hq + ch, v + 8 * ch);

@@ -397,16 +397,18 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
   a.out = nullptr;
   a.chunkA = nullptr;
   a.chunkB = nullptr;
+  a.seedA = a.seedB = nullptr;
   a.err = at<int>(ws, pl.status_off);
   return RACE_OK;
 }
 
-int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, const float *A0, const float *B0,
-                         float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
-                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, size_t rec_off = 0) {
+// Plan, kernel arguments and K/V tensor maps of the forward kernels.
+int fast_prepare(const void *K, const void *V, const float *planes_T, int64_t N, int64_t T, int64_t L, float eps,
+                 float scale, void *ws, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, fh::Plan &pl,
+                 size_t rec_off = 0) {
   const int64_t S = 16 * L;
   if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
-  fh::Plan pl = fh::plan(N, T, S, fh::sm_count());
+  pl = fh::plan(N, T, S, fh::sm_count());
   if (rec_off) pl.rec_off = rec_off;
   fast_args(a, pl, N, T, L, eps, scale, planes_T, ws);
   if (!fh::make_map(&mK, K, N, T))
@@ -415,6 +417,15 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
   if (!fh::make_map(&mV, V, N, T))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(V %p, N=%lld, T=%lld) failed: CUresult %d", V, (long long)N,
                 (long long)T, fh::last_encode_status());
+  return RACE_OK;
+}
+
+int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, const float *A0, const float *B0,
+                         float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
+                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, size_t rec_off = 0) {
+  const int64_t S = 16 * L;
+  fh::Plan pl;
+  RACE_TRY(fast_prepare(K, V, planes_T, N, T, L, eps, scale, ws, a, mK, mV, pl, rec_off));
   cudaError_t e = cudaMemsetAsync(at<int>(ws, pl.status_off), 0, sizeof(int), s);
   if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   const fk::TotSmem ts = fk::tot_smem_plan(a.ngroups, a.LP);
@@ -433,12 +444,22 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
   return rc;
 }
 
+// finish: the readout half of a sequence shard's split forward.  The workspace
+// holds the segment prefixes race_fwd_local left (unseeded); A0/B0, the
+// earlier shards' state, are added to each as the readout loads it.
 int fast_forward(const void *Q, const void *K, const void *V, const float *planes_T, void *out, const float *A0,
                  const float *B0, float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale,
-                 void *ws, cudaStream_t s, void *saved = nullptr) {
+                 void *ws, cudaStream_t s, void *saved = nullptr, bool finish = false) {
   fk::FwdArgs a;
   CUtensorMap mQ, mK, mV;
-  RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV));
+  if (finish) {
+    fh::Plan pl;
+    RACE_TRY(fast_prepare(K, V, planes_T, N, T, L, eps, scale, ws, a, mK, mV, pl));
+    a.seedA = A0;
+    a.seedB = B0;
+  } else {
+    RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV));
+  }
   if (!fh::make_map(&mQ, Q, N, T))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(Q) failed: CUresult %d", fh::last_encode_status());
   a.out = static_cast<__nv_bfloat16 *>(out);
@@ -665,7 +686,8 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int
   (void)chunk;
   RACE_NONNULL(bytes);
   *bytes = 0;
-  if (op == RACE_OP_FWD_QKV || op == RACE_OP_BWD_QKV || op == RACE_OP_STATE || op == RACE_OP_BWD_TOTALS) {
+  if (op == RACE_OP_FWD_QKV || op == RACE_OP_BWD_QKV || op == RACE_OP_STATE || op == RACE_OP_BWD_SPLIT ||
+      op == RACE_OP_FWD_SPLIT) {
     RACE_TRY(check_dtype(dtype));
     RACE_TRY(check_lp(L, P, &S));
   } else if (op != RACE_OP_FWD_PROBS && op != RACE_OP_BWD_PROBS) {
@@ -681,6 +703,11 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int
   else if (op == RACE_OP_BWD_SPLIT)
     *bytes = std::max(generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total,
                       generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total);
+  else if (op == RACE_OP_FWD_SPLIT && fh::eligible(dtype, D, L, P))
+    *bytes = fh::fwd_workspace_bytes(N, T, S);
+  else if (op == RACE_OP_FWD_SPLIT)
+    *bytes = std::max(generic_layout(RACE_OP_STATE, N, T, S, D).total,
+                      generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total);
   else
     *bytes = generic_layout(op, N, T, S, D).total;
   return ok();
@@ -935,11 +962,40 @@ int race_state_from_prefill(const void *K, const void *V, int dtype, const float
   return ok();
 }
 
-int race_fwd_sharded_phaseA(const void *K, const void *V, int dtype, const float *planes_T, float *A_tot,
-                            float *B_tot, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float logit_scale,
-                            void *workspace, size_t workspace_bytes, void *stream) {
+int race_fwd_local(const void *K, const void *V, int dtype, const float *planes_T, float *A_tot, float *B_tot,
+                   int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float logit_scale, void *workspace,
+                   size_t workspace_bytes, void *stream) {
+  // the tcgen05 path keeps its (unseeded) segment prefixes in the workspace for
+  // race_fwd_finish; the generic path recomputes everything there
   return race_state_from_prefill(K, V, dtype, planes_T, nullptr, nullptr, A_tot, B_tot, N, T, D, L, P, logit_scale,
                                  workspace, workspace_bytes, stream);
+}
+
+int race_fwd_finish(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
+                    void *saved, size_t saved_bytes, const float *A0, const float *B0, int64_t N, int64_t T,
+                    int64_t D, int64_t L, int64_t P, float eps, float logit_scale, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(out);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  if (fh::eligible(dtype, D, L, P)) {
+    RACE_TRY(check_ws(workspace, workspace_bytes, fh::fwd_workspace_bytes(N, T, S)));
+    RACE_TRY(check_fast_ptrs({Q, K, V, out}));
+    if (saved_bytes && saved_bytes < fh::saved_plan(N, T, S).total)
+      return fail(RACE_ERR_WORKSPACE, "saved-state buffer too small");
+    RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, nullptr, nullptr, N, T, L, eps, logit_scale, workspace,
+                          as_stream(stream), saved_bytes ? saved : nullptr, true));
+    return ok();
+  }
+  if (saved_bytes) return fail(RACE_ERR_UNSUPPORTED, "saved chunk states need the tcgen05 path");
+  return race_fwd_qkv(Q, K, V, dtype, planes_T, out, A0, B0, nullptr, nullptr, N, T, D, L, P, eps, logit_scale,
+                      workspace, workspace_bytes, stream);
 }
 
 int race_bwd_local(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,

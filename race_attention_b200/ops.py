@@ -291,6 +291,49 @@ def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None)
     return A, B
 
 
+class FwdSplit:
+    """What race_fwd_local leaves for race_fwd_finish: K, V and the workspace."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+
+
+def fwd_local(K, V, planes_T, L, P, logit_scale=None):
+    """First half of a shard's forward: (A_tot[N,S], B_tot[N,S,D], handle) -- this shard's state
+    totals; the handle (holding its segment prefixes) goes to fwd_finish."""
+    dev, K, _, V, planes_T, N, T, D, S, scale = _qkv_common(K, K, V, planes_T, L, P, logit_scale)
+    A = torch.empty((N, S), dtype=torch.float32, device=dev)
+    B = torch.empty((N, S, D), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_FWD_SPLIT, N, T, S, D, L, P, _dtype_code(K), dev)
+        _lib.check(lib.race_fwd_local(_ptr(K), _ptr(V), _dtype_code(K), _ptr(planes_T), _ptr(A), _ptr(B), N, T, D,
+                                      L, P, scale, _ptr(ws), nb, _stream(dev)), "race_fwd_local")
+        if fast_path(K.dtype, D, L, P):
+            _check_status(ws, "race_fwd_local")
+    return A, B, FwdSplit(K=K, V=V, planes_T=planes_T, L=L, P=P, scale=scale, ws=ws, nb=nb, dev=dev)
+
+
+def fwd_finish(h, Q, A0=None, B0=None, eps=1e-6, save=False):
+    """Second half: out (and, with save=True, the chunk-state buffer for bwd_local/bwd_qkv, None when
+    unused) given A0/B0 = the sum of the totals of all earlier shards."""
+    dev, Q, K, V, planes_T, N, T, D, S, _ = _qkv_common(Q, h.K, h.V, h.planes_T, h.L, h.P, h.scale)
+    A0, B0 = _opt_state(A0, B0, N, S, D, dev)
+    out = torch.empty_like(Q)
+    lib = _lib.load()
+    saved = None
+    with torch.cuda.device(dev):
+        sb = saved_bytes(N, T, D, h.L, h.P, Q.dtype) if save else 0
+        if sb:
+            saved = torch.empty(sb, dtype=torch.uint8, device=dev)
+        _lib.check(lib.race_fwd_finish(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out),
+                                       _ptr(saved), sb, _ptr(A0), _ptr(B0), N, T, D, h.L, h.P, float(eps), h.scale,
+                                       _ptr(h.ws), h.nb, _stream(dev)), "race_fwd_finish")
+        if fast_path(Q.dtype, D, h.L, h.P):
+            _check_status(h.ws, "race_fwd_finish")
+    return (out, saved) if save else out
+
+
 class BwdSplit:
     """What race_bwd_local leaves for race_bwd_finish: the inputs and the workspace."""
 

@@ -4,9 +4,10 @@ Rank r holds the contiguous token slice [r*T/W, (r+1)*T/W) of every stream.
 The normaliser 1/(A_t + eps) is nonlinear in the running bucket mass, so the
 readout must start from the exact prefix of all earlier ranks:
 
-forward   A. local totals (A_tot [N,S], B_tot [N,S,D]) of this slice
+forward   A. local totals (A_tot [N,S], B_tot [N,S,D]) of this slice; its
+             segment prefixes stay in the workspace
           -> all_gather -> prefix = sum of ranks < r (fixed order, float64)
-          B. fused readout of the slice starting from that prefix
+          B. fused readout of the slice, that prefix added to every segment's
 backward  A. the slice's gradients with a zero suffix at its end, and their
              start-state totals (gA_tot, gB_tot), given the prefix
           -> all_gather -> suffix = sum of ranks > r
@@ -26,12 +27,13 @@ from . import ops
 
 
 class CudaShardBackend:
-    def fwd_totals(self, K, V, planes_T, L, P, scale):
-        return ops.state_from_prefill(K, V, planes_T, L, P, scale)
+    def fwd_local(self, K, V, planes_T, L, P, scale):
+        """(A_tot, B_tot, handle) of this shard."""
+        return ops.fwd_local(K, V, planes_T, L, P, scale)
 
-    def fwd(self, Q, K, V, planes_T, L, P, eps, scale, A0, B0):
+    def fwd_finish(self, handle, Q, eps, A0, B0):
         """(out, saved): saved = chunk states kept for the backward (None when unused)."""
-        return ops.fwd_qkv(Q, K, V, planes_T, L, P, eps, scale, A0, B0, save=True)
+        return ops.fwd_finish(handle, Q, A0, B0, eps, save=True)
 
     def bwd_local(self, Q, K, V, dO, planes_T, L, P, eps, scale, A0, B0, saved):
         """(gA_tot, gB_tot, handle) of this shard."""
@@ -72,9 +74,10 @@ class ShardedRaceFn(torch.autograd.Function):
         D = shape[-1]
         Qn, Kn, Vn = (x.reshape(-1, x.shape[-2], D) for x in (Q, K, V))
         scale = ops.default_logit_scale(D) if logit_scale is None else float(logit_scale)
-        A_tot, B_tot = backend.fwd_totals(Kn, Vn, planes_T, L, P, scale)
+        A_tot, B_tot, handle = backend.fwd_local(Kn, Vn, planes_T, L, P, scale)
         A0, B0 = exchange(A_tot, B_tot, group, "prefix")
-        out, saved = backend.fwd(Qn, Kn, Vn, planes_T, L, P, eps, scale, A0, B0)
+        out, saved = backend.fwd_finish(handle, Qn, eps, A0, B0)
+        del handle
         ctx.save_for_backward(Qn, Kn, Vn, planes_T, A0, B0, saved)
         ctx.cfg = (L, P, eps, scale, group, backend, shape)
         return out.reshape(shape)

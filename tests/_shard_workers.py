@@ -22,12 +22,13 @@ class OracleShardBackend:
     def _t(x):
         return torch.from_numpy(np.ascontiguousarray(x)).float()
 
-    def fwd_totals(self, K, V, planes_T, L, P, scale):
+    def fwd_local(self, K, V, planes_T, L, P, scale):
         pk = O.soft_hash(K, planes_T, L, P, scale)
         _, A, B = O.race_fwd(pk, pk, V)
-        return self._t(A), self._t(B)
+        return self._t(A), self._t(B), (K, V, planes_T, L, P, scale)
 
-    def fwd(self, Q, K, V, planes_T, L, P, eps, scale, A0, B0):
+    def fwd_finish(self, handle, Q, eps, A0, B0):
+        K, V, planes_T, L, P, scale = handle
         out, _, _ = O.race_qkv_fwd(Q, K, V, planes_T, L, P, eps, scale, A0, B0)
         return self._t(out), None
 

@@ -50,9 +50,10 @@ def test_state_from_prefill_with_initial_state():
 @pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 2e-2)])
 def test_sequence_shard_phases_emulated(world, dtype, tol):
-    """W ranks emulated on one GPU: forward phase A totals -> host prefix sums ->
-    forward phase B (keeping chunk states) ; backward local half -> host suffix sums
-    -> finishing half; the concatenation equals the single-run result (oracle)."""
+    """W ranks emulated on one GPU: forward local half (totals) -> host prefix sums ->
+    finishing half (readout, keeping chunk states) ; backward local half -> host
+    suffix sums -> finishing half; the concatenation equals the single-run result
+    (oracle)."""
     import race_attention_b200 as rb
     N, T, D, L, P = 4, 333, 64, 8, 4
     g = torch.Generator().manual_seed(world)
@@ -62,13 +63,14 @@ def test_sequence_shard_phases_emulated(world, dtype, tol):
     bounds = np.linspace(0, T, world + 1).astype(int)
     sl = [slice(bounds[r], bounds[r + 1]) for r in range(world)]
     c = lambda x, r: x[:, sl[r]].cuda().contiguous()  # noqa: E731
-    tots = [rb.ops.state_from_prefill(c(K, r), c(V, r), pc, L, P) for r in range(world)]
+    tots = [rb.ops.fwd_local(c(K, r), c(V, r), pc, L, P) for r in range(world)]
     pref = []
     for r in range(world):
         A = sum((tots[i][0].double() for i in range(r)), torch.zeros_like(tots[0][0], dtype=torch.float64))
         B = sum((tots[i][1].double() for i in range(r)), torch.zeros_like(tots[0][1], dtype=torch.float64))
         pref.append((A.float(), B.float()))
-    fw = [rb.ops.fwd_qkv(c(Q, r), c(K, r), c(V, r), pc, L, P, A0=pref[r][0], B0=pref[r][1], save=True)
+    # rank 0 has no earlier shard: no prefix at all
+    fw = [rb.ops.fwd_finish(tots[r][2], c(Q, r), *(pref[r] if r else (None, None)), save=True)
           for r in range(world)]
     outs = [f[0] for f in fw]
     gt = [rb.ops.bwd_local(c(Q, r), c(K, r), c(V, r), c(dO, r), pc, L, P, A0=pref[r][0], B0=pref[r][1],
