@@ -292,6 +292,8 @@ def run_ours(args, cfg):
     # e2e: same step through the public API with host (pinned) buffers, copies inside the timed region
     e2e = None
     if not args.no_e2e:
+        for t in (qv, kv, vv):
+            t.grad = None
         e2e = run_e2e(layer, cfg, dev, world, barrier, args, planes)
 
     cpu = None
@@ -318,24 +320,35 @@ def run_ours(args, cfg):
 # outputs, D*e each; chunk-state records are implementation traffic and excluded),
 # and the MMA work it issues per 128-token chunk of one stream (fp32-accumulated
 # bf16 FMAs, from the kernels' MMA schedules for S = 16L buckets, D = 64).
-KERNEL_IO = {"fwd_totals_kernel": 2, "fwd_readout_kernel": 4, "bwd_fwd_kernel": 5, "bwd_rev_kernel": 6}
+# Algorithmic bytes of each tcgen05 kernel, in units of D*e per token-head: the
+# tensors of the layer's algorithmic set (Q, K, V, O; Q, K, V, dO, dQ, dK, dV =
+# 11 D e) that the kernel reads or writes.  Chunk states, the backward's d proj
+# intermediates and recompute re-reads are implementation traffic (the ncu
+# figure shows them).
+KERNEL_IO = {"fwd_totals_kernel": 2,      # K, V
+             "fwd_readout_kernel": 4,     # Q, K, V -> O
+             "bwd_rev_kernel": 4,         # Q, K, V, dO
+             "bwd_fix_kernel": 5}         # K, V -> dQ, dK, dV
 
 
 def mma_fma_per_chunk(kernel, S, D=64, C=128):
+    """Multiply-adds the kernel issues to the tensor pipe per 128-token chunk (its
+    MMA list; the chunked form's masked products included)."""
     LP = S // 4
     if kernel == "fwd_totals_kernel":
         return C * D * LP + (S // 128) * (128 * D * C + 128 * 16 * C)
     if kernel == "fwd_readout_kernel":
         return 2 * C * D * LP + (S // 128) * (C * 128 * C + C * C * 128 + C * D * 128 + C * D * C + 128 * D * C)
-    g = S // 64  # 64-bucket groups of the backward walks
-    proj = 2 * C * 16 * D
-    if kernel == "bwd_fwd_kernel":
-        per = proj + C * 64 * C + (C * 64 * D + C * 64 * C) + 64 * D * C + 64 * D * C + 64 * 16 * C
-        return C * C * D + g * per + C * D * LP
     if kernel == "bwd_rev_kernel":
-        per = (proj + C * 64 * C + (C * 64 * D + C * 64 * C) + C * C * 64 + (C * 64 * D + C * 64 * C)
-               + 64 * D * C + C * 64 * C + 64 * 16 * C + C * D * 64 + C * D * C)
-        return C * C * D + g * per + C * D * LP
+        # per 64-bucket group: proj of K and Q (planes hi + lo), Apref, G, Q2, dpk (three
+        # products), gB, gA, dV (two products); per chunk: P1 = dO V^T
+        proj = 2 * 2 * C * 16 * D
+        per = (proj + C * 64 * C + (C * 64 * D + C * 64 * C) + C * C * 64
+               + (C * 64 * D + C * 64 * C + C * 64 * C) + 64 * D * C + 64 * 16 * C + (C * D * 64 + C * D * C))
+        return C * C * D + (S // 64) * per
+    if kernel == "bwd_fix_kernel":
+        # proj (planes hi + lo), V gB^T, dQ (2 passes), dK (3 passes), dV = Pk gB
+        return 2 * C * LP * D + C * S * D + 2 * C * D * LP + 3 * C * D * LP + C * D * S
     return 0
 
 
@@ -399,32 +412,74 @@ def roofline(kernels, cfg, ms, fwd_ms, bwd_ms):
 
 
 def run_e2e(layer, cfg, dev, world, barrier, args, planes):
+    """The step through the public autograd API with every step's inputs copied in
+    from pinned host memory and its results (out, dQ, dK, dV) copied back, as a
+    training loop with a prefetching loader runs it: step i+1's inputs go up on one
+    copy stream and step i-1's results come down on another while step i computes
+    (two device input slots; each copy waits only for what it overwrites or reads)."""
     B, H, T, D, L, P, dtype, scale = cfg
-    steps = max(1, min(3, args.steps))
+    steps = max(4, min(8, 2 * args.steps))
     host_in = [torch.empty((B, H, T, D), dtype=dtype, pin_memory=True) for _ in range(4)]
     host_out = [torch.empty((B, H, T, D), dtype=dtype, pin_memory=True) for _ in range(4)]
     g = torch.Generator().manual_seed(7)
     for h in host_in:
         h.copy_(torch.randn(B, H, T, D, generator=g).mul_(scale).to(dtype))
     nbytes = host_in[0].numel() * host_in[0].element_size()
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    slots = [[torch.empty((B, H, T, D), dtype=dtype, device=dev) for _ in range(4)] for _ in range(2)]
+    freed = [None, None]  # per slot: the event after the last compute that read it
 
-    def step():
-        q, k, v, do = (h.to(dev, non_blocking=True) for h in host_in)
-        for t in (q, k, v):
-            t.requires_grad_(True)
-        out = layer(q, k, v)
+    def h2d(i):
+        j = i % 2
+        with torch.cuda.stream(s_in):
+            if freed[j] is not None:
+                s_in.wait_event(freed[j])
+            for d, h in zip(slots[j], host_in):
+                d.copy_(h, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+        return ev
+
+    def compute(i, ev_in):
+        j = i % 2
+        main.wait_event(ev_in)
+        q, k, v, do = slots[j]
+        leaves = [x.detach().requires_grad_(True) for x in (q, k, v)]
+        out = layer(*leaves)
         out.backward(do)
-        for src, dst in zip((out, q.grad, k.grad, v.grad), host_out):
-            dst.copy_(src.detach(), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(main)
+        freed[j] = ev
+        return (out.detach(), leaves[0].grad, leaves[1].grad, leaves[2].grad), ev
 
-    step()
+    def d2h(res, ev):
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev)
+            for src, dst in zip(res, host_out):
+                dst.copy_(src, non_blocking=True)
+                src.record_stream(s_out)
+
+    def run(n):
+        s_in.wait_stream(main)
+        s_out.wait_stream(main)
+        ev_in = h2d(0)
+        for i in range(n):
+            nxt = h2d(i + 1) if i + 1 < n else None
+            res, ev = compute(i, ev_in)
+            d2h(res, ev)
+            del res
+            ev_in = nxt
+        main.wait_stream(s_out)
+        main.wait_stream(s_in)
+
+    run(2)
     torch.cuda.synchronize()
     barrier()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
+    s.record(main)
+    run(steps)
+    e.record(main)
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / steps
     if world > 1:
@@ -434,7 +489,8 @@ def run_e2e(layer, cfg, dev, world, barrier, args, planes):
         ms = float(t.item())
     return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * nbytes,
             "d2h_bytes_per_step": 4 * nbytes, "ms_per_step": ms, "steps": steps,
-            "api": "race_attention_b200.race_causal (autograd) from pinned host tensors"}
+            "api": "race_attention_b200.race_causal (autograd) from pinned host tensors; next step's H2D and "
+                   "previous step's D2H on copy streams overlap this step's compute (fill and drain timed)"}
 
 
 if __name__ == "__main__":

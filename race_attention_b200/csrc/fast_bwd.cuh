@@ -53,30 +53,45 @@ struct BwdArgs {
   int *err;
 };
 
-// d proj of one table: softmax backward over the corners, through sum_p, tanh
-__device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g16, const float *th4, float scale,
-                                                float *out4) {
-  float c = 0.f;
+// d proj of one table from the gradient g16 of its 16 corner probabilities.
+// p_r = prod_b f_b(r) with f_b = q_b or 1 - q_b by bit (3-b) of r, so
+//   dL/dz_b = q_b (1 - q_b) dL/dq_b = sum_{r: bit set} g_r p_r - q_b sum_r g_r p_r
+// (the softmax backward over the corner logits, sum_r sign_b(r) p_r (g_r - c),
+// written with sum_{bit set} p_r = q_b), then z_b = 2 scale tanh(proj_b).
+// The bit-set sums come from one pairwise-sum tree.
+__device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g16, const float *q4, const float *th4,
+                                                float scale, float *out4) {
+  float gp[16];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) c = fmaf(p16[r], g16[r], c);
-  float dl[16], all = 0.f;
+  for (int r = 0; r < 16; ++r) gp[r] = p16[r] * g16[r];
+  float a[8], s3 = 0.f;  // plane 3: bit 0
 #pragma unroll
-  for (int r = 0; r < 16; ++r) {
-    dl[r] = p16[r] * (g16[r] - c);
-    all += dl[r];
+  for (int i = 0; i < 8; ++i) {
+    a[i] = gp[2 * i] + gp[2 * i + 1];
+    s3 += gp[2 * i + 1];
   }
+  float b[4], s2 = 0.f;  // plane 2: bit 1
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    float set = 0.f;
-#pragma unroll
-    for (int r = 0; r < 16; ++r)
-      if ((r >> (3 - p)) & 1) set += dl[r];
-    out4[p] = (2.f * set - all) * scale * (1.f - th4[p] * th4[p]);
+  for (int j = 0; j < 4; ++j) {
+    b[j] = a[2 * j] + a[2 * j + 1];
+    s2 += a[2 * j + 1];
   }
+  const float s1 = b[1] + b[3];  // plane 1: bit 2
+  const float s0 = b[2] + b[3];  // plane 0: bit 3
+  const float c = (b[0] + b[1]) + s0;
+  const float set[4] = {s0, s1, s2, s3};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) out4[p] = fmaf(-q4[p], c, set[p]) * (2.f * scale) * fmaf(-th4[p], th4[p], 1.f);
 }
 
-// x rounded to bf16 (round to nearest even, as the tile stores) and back
-__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+// bf16 roundings (to nearest even, as the MMA operands are stored) of two values
+// with one packed conversion
+__device__ __forceinline__ void bf16r2(float a, float b, float &ra, float &rb) {
+  const uint32_t p = tc::pack_bf16(a, b);
+  ra = __uint_as_float(p << 16);
+  rb = __uint_as_float(p & 0xffff0000u);
+}
 
 __device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float *v) {
   uint4 w;
@@ -89,11 +104,13 @@ __device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float
 
 // --------------------------------------------------------------------------
 struct BwdSmem {
-  uint32_t q, k, v, o, p1m, tril, planes, plo, pk, w, da, bst, gbst, diag, a0, ga, bars, total;
+  uint32_t q, k, v, o, p1m, tril, planes, plo, pk, w, da, bst, gbst, ones, diag, a0, ga, bars, total;
 };
 
 // planes and plo: bf16 planes and their residuals planes - bf16(planes), so that the
-// projections are exact to ~2^-17; diag: the fp32 diagonal of P1 = dO V^T.
+// projections are exact to ~2^-17; tril and p1m: strictly lower triangles (tau < t),
+// the diagonal terms being added in fp32 by the epilogue from diag, the fp32
+// diagonal of P1 = dO V^T; ones: the B operand of the gA column sums.
 __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   BwdSmem m;
   uint32_t o = 0;
@@ -110,6 +127,7 @@ __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   m.da = o; o += TILE;  // must follow w: [w | da] is the 2-block Q2m tile
   m.bst = o; o += GW * 128;
   m.gbst = o; o += GW * 128;
+  m.ones = o; o += 16 * C * 2;  // K-major [16 x 128] of ones: the B of gA += dA^T 1
   m.diag = o; o += C * 4;
   m.a0 = o; o += (uint32_t)align_up((size_t)S * 4, 128);
   m.ga = o; o += 2 * GW * 4;  // two buffers (group parity)
@@ -140,8 +158,10 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 //            {DA} dpk += tril^T dA -> [DPK] ; gA += dA^T 1 ; dV (+)= Pk gBst -> [D2] ;
 //            proj of the next group -> [PROJ] ; {Q2} dV += Q2m dO ;
 // (critical MMAs first in each handoff: the tensor pipe runs them in order)
-//            chunk end: dK = dprojK planes -> [OUT] ; next chunk's proj(0) ;
+//            chunk end: [OUT] ; next chunk's proj(0) ;
 //            V/dO/Bst refill once every reader completed.
+// P1m and tril are strictly lower triangular: the tau = t terms of Apref, G and
+// dpk (pk_t, P1[t][t] pk_t, dA_t + P1[t][t] W_t) are added by the epilogue in fp32.
 //   epilogue: [PROJ] Pk, plane sigmoids, gBst and gA suffix copies {PK} ;
 //            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK, [D2] Q2m {Q2} ;
 //            chunk end: [OUT] dK, dV rows {OUTFREE}.
@@ -195,7 +215,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     const uint32_t id_mm = tc::idesc_bf16(C, GW, true, true);
     const uint32_t id_q2 = tc::idesc_bf16(C, C, false, false);
     const uint32_t id_st = tc::idesc_bf16(GW, HD, true, true);
-    const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, true);
+    const uint32_t id_cs = tc::idesc_bf16(GW, 16, true, false);
     const uint32_t id_dv = tc::idesc_bf16(C, HD, false, true);
     const uint32_t oq = P.q, ok_ = P.k, ov = P.v, oo = P.o, obst = P.bst;
     const int nchunks = a.nchunks;
@@ -331,7 +351,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
-                         tc::desc_mnmajor(sbase + P.tril, k0, TILE), id_cs, true);
+                         tc::desc_kmajor(sbase + P.ones, k0, 16 * 128), id_cs, true);
 #pragma unroll
           for (int k0 = 0; k0 < GW; k0 += 16)
             tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
@@ -395,13 +415,16 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       *reinterpret_cast<__nv_bfloat16 *>(sm + P.plo + off) = __float2bfloat16(pv - __bfloat162float(hi));
     }
     {
+      // strictly lower triangle: tril[t][tau] = tau < t (the diagonal terms are added in fp32)
       float v[8];
       for (int ch = 0; ch < 4; ++ch) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) <= t ? 1.f : 0.f;
+        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) < t ? 1.f : 0.f;
         tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
+    for (int i = threadIdx.x; i < 16 * C / 2; i += NEPI_T)  // bf16 ones, any layout
+      *reinterpret_cast<uint32_t *>(sm + P.ones + 4 * i) = 0x3F803F80u;
     for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end (zero: segment-local walk) -> TMEM
       const int g = 2 * b + mpar;
       float v[16];
@@ -432,18 +455,24 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_P1], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
+        // warps above the diagonal (hq > q4) store zeros without reading TMEM
         float v[32];
-        tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
-        tc::tmem_wait_ld();
-        if (hq == q4) {  // fp32 diagonal P1[t][t] (the exact-diagonal corrections below)
-          float dg = 0.f;
+        if (hq <= q4) {
+          tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
+          tc::tmem_wait_ld();
+          if (hq == q4) {  // fp32 diagonal P1[t][t] (the exact-diagonal corrections below)
+            float dg = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
-          sDiag[t] = dg;
+            for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
+            sDiag[t] = dg;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)  // strictly lower: the diagonal term is added in fp32
+              if (i >= lane) v[i] = 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * hq + i > t) v[i] = 0.f;
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
       }
@@ -496,20 +525,22 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           float ap[16], w[16];
           tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, ap);
           tc::tmem_wait_ld();
-          {  // the MMA summed bf16(pk_t) on the diagonal: use pk_t itself there
+          if (t < nt) {  // the MMA summed tau < t: the diagonal pk_t in fp32
             float pk[16];
             corner_probs(qK, pk);
-            if (t < nt) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) ap[i] += pk[i] - bf16r(pk[i]);
-            }
+            for (int i = 0; i < 16; ++i) ap[i] += pk[i];
           }
           corner_probs(qQ, w);
           const int sb = g * GW + 16 * hq;
           add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
           rcp_n<16>(ap, inv, a.batch_rcp);
+          if (t >= nt) {  // rows past the end: W, dpq, dA and the corrections below all vanish
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = t < nt ? w[i] * inv[i] : 0.f;
+            for (int i = 0; i < 16; ++i) inv[i] = 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] *= inv[i];
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, w + 8 * ch);
         }
@@ -526,26 +557,26 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           corner_probs(qQ, pq);
           corner_probs(qK, pk);
           const bool live = t < nt;
-          // Exact diagonal (tau = t).  Its share of G is P1[t][t] pk_t and of dpk it is
-          // dA_t + P1[t][t] W_t = W_t (P1[t][t] - dpq_t), which cancels exactly at the first
-          // tokens; the MMAs used bf16 roundings of each factor, so swap them for fp32 ones
-          // (G here, dpk through corr in the dpk phase).
-          const float p1 = sDiag[t], p1b = bf16r(p1);
+          // Exact diagonal (tau = t), in fp32: the MMAs with P1m and tril cover tau < t only.
+          // G gets P1[t][t] pk_t ; dpk gets dA_t + P1[t][t] W_t = W_t (P1[t][t] - dpq_t), which
+          // cancels exactly at the first tokens (carried to the dpk phase in corr).
+          // (rows past the end have inv = 0, so W, dpq, dA and corr are zero there)
+          const float p1 = sDiag[t];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float g = G[i] + p1 * pk[i] - p1b * bf16r(pk[i]);
-            const float w = live ? pq[i] * inv[i] : 0.f;
-            const float dpq = live ? g * inv[i] : 0.f;
+            const float g = fmaf(p1, pk[i], G[i]);
+            const float w = pq[i] * inv[i];
+            const float dpq = g * inv[i];
             const float da = -w * dpq;
             G[i] = da;
-            corr[i] = live ? (da - bf16r(da)) + (p1 * w - p1b * bf16r(w)) : 0.f;
+            corr[i] = fmaf(p1, w, da);
             inv[i] = dpq;
           }
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, G + 8 * ch);
           if (a.dprojQ != nullptr && live) {  // d proj_Q of table 4g + hq -> the fix-up's dQ
             float dp[4];
-            table_probs_bwd(pq, inv, thQ, a.scale, dp);
+            table_probs_bwd(pq, inv, qQ, thQ, a.scale, dp);
             uint2 w2;
             w2.x = tc::pack_bf16(dp[0], dp[1]);
             w2.y = tc::pack_bf16(dp[2], dp[3]);
@@ -564,21 +595,30 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           float dpk[16], pk[16], dp[4];
           tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, dpk);
           tc::tmem_wait_ld();
+          add_shared_row<16>(sbase + P.ga + 4 * ((g & 1) * GW + 16 * hq), dpk);  // + suffix gA
 #pragma unroll
-          for (int i = 0; i < 16; ++i) dpk[i] += sGA[(g & 1) * GW + 16 * hq + i] + inv[i];  // + diagonal correction
+          for (int i = 0; i < 16; ++i) dpk[i] += inv[i];  // + the fp32 diagonal term
           corner_probs(qK, pk);
-          table_probs_bwd(pk, dpk, thK, a.scale, dp);
+          table_probs_bwd(pk, dpk, qK, thK, a.scale, dp);
           if (t < nt)  // segment-local d proj_K of table 4g + hq, fp32, to the fix-up
             *reinterpret_cast<float4 *>(a.dprojK + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * hq) =
                 make_float4(dp[0], dp[1], dp[2], dp[3]);
           // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64),
           // written once gB, gA and the rest of dpk (readers of w and dA) completed
+          // (warps below the diagonal, hq < q4, store zeros without reading TMEM)
           float v[32];
-          tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
-          tc::tmem_wait_ld();
+          if (hq >= q4) {
+            tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
+            tc::tmem_wait_ld();
+            if (hq == q4) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (32 * hq + i < t) v[i] = 0.f;
+              for (int i = 0; i < 32; ++i)
+                if (i < lane) v[i] = 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          }
           ok = tc::warp_all(tc::mbar_wait(&bars[V3_D2], u & 1, abort));
           if (ok) {
 #pragma unroll
@@ -895,7 +935,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
             tc::tmem_wait_ld();
             add_shared_row<16>(sbase + P.ga + 4 * b0, g16);
             corner_probs(qK + 4 * tb, p16);
-            table_probs_bwd(p16, g16, thK + 4 * tb, a.scale, dp);
+            table_probs_bwd(p16, g16, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
             const int j = 4 * (tq * hq + tb);  // first projection column of the table
             // then hi + lo bf16 for the dK MMA
             dp[0] += loc[tb].x;
@@ -903,8 +943,10 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
             dp[2] += loc[tb].z;
             dp[3] += loc[tb].w;
             float lo[4];
+            bf16r2(dp[0], dp[1], lo[0], lo[1]);
+            bf16r2(dp[2], dp[3], lo[2], lo[3]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) lo[i] = dp[i] - __bfloat162float(__float2bfloat16(dp[i]));
+            for (int i = 0; i < 4; ++i) lo[i] = dp[i] - lo[i];
             tc::st_row_half(sbase + P.dp, t, j >> 3, (j >> 2) & 1, dp);
             tc::st_row_half(sbase + P.dplo, t, j >> 3, (j >> 2) & 1, lo);
           }
