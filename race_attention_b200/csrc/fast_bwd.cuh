@@ -104,11 +104,12 @@ __device__ __forceinline__ void st_bf16x8_global(__nv_bfloat16 *dst, const float
 
 // --------------------------------------------------------------------------
 struct BwdSmem {
-  uint32_t q, k, v, o, p1m, tril, planes, plo, pk, w, da, bst, gbst, ones, diag, a0, ga, bars, total;
+  uint32_t q, k, v, o, p1m, tril, planes, pk, w, da, bst, gbst, ones, diag, a0, ga, bars, total;
 };
 
-// planes and plo: bf16 planes and their residuals planes - bf16(planes), so that the
-// projections are exact to ~2^-17; tril and p1m: strictly lower triangles (tau < t),
+// planes: per 64-bucket group g, 32 K-major rows: the group's 16 bf16 planes (rows 32g..)
+// then their residuals planes - bf16(planes) (rows 32g+16..), so one N = 32 MMA gives
+// both halves of the projections (exact to ~2^-17 once summed); tril and p1m: strictly lower triangles (tau < t),
 // the diagonal terms being added in fp32 by the epilogue from diag, the fp32
 // diagonal of P1 = dO V^T; ones: the B operand of the gA column sums.
 __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
@@ -120,8 +121,7 @@ __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   m.o = o; o += TILE;
   m.p1m = o; o += 2 * TILE;
   m.tril = o; o += 2 * TILE;
-  m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
-  m.plo = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
+  m.planes = o; o += (uint32_t)align_up((size_t)2 * LP * 128, 1024);
   m.pk = o; o += TILE;
   m.w = o; o += TILE;
   m.da = o; o += TILE;  // must follow w: [w | da] is the 2-block Q2m tile
@@ -147,28 +147,27 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 // ===========================================================================
 // reverse walk of the backward pass
 //
-// TMEM: X [0,128) = P1 at chunk start, then Q2 per group;
-// R [128,192) = Apref, then dpk; GD [192,256) = G; PJ [256,288) = proj of one
-// group; then GB, GA (M=64 suffix-state blocks) and DV [.., +64).
+// TMEM: X [0,128) = P1 at chunk start, then Q2 summed over the chunk's groups;
+// R [128,192) = Apref, then dpk; GD [192,256) = proj of the group (K and Q x hi | lo
+// planes), then G; then GB, GA (M=64 suffix-state blocks) and DV [.., +64).
 // Schedule per group g ({X} named barrier, [X] mbarrier):
-//   control: {PK} Apref -> [APREF] ; {P1M, first group} ; [BST] G = dO Bst^T
-//            + P1m Pk -> [G] ;
-//            {W} Q2 = Pk W^T ; dpk = V gBst^T + P1m^T W (in R) ; gB += W^T dO ;
-//            ([G] done: next group's Bst load) ;
-//            {DA} dpk += tril^T dA -> [DPK] ; gA += dA^T 1 ; dV (+)= Pk gBst -> [D2] ;
-//            proj of the next group -> [PROJ] ; {Q2} dV += Q2m dO ;
+//   control: {PK} Apref -> [APREF] ; {P1M, first group} ; G = P1m Pk, [BST] + dO Bst^T
+//            -> [G] ; {W} dpk = V gBst^T + P1m^T W (in R) ;
+//            {DA} dpk += tril^T dA -> [DPK] ; next group's Bst load ; Q2 += Pk W^T ;
+//            gA += dA^T 1 ; dV (+)= Pk gBst ; gB += W^T dO ;
+//            proj of the next group -> [PROJ] (last group: -> [D2]) ;
 // (critical MMAs first in each handoff: the tensor pipe runs them in order)
-//            chunk end: [OUT] ; next chunk's proj(0) ;
+//            chunk end: {Q2} dV += Q2m dO -> [OUT] ; next chunk's proj(0) ;
 //            V/dO/Bst refill once every reader completed.
 // P1m and tril are strictly lower triangular: the tau = t terms of Apref, G and
 // dpk (pk_t, P1[t][t] pk_t, dA_t + P1[t][t] W_t) are added by the epilogue in fp32.
 //   epilogue: [PROJ] Pk, plane sigmoids, gBst and gA suffix copies {PK} ;
-//            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK, [D2] Q2m {Q2} ;
-//            chunk end: [OUT] dK, dV rows {OUTFREE}.
+//            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK ;
+//            chunk end: [D2] Q2m {Q2} ; [OUT] dV rows {OUTFREE}.
 enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_D2, V3_OUT, V3_TFREE, V3_FINAL,
        V3_COUNT };
 enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC };
-constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_PJ = 256, B3_ST = 288;
+constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_ST = 256;
 
 __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                           const __grid_constant__ CUtensorMap tmK,
@@ -208,7 +207,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
     const bool leader = lane == 0;
     const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
-    const uint32_t id_proj = tc::idesc_bf16(C, 16, false, false);
+    const uint32_t id_proj = tc::idesc_bf16(C, 32, false, false);
     const uint32_t id_apref = tc::idesc_bf16(C, GW, false, true);
     const uint32_t id_gk = tc::idesc_bf16(C, GW, false, false);
     const uint32_t id_gm = tc::idesc_bf16(C, GW, false, true);
@@ -236,16 +235,15 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       tc::mbar_arrive_expect_tx(&bars[V3_BST], GW * 128);
       tc::tma_load_2d(sm + obst, &tmB, &bars[V3_BST], 0, row);
     };
-    auto issue_proj = [=](int g) {  // x (planes_hi + planes_lo): the projections to ~2^-17
+    // proj of group g into GD (free between the epilogue's G read and the next G):
+    // K x [planes_hi | planes_lo] in GD[0, 32), Q x the same in GD[32, 64)
+    auto issue_proj = [=](int g) {
+      const uint32_t pl = sbase + P.planes + (uint32_t)g * 32 * 128;
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const uint32_t pl = sbase + (part ? P.plo : P.planes) + (uint32_t)g * 16 * 128;
-#pragma unroll
-        for (int k0 = 0; k0 < HD; k0 += 16) {
-          const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
-          tc::mma_bf16(tmem + B3_PJ, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, part > 0 || k0 > 0);
-          tc::mma_bf16(tmem + B3_PJ + 16, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, part > 0 || k0 > 0);
-        }
+      for (int k0 = 0; k0 < HD; k0 += 16) {
+        const uint64_t bp = tc::desc_kmajor(pl, k0, 0);
+        tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.k, k0, 0), bp, id_proj, k0 > 0);
+        tc::mma_bf16(tmem + B3_GD + 32, tc::desc_kmajor(sbase + P.q, k0, 0), bp, id_proj, k0 > 0);
       }
       tc::mma_commit(&bars[V3_PROJ]);
     };
@@ -295,17 +293,19 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           ok = ok && !*abort;
         }
         if (leader && ok) {
+          tc::tc_fence_after();
+          // G = P1m Pk (needs only this group's Pk) + dO Bst^T once the state tile is in
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.p1m, k0, TILE),
+                         tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, k0 > 0);
           ok = tc::mbar_wait(&bars[V3_BST], u & 1, abort);
           if (ok) {
             tc::tc_fence_after();
 #pragma unroll
             for (int k0 = 0; k0 < HD; k0 += 16)
               tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.o, k0, 0), tc::desc_kmajor(sbase + P.bst, k0, 0),
-                           id_gk, k0 > 0);
-#pragma unroll
-            for (int k0 = 0; k0 < C; k0 += 16)
-              tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.p1m, k0, TILE),
-                           tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, true);
+                           id_gk, true);
             tc::mma_commit(&bars[V3_G]);
             if (g + 1 == NG && k + 1 < nch) load_qk(c - 1);  // the chunk's last proj was consumed before {PK}
           }
@@ -314,12 +314,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
-          // Q2 (in X) = Pk W^T ; dpk (in R, Apref consumed) = V gBst^T + P1m^T W ;
-          // then, off the critical path, suffix gB += W^T dO
-#pragma unroll
-          for (int k0 = 0; k0 < GW; k0 += 16)
-            tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
-                         id_q2, k0 > 0);
+          // dpk (in R, Apref consumed) = V gBst^T + P1m^T W: the W-dependent MMAs on the way to {DA}
 #pragma unroll
           for (int k0 = 0; k0 < HD; k0 += 16)
             tc::mma_bf16(tmem + B3_R, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gbst, k0, 0),
@@ -328,26 +323,27 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
                          id_mm, true);
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
-                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
-          // the Bst tile is free once G completed: next group's chunk-start state
-          if (g + 1 < NG) {
-            ok = tc::mbar_wait(&bars[V3_G], u & 1, abort);
-            if (ok) load_bst(c, g + 1);
-          }
         }
         tc::named_bar_sync(N3_DA, NTHR);
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
-          // dpk += tril^T dA -> [DPK] ; then gA += dA^T 1 ; dV (+)= Pk gBst -> [D2] ; next proj
+          // dpk += tril^T dA -> [DPK] ; the next group's chunk-start state (every epilogue
+          // thread saw G complete before {DA}, so the Bst tile is free) ; Q2 (in X, summed over
+          // the chunk's groups) += Pk W^T ; gA += dA^T 1 ; dV (+)= Pk gBst ; suffix gB += W^T dO ;
+          // last group: -> [D2] (every reader of W and dA: the epilogue then overwrites them
+          // with Q2m) ; else next group's proj -> [PROJ] (its commit also covers the readers of
+          // this group's Pk and gBst tiles, which the epilogue rewrites after it)
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.tril, k0, TILE),
                          tc::desc_mnmajor(sbase + P.da, k0, 0), id_mm, true);
           tc::mma_commit(&bars[V3_DPK]);
+          if (g + 1 < NG) load_bst(c, g + 1);
+#pragma unroll
+          for (int k0 = 0; k0 < GW; k0 += 16)
+            tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
+                         id_q2, g > 0 || k0 > 0);
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
@@ -356,19 +352,25 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           for (int k0 = 0; k0 < GW; k0 += 16)
             tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
                          id_dv, g > 0 || k0 > 0);
-          tc::mma_commit(&bars[V3_D2]);
-          if (g + 1 < NG) issue_proj(g + 1);
-        }
-        tc::named_bar_sync(N3_Q2, NTHR);
-        ok = ok && !*abort;
-        if (leader && ok) {
-          tc::tc_fence_after();
-          // dV += Q2m dO (Q2m is the two-block tile [w | da])
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0),
-                         id_dv, true);
+            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
+          if (g + 1 < NG)
+            issue_proj(g + 1);
+          else
+            tc::mma_commit(&bars[V3_D2]);
         }
+      }
+      tc::named_bar_sync(N3_Q2, NTHR);
+      ok = ok && !*abort;
+      if (leader && ok) {
+        tc::tc_fence_after();
+        // dV += Q2m dO (Q2m is the two-block tile [w | da])
+#pragma unroll
+        for (int k0 = 0; k0 < C; k0 += 16)
+          tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.w, k0, TILE), tc::desc_mnmajor(sbase + P.o, k0, 0),
+                       id_dv, true);
       }
       if (leader && ok) {
         tc::mma_commit(&bars[V3_OUT]);  // dV of the chunk complete
@@ -410,9 +412,11 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       const int j = i / HD, d = i % HD;
       const float pv = a.planes[(size_t)d * a.LP + j];
       const __nv_bfloat16 hi = __float2bfloat16(pv);
-      const uint32_t off = tc::sw128_off(j, d >> 3) + (d & 7) * 2;
-      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + off) = hi;
-      *reinterpret_cast<__nv_bfloat16 *>(sm + P.plo + off) = __float2bfloat16(pv - __bfloat162float(hi));
+      const int row = 32 * (j >> 4) + (j & 15);  // hi row of plane j; its residual 16 rows on
+      const uint32_t cb = (uint32_t)(d & 7) * 2;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(row, d >> 3) + cb) = hi;
+      *reinterpret_cast<__nv_bfloat16 *>(sm + P.planes + tc::sw128_off(row + 16, d >> 3) + cb) =
+          __float2bfloat16(pv - __bfloat162float(hi));
     }
     {
       // strictly lower triangle: tril[t][tau] = tau < t (the diagonal terms are added in fp32)
@@ -487,15 +491,18 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         tc::tc_fence_after();
         if (ok) {
           float pr[16], bv[16], av;
-          tc::tmem_ld4(tmem + lane_off + B3_PJ + 4 * hq, thK);
-          tc::tmem_ld4(tmem + lane_off + B3_PJ + 16 + 4 * hq, thQ);
+          float loK[4], loQ[4];  // the residual-plane halves
+          tc::tmem_ld4(tmem + lane_off + B3_GD + 4 * hq, thK);
+          tc::tmem_ld4(tmem + lane_off + B3_GD + 16 + 4 * hq, loK);
+          tc::tmem_ld4(tmem + lane_off + B3_GD + 32 + 4 * hq, thQ);
+          tc::tmem_ld4(tmem + lane_off + B3_GD + 48 + 4 * hq, loQ);
           tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
           tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            thK[i] = tanh_fast(thK[i]);
-            thQ[i] = tanh_fast(thQ[i]);
+            thK[i] = tanh_fast(thK[i] + loK[i]);
+            thQ[i] = tanh_fast(thQ[i] + loQ[i]);
           }
           plane_sigmoids(thK, a.scale, a.poly, qK);
           plane_sigmoids(thQ, a.scale, a.poly, qQ);
@@ -588,7 +595,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::named_bar_arrive(N3_DA, NTHR);
-        // ---- dpk -> d proj_K ; Q2m
+        // ---- dpk -> d proj_K
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_DPK], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
@@ -603,32 +610,33 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           if (t < nt)  // segment-local d proj_K of table 4g + hq, fp32, to the fix-up
             *reinterpret_cast<float4 *>(a.dprojK + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * hq) =
                 make_float4(dp[0], dp[1], dp[2], dp[3]);
-          // Q2m[tau = t][t'] = Q2 for t' >= tau ; blocks: w (t' < 64), da (t' >= 64),
-          // written once gB, gA and the rest of dpk (readers of w and dA) completed
-          // (warps below the diagonal, hq < q4, store zeros without reading TMEM)
-          float v[32];
-          if (hq >= q4) {
-            tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
-            tc::tmem_wait_ld();
-            if (hq == q4) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < lane) v[i] = 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          }
-          ok = tc::warp_all(tc::mbar_wait(&bars[V3_D2], u & 1, abort));
-          if (ok) {
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, v + 8 * ch);
-          }
         }
-        tc::fence_async_smem();
-        tc::tc_fence_before();
-        tc::named_bar_arrive(N3_Q2, NTHR);
       }
+      // ---- Q2m[tau = t][t'] = Q2 (summed over the groups) for t' >= tau ; blocks: w (t' < 64),
+      // da (t' >= 64), once Q2 and every reader of w and dA completed
+      // (warps below the diagonal, hq < q4, store zeros without reading TMEM)
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_D2], k & 1, abort));
+      tc::tc_fence_after();
+      if (ok) {
+        float v[32];
+        if (hq >= q4) {
+          tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
+          tc::tmem_wait_ld();
+          if (hq == q4) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < lane) v[i] = 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, v + 8 * ch);
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      tc::named_bar_arrive(N3_Q2, NTHR);
       // ---- dK, dV rows
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_OUT], k & 1, abort));
       tc::tc_fence_after();
