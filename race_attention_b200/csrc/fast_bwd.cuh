@@ -700,15 +700,20 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
 // another, so one CTA per (stream, segment) loops over its chunks with the
 // segment's gB_in held in shared memory (bf16, the MMA operand for both
 // products).
-//   control: [KV] proj = K (planes_hi + planes_lo) -> [PROJ] ; Dfix = V gB_in^T -> [DPK] ;
-//            {OUTFREE} dQ = dprojQ planes ; {PK} dV = Pk gB_in ; {DP} dK = dproj planes -> [OUT]
+// The outputs leave through shared memory and TMA tile stores (dK and dQ rows staged in
+// the d proj tiles, dV rows in the tile the walk's dV came in through), not per-thread
+// 16-byte stores that split every warp instruction into 32 row transactions.
+//   control: [KV] proj = K (planes_hi + planes_lo) -> [PROJ] ;
+//            {OUTFREE} store the previous chunk's dK, dV, dQ tiles, wait until they are read,
+//            load this chunk's dV tile -> [DVL], Dfix = V gB_in^T -> [DPK] ;
+//            dQ = dprojQ planes ; {PK} dV = Pk gB_in ; {DP} dK = dproj planes -> [OUT]
 //   epilogue: [PROJ] Pk {PK} ; [DPK] dproj = softmax bwd of (Dfix + gA_in) {DP} ;
-//             [OUT] dK += , dV += , dQ = {OUTFREE}
-enum { VF_KV = 0, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_FINAL, VF_COUNT };
+//             [OUT] [DVL] dK, dV += , dQ rows into the tiles {OUTFREE}
+enum { VF_KV = 0, VF_DVL, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_FINAL, VF_COUNT };
 enum { NF_INIT = 1, NF_PK, NF_DP, NF_OUTFREE };
 
 struct FixSmem {
-  uint32_t k, v, dq, pk, gb, dp, dplo, planes, plo, ga, bars, total;
+  uint32_t k, v, dq, dvl, pk, gb, dp, dplo, planes, plo, ga, bars, total;
 };
 
 __host__ __device__ __forceinline__ FixSmem fix_smem_plan(int LP, int S) {
@@ -717,9 +722,10 @@ __host__ __device__ __forceinline__ FixSmem fix_smem_plan(int LP, int S) {
   m.k = o; o += TILE;
   m.v = o; o += TILE;
   m.dq = o; o += TILE;
+  m.dvl = o; o += TILE;                      // the walk's dV rows in, dV rows out
   m.pk = o; o += (uint32_t)(S / 64) * TILE;  // [128 t x S] K-major, 64-column blocks
   m.gb = o; o += (uint32_t)S * 128;          // [S rows x 64 d] bf16
-  m.dp = o; o += TILE;                       // d proj_K = hi + lo, bf16 tiles
+  m.dp = o; o += TILE;                       // d proj_K = hi + lo, bf16 tiles; then dK, dQ rows out
   m.dplo = o; o += TILE;
   m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
   m.plo = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
@@ -734,7 +740,11 @@ constexpr uint32_t FX_PJ = 0, FX_D = 64;
 
 __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV,
-                                                          const __grid_constant__ CUtensorMap tmDQ, BwdArgs a) {
+                                                          const __grid_constant__ CUtensorMap tmDQ,
+                                                          const __grid_constant__ CUtensorMap tmVL,
+                                                          const __grid_constant__ CUtensorMap tmOK,
+                                                          const __grid_constant__ CUtensorMap tmOV,
+                                                          const __grid_constant__ CUtensorMap tmOQ, BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   const FixSmem P = fix_smem_plan(a.LP, a.S);
@@ -776,8 +786,18 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       tc::tma_load_3d(sm + ov, &tmV, &bars[VF_KV], 0, t0, n);
       tc::tma_load_3d(sm + oq, &tmDQ, &bars[VF_KV], 0, t0, n);
     };
-    // proj = K planes and Dfix = V gB_in^T for the chunk in the tiles
-    auto issue_front = [=]() {
+    auto load_dvl = [=, &tmVL](int c) {
+      tc::mbar_arrive_expect_tx(&bars[VF_DVL], TILE);
+      tc::tma_load_3d(sm + P.dvl, &tmVL, &bars[VF_DVL], 0, (c_begin + c) * C, n);
+    };
+    auto store_out = [=, &tmOK, &tmOV, &tmOQ](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::tma_store_3d(&tmOK, sm + P.dp, 0, t0, n);
+      tc::tma_store_3d(&tmOV, sm + P.dvl, 0, t0, n);
+      tc::tma_store_3d(&tmOQ, sm + P.dplo, 0, t0, n);
+      tc::bulk_commit();
+    };
+    auto issue_proj = [=]() {  // proj = K planes for the chunk in the tiles
 #pragma unroll
       for (int part = 0; part < 2; ++part)
 #pragma unroll
@@ -785,6 +805,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
           tc::mma_bf16(tmem + FX_PJ, tc::desc_kmajor(sbase + P.k, k0, 0),
                        tc::desc_kmajor(sbase + (part ? P.plo : P.planes), k0, 0), id_proj, part > 0 || k0 > 0);
       tc::mma_commit(&bars[VF_PROJ]);
+    };
+    auto issue_dfix = [=]() {  // Dfix = V gB_in^T
 #pragma unroll
       for (int k0 = 0; k0 < HD; k0 += 16)
         tc::mma_bf16(tmem + FX_D, tc::desc_kmajor(sbase + P.v, k0, 0), tc::desc_kmajor(sbase + P.gb, k0, 0), id_vg,
@@ -801,18 +823,33 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       }
     };
     bool ok = true;
-    if (leader && nch > 0) load(0);
+    if (leader && nch > 0) {
+      load(0);
+      load_dvl(0);
+    }
     tc::named_bar_sync(NF_INIT, NTHR);  // planes, gB_in, gA_in in shared memory
     if (leader && nch > 0) {
       ok = tc::mbar_wait(&bars[VF_KV], 0, abort);
       if (ok) {
         tc::tc_fence_after();
-        issue_front();
+        issue_proj();
+        issue_dfix();
       }
     }
     for (int c = 0; c < nch; ++c) {
-      if (c > 0) tc::named_bar_sync(NF_OUTFREE, NTHR);  // dQ, dK, dV of the previous chunk are out
-      ok = ok && !*abort;
+      if (c > 0) {
+        tc::named_bar_sync(NF_OUTFREE, NTHR);  // the previous chunk's dK, dV, dQ rows are in the tiles
+        ok = ok && !*abort;
+        if (leader && ok) {
+          store_out(c - 1);
+          // the tiles are read out before this chunk's dV rows come in and before the epilogue
+          // rewrites the d proj tiles (it waits for [DPK], committed after this)
+          tc::bulk_wait_read();
+          load_dvl(c);
+          tc::tc_fence_after();
+          issue_dfix();
+        }
+      }
       if (leader && ok) {
         tc::tc_fence_after();
         issue_planes(T_DQ, P.dq, 0);
@@ -838,12 +875,18 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
           ok = tc::mbar_wait(&bars[VF_KV], (c + 1) & 1, abort);
           if (ok) {
             tc::tc_fence_after();
-            issue_front();
+            issue_proj();
           }
         }
       }
     }
+    if (nch > 0) {
+      tc::named_bar_sync(NF_OUTFREE, NTHR);  // the last chunk's rows are in the tiles
+      ok = ok && !*abort;
+      if (leader && ok) store_out(nch - 1);
+    }
     if (leader && nch > 0) {
+      tc::bulk_wait();  // stores complete (and shared memory read) before the CTA exits
       tc::mma_commit(&bars[VF_FINAL]);
       if (!tc::mbar_wait_drain(&bars[VF_FINAL], 0)) atomicExch(a.err, 2);
     }
@@ -963,13 +1006,11 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       tc::fence_async_smem();
       tc::tc_fence_before();
       tc::named_bar_arrive(NF_DP, NTHR);
-      // ---- dK, dV += dV_fix, dQ (row t, d in [16hq, 16hq+16))
-      uint4 dvl[2];  // the walk's dV rows, loaded before the wait
-      const __nv_bfloat16 *dvsrc = a.dVloc ? a.dVloc : a.dV;
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch)
-        dvl[ch] = live ? *reinterpret_cast<const uint4 *>(dvsrc + row + 16 * hq + 8 * ch) : make_uint4(0, 0, 0, 0);
+      // ---- dK, dV += dV_fix, dQ rows (row t, d in [16hq, 16hq+16)) into the output tiles:
+      // dK into the d proj_K hi tile and dQ into its lo tile (both read by the dK MMAs, complete
+      // at [OUT]), dV in place in the tile holding the walk's dV rows
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_OUT], c & 1, abort));
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_DVL], c & 1, abort));
       tc::tc_fence_after();
       if (ok) {
         float vq[16], vk[16], vv[16];
@@ -977,25 +1018,24 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
         tc::tmem_ld16(tmem + lane_off + T_DK + 16 * hq, vk);
         tc::tmem_ld16(tmem + lane_off + T_DV + 16 * hq, vv);
         tc::tmem_wait_ld();
-        if (live) {
-          const size_t orow = row + 16 * hq;
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            const uint4 v4 = dvl[ch];
-            const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
+        for (int ch = 0; ch < 2; ++ch) {
+          const uint32_t off = tc::sw128_off(t, 2 * hq + ch);
+          const uint4 v4 = *reinterpret_cast<const uint4 *>(sm + P.dvl + off);
+          const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              vv[8 * ch + 2 * e] += __uint_as_float(vw[e] << 16);
-              vv[8 * ch + 2 * e + 1] += __uint_as_float(vw[e] & 0xFFFF0000u);
-            }
-            st_bf16x8_global(a.dK + orow + 8 * ch, vk + 8 * ch);
-            st_bf16x8_global(a.dV + orow + 8 * ch, vv + 8 * ch);
-            if (a.dQ != nullptr) st_bf16x8_global(a.dQ + orow + 8 * ch, vq + 8 * ch);
+          for (int e = 0; e < 4; ++e) {
+            vv[8 * ch + 2 * e] += __uint_as_float(vw[e] << 16);
+            vv[8 * ch + 2 * e + 1] += __uint_as_float(vw[e] & 0xFFFF0000u);
           }
+          tc::st_row_chunk(sbase + P.dvl, t, 2 * hq + ch, vv + 8 * ch);
+          tc::st_row_chunk(sbase + P.dp, t, 2 * hq + ch, vk + 8 * ch);
+          tc::st_row_chunk(sbase + P.dplo, t, 2 * hq + ch, vq + 8 * ch);
         }
       }
+      tc::fence_async_smem();
       tc::tc_fence_before();
-      if (c + 1 < nch) tc::named_bar_arrive(NF_OUTFREE, NTHR);
+      tc::named_bar_arrive(NF_OUTFREE, NTHR);
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }
