@@ -153,19 +153,19 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 // Schedule per group g ({X} named barrier, [X] mbarrier):
 //   control: {PK} Apref -> [APREF] ; {P1M, first group} ; G = P1m Pk, [BST] + dO Bst^T
 //            -> [G] ; {W} dpk = V gBst^T + P1m^T W (in R) ;
-//            {DA} dpk += tril^T dA -> [DPK] ; next group's Bst load ; Q2 += Pk W^T ;
-//            gA += dA^T 1 ; dV (+)= Pk gBst ; gB += W^T dO ;
-//            proj of the next group -> [PROJ] (last group: -> [D2]) ;
+//            {DA} dpk += tril^T dA -> [DPK] ; next group's Bst load and proj -> [PROJ] ;
+//            gA += dA^T 1 ; gB += W^T dO ; Q2 += Pk W^T ; dV (+)= Pk gBst -> [TF]
+//            (last group: also -> [D2]) ;
 // (critical MMAs first in each handoff: the tensor pipe runs them in order)
 //            chunk end: {Q2} dV += Q2m dO -> [OUT] ; next chunk's proj(0) ;
 //            V/dO/Bst refill once every reader completed.
 // P1m and tril are strictly lower triangular: the tau = t terms of Apref, G and
 // dpk (pk_t, P1[t][t] pk_t, dA_t + P1[t][t] W_t) are added by the epilogue in fp32.
-//   epilogue: [PROJ] Pk, plane sigmoids, gBst and gA suffix copies {PK} ;
+//   epilogue: [PROJ] Pk, plane sigmoids, [TF] gBst and gA suffix copies {PK} ;
 //            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK ;
 //            chunk end: [D2] Q2m {Q2} ; [OUT] dV rows {OUTFREE}.
-enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_D2, V3_OUT, V3_TFREE, V3_FINAL,
-       V3_COUNT };
+enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_TF, V3_D2, V3_OUT, V3_TFREE,
+       V3_FINAL, V3_COUNT };
 enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC };
 constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_ST = 256;
 
@@ -299,7 +299,9 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.p1m, k0, TILE),
                          tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, k0 > 0);
-          ok = tc::mbar_wait(&bars[V3_BST], u & 1, abort);
+          // (groups after the first: the Bst tile was waited for at the end of the previous
+          // group's {DA} step, off this critical path)
+          if (g == 0) ok = tc::mbar_wait(&bars[V3_BST], u & 1, abort);
           if (ok) {
             tc::tc_fence_after();
 #pragma unroll
@@ -329,37 +331,41 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
         if (leader && ok) {
           tc::tc_fence_after();
           // dpk += tril^T dA -> [DPK] ; the next group's chunk-start state (every epilogue
-          // thread saw G complete before {DA}, so the Bst tile is free) ; Q2 (in X, summed over
-          // the chunk's groups) += Pk W^T ; gA += dA^T 1 ; dV (+)= Pk gBst ; suffix gB += W^T dO ;
-          // last group: -> [D2] (every reader of W and dA: the epilogue then overwrites them
-          // with Q2m) ; else next group's proj -> [PROJ] (its commit also covers the readers of
-          // this group's Pk and gBst tiles, which the epilogue rewrites after it)
+          // thread saw G complete before {DA}, so the Bst tile is free) ; next group's proj ->
+          // [PROJ] ; then gA += dA^T 1, suffix gB += W^T dO, Q2 (in X, summed over the chunk's
+          // groups) += Pk W^T, dV (+)= Pk gBst -> [TF] (the epilogue reads the next group's
+          // suffix states from the gA/gB blocks and rewrites the Pk and gBst tiles after it);
+          // last group: also -> [D2] (every reader of W and dA: the epilogue then overwrites
+          // them with Q2m)
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.tril, k0, TILE),
                          tc::desc_mnmajor(sbase + P.da, k0, 0), id_mm, true);
           tc::mma_commit(&bars[V3_DPK]);
-          if (g + 1 < NG) load_bst(c, g + 1);
-#pragma unroll
-          for (int k0 = 0; k0 < GW; k0 += 16)
-            tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
-                         id_q2, g > 0 || k0 > 0);
+          if (g + 1 < NG) {
+            load_bst(c, g + 1);
+            issue_proj(g + 1);
+          }
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
                          tc::desc_kmajor(sbase + P.ones, k0, 16 * 128), id_cs, true);
 #pragma unroll
-          for (int k0 = 0; k0 < GW; k0 += 16)
-            tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
-                         id_dv, g > 0 || k0 > 0);
-#pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
                          tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
-          if (g + 1 < NG)
-            issue_proj(g + 1);
-          else
-            tc::mma_commit(&bars[V3_D2]);
+#pragma unroll
+          for (int k0 = 0; k0 < GW; k0 += 16)
+            tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
+                         id_q2, g > 0 || k0 > 0);
+#pragma unroll
+          for (int k0 = 0; k0 < GW; k0 += 16)
+            tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
+                         id_dv, g > 0 || k0 > 0);
+          tc::mma_commit(&bars[V3_TF]);
+          if (g + 1 == NG) tc::mma_commit(&bars[V3_D2]);
+          // the next group's Bst tile, loaded above, while the epilogue works on dpk and Pk
+          if (g + 1 < NG) ok = tc::mbar_wait(&bars[V3_BST], (u + 1) & 1, abort);
         }
       }
       tc::named_bar_sync(N3_Q2, NTHR);
@@ -486,18 +492,17 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
         float thK[4], thQ[4], qK[4], qQ[4], inv[16];  // tanh and plane sigmoids of table 4g + hq
-        // ---- Pk ; suffix gB (bf16) and gA copies of group g
+        // ---- Pk ; suffix gB (bf16) and gA copies of group g (once [TF] of the previous group
+        // says the gA/gB blocks are updated and the Pk and gBst tiles read)
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_PROJ], u & 1, abort));
         tc::tc_fence_after();
+        float pr[16];
         if (ok) {
-          float pr[16], bv[16], av;
           float loK[4], loQ[4];  // the residual-plane halves
           tc::tmem_ld4(tmem + lane_off + B3_GD + 4 * hq, thK);
           tc::tmem_ld4(tmem + lane_off + B3_GD + 16 + 4 * hq, loK);
           tc::tmem_ld4(tmem + lane_off + B3_GD + 32 + 4 * hq, thQ);
           tc::tmem_ld4(tmem + lane_off + B3_GD + 48 + 4 * hq, loQ);
-          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
-          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -511,6 +516,14 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
 #pragma unroll
             for (int i = 0; i < 16; ++i) pr[i] = 0.f;
           }
+        }
+        if (ok && u > 0) ok = tc::warp_all(tc::mbar_wait(&bars[V3_TF], (u - 1) & 1, abort));
+        tc::tc_fence_after();
+        if (ok) {
+          float bv[16], av;
+          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
+          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
+          tc::tmem_wait_ld();
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
           if (mpar == (g & 1)) {
