@@ -136,6 +136,33 @@ __host__ __device__ __forceinline__ BwdSmem bwd_smem_plan(int LP, int S) {
   return m;
 }
 
+// TMEM loads / stores of n consecutive columns of this thread's lane
+template <int n>
+__device__ __forceinline__ void tmem_ldn(uint32_t addr, float *v) {
+  if constexpr (n == 4) {
+    tc::tmem_ld4(addr, *reinterpret_cast<float(*)[4]>(v));
+  } else if constexpr (n == 8) {
+    tc::tmem_ld8(addr, *reinterpret_cast<float(*)[8]>(v));
+  } else if constexpr (n == 16) {
+    tc::tmem_ld16(addr, *reinterpret_cast<float(*)[16]>(v));
+  } else {
+    static_assert(n % 32 == 0, "tmem_ldn: 4, 8, 16 or a multiple of 32 columns");
+#pragma unroll
+    for (int i = 0; i < n / 32; ++i) tc::tmem_ld32(addr + 32 * i, *reinterpret_cast<float(*)[32]>(v + 32 * i));
+  }
+}
+template <int n>
+__device__ __forceinline__ void tmem_stn(uint32_t addr, const float *v) {
+  if constexpr (n == 16) {
+    tc::tmem_st16(addr, *reinterpret_cast<const float(*)[16]>(v));
+  } else {
+    static_assert(n % 32 == 0, "tmem_stn: 16 or a multiple of 32 columns");
+#pragma unroll
+    for (int i = 0; i < n / 32; ++i)
+      tc::tmem_st32(addr + 32 * i, *reinterpret_cast<const float(*)[32]>(v + 32 * i));
+  }
+}
+
 // row of an M=64 accumulator held by this thread's TMEM lane (lane quarter q, lane i):
 // group parity (i >= 16) and row 16q + (i & 15)
 __device__ __forceinline__ int m64_row(int q4, int lane) { return 16 * q4 + (lane & 15); }
@@ -166,14 +193,23 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 //            chunk end: [D2] Q2m {Q2} ; [OUT] dV rows {OUTFREE}.
 enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_TF, V3_D2, V3_OUT, V3_TFREE,
        V3_FINAL, V3_COUNT };
+// the reverse walk's epilogue layout (see bwd_rev_kernel): 16 warps measured 3 % faster than 8
+// warps of twice the width (fewer warps beside the MMA issuer, but less latency hiding)
+constexpr int REV_TPW = 1;
 enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC };
 constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_ST = 256;
 
-__global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
-                                                          const __grid_constant__ CUtensorMap tmK,
-                                                          const __grid_constant__ CUtensorMap tmV,
-                                                          const __grid_constant__ CUtensorMap tmO,
-                                                          const __grid_constant__ CUtensorMap tmB, BwdArgs a) {
+// TPW: tables per epilogue thread per 64-bucket group (1: 16 epilogue warps, 2: 8 epilogue warps
+// and twice the registers per thread -- two warps beside the MMA issuer on its SM
+// sub-partition instead of four, and each thread's work twice as wide)
+template <int TPW>
+__global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ? 96 : 224) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                                        const __grid_constant__ CUtensorMap tmK,
+                                                                        const __grid_constant__ CUtensorMap tmV,
+                                                                        const __grid_constant__ CUtensorMap tmO,
+                                                                        const __grid_constant__ CUtensorMap tmB,
+                                                                        BwdArgs a) {
+  constexpr int NE = 16 / TPW, NT = 32 * (NE + 1), NET = 32 * NE;  // epilogue warps, threads
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   const BwdSmem P = bwd_smem_plan(a.LP, a.S);
@@ -196,14 +232,14 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     for (int i = 0; i < V3_COUNT; ++i) tc::mbar_init(&bars[i], 1);
     tc::fence_mbar_init();
   }
-  if (warp == NEPI) tc::tmem_alloc(&s_tmem, 512);
+  if (warp == NE) tc::tmem_alloc(&s_tmem, 512);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
   volatile int *abort = &s_abort;
 
-  if (warp == NEPI) {
+  if (warp == NE) {
     // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
     const bool leader = lane == 0;
     const uint32_t id_p1 = tc::idesc_bf16(C, C, false, false);
@@ -253,7 +289,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       load_vo(nch - 1);
       load_bst(nch - 1, 0);
     }
-    tc::named_bar_sync(N3_INIT, NTHR);  // planes, tril and suffix state are in place
+    tc::named_bar_sync(N3_INIT, NT);  // planes, tril and suffix state are in place
     if (leader && nch > 0) {
       ok = tc::mbar_wait(&bars[V3_QK], 0, abort);
       if (ok) {
@@ -263,7 +299,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     }
     for (int k = 0; k < nch; ++k) {
       const int c = nch - 1 - k;
-      if (k > 0) tc::named_bar_sync(N3_OUTFREE, NTHR);  // dK and dV of the previous chunk are out
+      if (k > 0) tc::named_bar_sync(N3_OUTFREE, NT);  // dK and dV of the previous chunk are out
       ok = ok && !*abort;
       if (leader && ok) {
         ok = tc::mbar_wait(&bars[V3_VO], k & 1, abort);
@@ -278,7 +314,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       }
       for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
-        tc::named_bar_sync(N3_PK, NTHR);
+        tc::named_bar_sync(N3_PK, NT);
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
@@ -289,7 +325,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           tc::mma_commit(&bars[V3_APREF]);
         }
         if (g == 0) {
-          tc::named_bar_sync(N3_P1M, NTHR);
+          tc::named_bar_sync(N3_P1M, NT);
           ok = ok && !*abort;
         }
         if (leader && ok) {
@@ -312,7 +348,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
             if (g + 1 == NG && k + 1 < nch) load_qk(c - 1);  // the chunk's last proj was consumed before {PK}
           }
         }
-        tc::named_bar_sync(N3_W, NTHR);
+        tc::named_bar_sync(N3_W, NT);
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
@@ -326,7 +362,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
             tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.p1m, k0, TILE), tc::desc_mnmajor(sbase + P.w, k0, 0),
                          id_mm, true);
         }
-        tc::named_bar_sync(N3_DA, NTHR);
+        tc::named_bar_sync(N3_DA, NT);
         ok = ok && !*abort;
         if (leader && ok) {
           tc::tc_fence_after();
@@ -368,7 +404,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
           if (g + 1 < NG) ok = tc::mbar_wait(&bars[V3_BST], (u + 1) & 1, abort);
         }
       }
-      tc::named_bar_sync(N3_Q2, NTHR);
+      tc::named_bar_sync(N3_Q2, NT);
       ok = ok && !*abort;
       if (leader && ok) {
         tc::tc_fence_after();
@@ -402,19 +438,22 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     }
     __syncwarp();
   } else {
-    // ============================== epilogue warps: row t, column quarter hq
-    // (in a 64-bucket group, quarter hq owns table 4g + hq: buckets [16hq, 16hq+16))
+    // ============================== epilogue warps: row t, column slot hq
+    // (NE = 16/TPW warps, four per TMEM lane quarter; in a 64-bucket group slot hq owns
+    // tables 4g + TPW hq + [0, TPW): buckets and d columns [TB hq, TB hq + TB), TB = 16 TPW;
+    // in a 128-column token tile, columns [CW hq, CW hq + CW), CW = 32 TPW)
+    constexpr int TB = 16 * TPW, CW = 32 * TPW;
     const int q4 = warp & 3, hq = warp >> 2;
     const int t = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const uint32_t blk = (uint32_t)(hq >> 1) * TILE;  // 64-column block holding this quarter's 32 columns
-    const int ch0 = (hq & 1) * 4;                      // its first 16-byte chunk inside that block
+    const uint32_t blk = (uint32_t)((CW * hq) >> 6) * TILE;  // 64-column block holding this slot's columns
+    const int ch0 = ((CW * hq) & 63) >> 3;                    // its first 16-byte chunk inside that block
     const int mrow = m64_row(q4, lane), mpar = lane >> 4;
     float *sA = reinterpret_cast<float *>(sm + P.a0);
     float *sGA = reinterpret_cast<float *>(sm + P.ga);
     float *sDiag = reinterpret_cast<float *>(sm + P.diag);
     const float *sst = a.suf_state ? a.suf_state + ((size_t)n * a.nseg + seg) * E : nullptr;
-    for (int i = threadIdx.x; i < a.LP * HD; i += NEPI_T) {  // planes = hi + lo, both bf16
+    for (int i = threadIdx.x; i < a.LP * HD; i += NET) {  // planes = hi + lo, both bf16
       const int j = i / HD, d = i % HD;
       const float pv = a.planes[(size_t)d * a.LP + j];
       const __nv_bfloat16 hi = __float2bfloat16(pv);
@@ -427,244 +466,279 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
     {
       // strictly lower triangle: tril[t][tau] = tau < t (the diagonal terms are added in fp32)
       float v[8];
-      for (int ch = 0; ch < 4; ++ch) {
+      for (int ch = 0; ch < CW / 8; ++ch) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = (32 * hq + ch * 8 + e) < t ? 1.f : 0.f;
+        for (int e = 0; e < 8; ++e) v[e] = (CW * hq + ch * 8 + e) < t ? 1.f : 0.f;
         tc::st_row_chunk(sbase + P.tril + blk, t, ch0 + ch, v);
       }
     }
-    for (int i = threadIdx.x; i < 16 * C / 2; i += NEPI_T)  // bf16 ones, any layout
+    for (int i = threadIdx.x; i < 16 * C / 2; i += NET)  // bf16 ones, any layout
       *reinterpret_cast<uint32_t *>(sm + P.ones + 4 * i) = 0x3F803F80u;
     for (int b = 0; b < nblk; ++b) {  // suffix state at the segment end (zero: segment-local walk) -> TMEM
       const int g = 2 * b + mpar;
-      float v[16];
+      float v[TB];
       if (g < NG && sst != nullptr) {
-        const float *src = sst + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
+        const float *src = sst + S + (size_t)(g * GW + mrow) * HD + TB * hq;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = src[i];
+        for (int i = 0; i < TB; ++i) v[i] = src[i];
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        for (int i = 0; i < TB; ++i) v[i] = 0.f;
       }
-      tc::tmem_st16(tmem + lane_off + T_GB + 64 * b + 16 * hq, v);
+      tmem_stn<TB>(tmem + lane_off + T_GB + 64 * b + TB * hq, v);
       if (hq == 0) tc::tmem_st1(tmem + lane_off + T_GA + 16 * b, g < NG && sst != nullptr ? sst[g * GW + mrow] : 0.f);
     }
     tc::tmem_wait_st();
     tc::fence_async_smem();
     tc::tc_fence_before();
-    tc::named_bar_sync(N3_INIT, NTHR);
+    tc::named_bar_sync(N3_INIT, NT);
 
     bool ok = true;
     for (int k = 0; k < nch; ++k) {
       const int c = nch - 1 - k, cg = c_begin + c, tok0 = cg * C;
       const int nt = min(C, a.T - tok0);
       // chunk-start A + eps (stored by the forward walk)
-      for (int s = threadIdx.x; s < S; s += NEPI_T) sA[s] = a.chunkA[((size_t)n * a.nchunks + cg) * S + s];
-      tc::named_bar_sync(N3_ESYNC, NEPI_T);  // sA visible to all epilogue threads
+      for (int s = threadIdx.x; s < S; s += NET) sA[s] = a.chunkA[((size_t)n * a.nchunks + cg) * S + s];
+      tc::named_bar_sync(N3_ESYNC, NET);  // sA visible to all epilogue threads
       // ---- P1m = tril-masked dO V^T
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_P1], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
-        // warps above the diagonal (hq > q4) store zeros without reading TMEM
-        float v[32];
-        if (hq <= q4) {
-          tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
-          tc::tmem_wait_ld();
-          if (hq == q4) {  // fp32 diagonal P1[t][t] (the exact-diagonal corrections below)
-            float dg = 0.f;
+        // 32 columns at a time; column runs all at or above the diagonal store zeros without
+        // reading TMEM
 #pragma unroll
-            for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
-            sDiag[t] = dg;
+        for (int h = 0; h < CW / 32; ++h) {
+          const int col0 = CW * hq + 32 * h;  // first token column of this run
+          float v[32];
+          if (col0 < 32 * q4 + 32) {
+            tc::tmem_ld32(tmem + lane_off + B3_X + col0, v);
+            tc::tmem_wait_ld();
+            if (col0 + 32 > 32 * q4) {  // the run holds this row's diagonal (col0 == 32 q4)
+              float dg = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i)  // strictly lower: the diagonal term is added in fp32
-              if (i >= lane) v[i] = 0.f;
+              for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
+              sDiag[t] = dg;  // fp32 diagonal P1[t][t] (the exact-diagonal terms below)
+#pragma unroll
+              for (int i = 0; i < 32; ++i)  // strictly lower: the diagonal term is added in fp32
+                if (i >= lane) v[i] = 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
           }
-        } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + 4 * h + ch, v + 8 * ch);
         }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + ch, v + 8 * ch);
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
-      tc::named_bar_arrive(N3_P1M, NTHR);
+      tc::named_bar_arrive(N3_P1M, NT);
       for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
-        float thK[4], thQ[4], qK[4], qQ[4], inv[16];  // tanh and plane sigmoids of table 4g + hq
+        // tanh, plane sigmoids of the slot's tables ; 1/(A + eps), then dpq, then the diagonal terms
+        float thK[4 * TPW], thQ[4 * TPW], qK[4 * TPW], qQ[4 * TPW], inv[TB];
         // ---- Pk ; suffix gB (bf16) and gA copies of group g (once [TF] of the previous group
         // says the gA/gB blocks are updated and the Pk and gBst tiles read)
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_PROJ], u & 1, abort));
         tc::tc_fence_after();
-        float pr[16];
         if (ok) {
-          float loK[4], loQ[4];  // the residual-plane halves
-          tc::tmem_ld4(tmem + lane_off + B3_GD + 4 * hq, thK);
-          tc::tmem_ld4(tmem + lane_off + B3_GD + 16 + 4 * hq, loK);
-          tc::tmem_ld4(tmem + lane_off + B3_GD + 32 + 4 * hq, thQ);
-          tc::tmem_ld4(tmem + lane_off + B3_GD + 48 + 4 * hq, loQ);
+          float loK[4 * TPW], loQ[4 * TPW];  // the residual-plane halves
+          tmem_ldn<4 * TPW>(tmem + lane_off + B3_GD + 4 * TPW * hq, thK);
+          tmem_ldn<4 * TPW>(tmem + lane_off + B3_GD + 16 + 4 * TPW * hq, loK);
+          tmem_ldn<4 * TPW>(tmem + lane_off + B3_GD + 32 + 4 * TPW * hq, thQ);
+          tmem_ldn<4 * TPW>(tmem + lane_off + B3_GD + 48 + 4 * TPW * hq, loQ);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < 4 * TPW; ++i) {
             thK[i] = tanh_fast(thK[i] + loK[i]);
             thQ[i] = tanh_fast(thQ[i] + loQ[i]);
           }
-          plane_sigmoids(thK, a.scale, a.poly, qK);
-          plane_sigmoids(thQ, a.scale, a.poly, qQ);
-          corner_probs(qK, pr);
-          if (t >= nt) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) pr[i] = 0.f;
+          for (int tb = 0; tb < TPW; ++tb) {
+            plane_sigmoids(thK + 4 * tb, a.scale, a.poly, qK + 4 * tb);
+            plane_sigmoids(thQ + 4 * tb, a.scale, a.poly, qQ + 4 * tb);
           }
         }
         if (ok && u > 0) ok = tc::warp_all(tc::mbar_wait(&bars[V3_TF], (u - 1) & 1, abort));
         tc::tc_fence_after();
         if (ok) {
-          float bv[16], av;
-          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * (g >> 1) + 16 * hq, bv);
-          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
-          tc::tmem_wait_ld();
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.pk, t, 2 * hq + ch, pr + 8 * ch);
-          if (mpar == (g & 1)) {
+          for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
+            float pr[16], bv[16];
+            tmem_ldn<16>(tmem + lane_off + T_GB + 64 * (g >> 1) + TB * hq + 16 * tb, bv);
+            corner_probs(qK + 4 * tb, pr);
+            if (t >= nt) {
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 2 * hq + ch, bv + 8 * ch);
-            if (hq == 0) sGA[(g & 1) * GW + mrow] = av;
+              for (int i = 0; i < 16; ++i) pr[i] = 0.f;
+            }
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+              tc::st_row_chunk(sbase + P.pk, t, 2 * (TPW * hq + tb) + ch, pr + 8 * ch);
+            tc::tmem_wait_ld();
+            if (mpar == (g & 1)) {
+#pragma unroll
+              for (int ch = 0; ch < 2; ++ch)
+                tc::st_row_chunk(sbase + P.gbst, mrow, 2 * (TPW * hq + tb) + ch, bv + 8 * ch);
+            }
+          }
+          if (hq == 0) {
+            float av;
+            tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
+            tc::tmem_wait_ld();
+            if (mpar == (g & 1)) sGA[(g & 1) * GW + mrow] = av;
           }
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::named_bar_arrive(N3_PK, NTHR);
+        tc::named_bar_arrive(N3_PK, NT);
         // sGA (double-buffered by group parity: a warp may write the next group's
         // copy while a slower one still reads this one) complete before any read
-        tc::named_bar_sync(N3_GSYNC, NEPI_T);
+        tc::named_bar_sync(N3_GSYNC, NET);
         // ---- W = pq / (A + eps)
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_APREF], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
-          float ap[16], w[16];
-          tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, ap);
-          tc::tmem_wait_ld();
-          if (t < nt) {  // the MMA summed tau < t: the diagonal pk_t in fp32
-            float pk[16];
-            corner_probs(qK, pk);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ap[i] += pk[i];
+          for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
+            float ap[16], w[16];
+            tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, ap);
+            tc::tmem_wait_ld();
+            if (t < nt) {  // the MMA summed tau < t: the diagonal pk_t in fp32
+              float pk[16];
+              corner_probs(qK + 4 * tb, pk);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) ap[i] += pk[i];
+            }
+            corner_probs(qQ + 4 * tb, w);
+            const int sb = g * GW + TB * hq + 16 * tb;
+            add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
+            float *iv = inv + 16 * tb;
+            rcp_n<16>(ap, iv, a.batch_rcp);
+            if (t >= nt) {  // rows past the end: W, dpq, dA and the diagonal terms below all vanish
+#pragma unroll
+              for (int i = 0; i < 16; ++i) iv[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] *= iv[i];
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+              tc::st_row_chunk(sbase + P.w, t, 2 * (TPW * hq + tb) + ch, w + 8 * ch);
           }
-          corner_probs(qQ, w);
-          const int sb = g * GW + 16 * hq;
-          add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
-          rcp_n<16>(ap, inv, a.batch_rcp);
-          if (t >= nt) {  // rows past the end: W, dpq, dA and the corrections below all vanish
-#pragma unroll
-            for (int i = 0; i < 16; ++i) inv[i] = 0.f;
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] *= inv[i];
-#pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * hq + ch, w + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::named_bar_arrive(N3_W, NTHR);
+        tc::named_bar_arrive(N3_W, NT);
         // ---- dA = -W G / (A + eps)
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_G], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
-          float G[16], pq[16], pk[16], corr[16];
-          tc::tmem_ld16(tmem + lane_off + B3_GD + 16 * hq, G);
-          tc::tmem_wait_ld();
-          corner_probs(qQ, pq);
-          corner_probs(qK, pk);
           const bool live = t < nt;
           // Exact diagonal (tau = t), in fp32: the MMAs with P1m and tril cover tau < t only.
           // G gets P1[t][t] pk_t ; dpk gets dA_t + P1[t][t] W_t = W_t (P1[t][t] - dpq_t), which
-          // cancels exactly at the first tokens (carried to the dpk phase in corr).
-          // (rows past the end have inv = 0, so W, dpq, dA and corr are zero there)
+          // cancels exactly at the first tokens (carried to the dpk phase in inv).
+          // (rows past the end have inv = 0, so W, dpq, dA and these terms are zero there)
           const float p1 = sDiag[t];
+          uint32_t pw[2 * TPW];  // d proj_Q of the slot's tables, bf16 pairs
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float g = fmaf(p1, pk[i], G[i]);
-            const float w = pq[i] * inv[i];
-            const float dpq = g * inv[i];
-            const float da = -w * dpq;
-            G[i] = da;
-            corr[i] = fmaf(p1, w, da);
-            inv[i] = dpq;
-          }
+          for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
+            float G[16], pq[16], pk[16], dpq[16];
+            tmem_ldn<16>(tmem + lane_off + B3_GD + TB * hq + 16 * tb, G);
+            tc::tmem_wait_ld();
+            corner_probs(qQ + 4 * tb, pq);
+            corner_probs(qK + 4 * tb, pk);
+            float *iv = inv + 16 * tb;
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) tc::st_row_chunk(sbase + P.da, t, 2 * hq + ch, G + 8 * ch);
-          if (a.dprojQ != nullptr && live) {  // d proj_Q of table 4g + hq -> the fix-up's dQ
+            for (int i = 0; i < 16; ++i) {
+              const float gg = fmaf(p1, pk[i], G[i]);
+              const float w = pq[i] * iv[i];
+              dpq[i] = gg * iv[i];
+              const float da = -w * dpq[i];
+              G[i] = da;
+              iv[i] = fmaf(p1, w, da);  // the diagonal term, carried to the dpk phase
+            }
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+              tc::st_row_chunk(sbase + P.da, t, 2 * (TPW * hq + tb) + ch, G + 8 * ch);
             float dp[4];
-            table_probs_bwd(pq, inv, qQ, thQ, a.scale, dp);
-            uint2 w2;
-            w2.x = tc::pack_bf16(dp[0], dp[1]);
-            w2.y = tc::pack_bf16(dp[2], dp[3]);
-            *reinterpret_cast<uint2 *>(a.dprojQ + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * hq) = w2;
+            table_probs_bwd(pq, dpq, qQ + 4 * tb, thQ + 4 * tb, a.scale, dp);
+            pw[2 * tb] = tc::pack_bf16(dp[0], dp[1]);
+            pw[2 * tb + 1] = tc::pack_bf16(dp[2], dp[3]);
           }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) inv[i] = corr[i];  // carried to the dpk phase
+          if (a.dprojQ != nullptr && live) {  // d proj_Q of the slot's tables -> the fix-up's dQ
+            __nv_bfloat16 *dst = a.dprojQ + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * TPW * hq;
+            if constexpr (TPW == 1)
+              *reinterpret_cast<uint2 *>(dst) = make_uint2(pw[0], pw[1]);
+            else
+              *reinterpret_cast<uint4 *>(dst) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+          }
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
-        tc::named_bar_arrive(N3_DA, NTHR);
+        tc::named_bar_arrive(N3_DA, NT);
         // ---- dpk -> d proj_K
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_DPK], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
-          float dpk[16], pk[16], dp[4];
-          tc::tmem_ld16(tmem + lane_off + B3_R + 16 * hq, dpk);
-          tc::tmem_wait_ld();
-          add_shared_row<16>(sbase + P.ga + 4 * ((g & 1) * GW + 16 * hq), dpk);  // + suffix gA
 #pragma unroll
-          for (int i = 0; i < 16; ++i) dpk[i] += inv[i];  // + the fp32 diagonal term
-          corner_probs(qK, pk);
-          table_probs_bwd(pk, dpk, qK, thK, a.scale, dp);
-          if (t < nt)  // segment-local d proj_K of table 4g + hq, fp32, to the fix-up
-            *reinterpret_cast<float4 *>(a.dprojK + ((size_t)n * a.T + tok0 + t) * HD + 16 * g + 4 * hq) =
-                make_float4(dp[0], dp[1], dp[2], dp[3]);
+          for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
+            float dpk[16], pk[16], dp[4];
+            tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, dpk);
+            tc::tmem_wait_ld();
+            add_shared_row<16>(sbase + P.ga + 4 * ((g & 1) * GW + TB * hq + 16 * tb), dpk);  // + suffix gA
+#pragma unroll
+            for (int i = 0; i < 16; ++i) dpk[i] += inv[16 * tb + i];  // + the fp32 diagonal term
+            corner_probs(qK + 4 * tb, pk);
+            table_probs_bwd(pk, dpk, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
+            if (t < nt)  // segment-local d proj_K of table 4g + TPW hq + tb, fp32, to the fix-up
+              *reinterpret_cast<float4 *>(a.dprojK + ((size_t)n * a.T + tok0 + t) * HD + 16 * g +
+                                          4 * (TPW * hq + tb)) = make_float4(dp[0], dp[1], dp[2], dp[3]);
+          }
         }
       }
       // ---- Q2m[tau = t][t'] = Q2 (summed over the groups) for t' >= tau ; blocks: w (t' < 64),
       // da (t' >= 64), once Q2 and every reader of w and dA completed
-      // (warps below the diagonal, hq < q4, store zeros without reading TMEM)
+      // (32-column runs all below the diagonal store zeros without reading TMEM)
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_D2], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
-        float v[32];
-        if (hq >= q4) {
-          tc::tmem_ld32(tmem + lane_off + B3_X + 32 * hq, v);
-          tc::tmem_wait_ld();
-          if (hq == q4) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < lane) v[i] = 0.f;
+        for (int h = 0; h < CW / 32; ++h) {
+          const int col0 = CW * hq + 32 * h;  // first token column of this run
+          float v[32];
+          if (col0 + 32 > 32 * q4) {
+            tc::tmem_ld32(tmem + lane_off + B3_X + col0, v);
+            tc::tmem_wait_ld();
+            if (col0 < 32 * q4 + 32) {  // the run holds this row's diagonal
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < lane) v[i] = 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
           }
-        } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + 4 * h + ch, v + 8 * ch);
         }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, v + 8 * ch);
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
-      tc::named_bar_arrive(N3_Q2, NTHR);
-      // ---- dK, dV rows
+      tc::named_bar_arrive(N3_Q2, NT);
+      // ---- dV rows
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_OUT], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
-        float vv[16];
-        tc::tmem_ld16(tmem + lane_off + T_DV + 16 * hq, vv);
+        float vv[TB];
+        tmem_ldn<TB>(tmem + lane_off + T_DV + TB * hq, vv);
         tc::tmem_wait_ld();
         if (t < nt) {
-          __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq;
+          __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + TB * hq;
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
+          for (int ch = 0; ch < TB / 8; ++ch) st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
         }
       }
       tc::tc_fence_before();
-      if (k + 1 < nch) tc::named_bar_arrive(N3_OUTFREE, NTHR);
+      if (k + 1 < nch) tc::named_bar_arrive(N3_OUTFREE, NT);
     }
     // ---- segment-local gradient totals (suffix state at the segment start; OUT of the last
     // chunk covers every accumulation)
@@ -673,26 +747,26 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_rev_kernel(const __grid_constant_
       if (ok && nch > 0) {
         for (int b = 0; b < nblk; ++b) {
           const int g = 2 * b + mpar;
-          float bv[16], av;
-          tc::tmem_ld16(tmem + lane_off + T_GB + 64 * b + 16 * hq, bv);
+          float bv[TB], av;
+          tmem_ldn<TB>(tmem + lane_off + T_GB + 64 * b + TB * hq, bv);
           tc::tmem_ld1(tmem + lane_off + T_GA + 16 * b, av);
           tc::tmem_wait_ld();
           if (g < NG) {
-            float *dst = rec + S + (size_t)(g * GW + mrow) * HD + 16 * hq;
+            float *dst = rec + S + (size_t)(g * GW + mrow) * HD + TB * hq;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) dst[i] = bv[i];
+            for (int i = 0; i < TB; ++i) dst[i] = bv[i];
             if (hq == 0) rec[g * GW + mrow] = av;
           }
         }
       } else if (nch == 0) {
-        for (int i = threadIdx.x; i < (int)E; i += NEPI_T) rec[i] = 0.f;
+        for (int i = threadIdx.x; i < (int)E; i += NET) rec[i] = 0.f;
       }
     }
     if (!ok && lane == 0) atomicExch(a.err, 1);
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == NEPI) {
+  if (warp == NE) {
     if (s_abort && lane == 0) atomicExch(a.err, 1);
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);

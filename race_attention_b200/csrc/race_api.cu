@@ -563,10 +563,10 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
     // 2. segment-local reverse walk: dV and d proj_K without the later segments' suffix,
     //    d proj_Q, the segments' local totals
     const fk::BwdSmem rs = fk::bwd_smem_plan(b.LP, b.S);
-    RACE_TRY(set_smem(fk::bwd_rev_kernel, rs.total));
+    RACE_TRY(set_smem(fk::bwd_rev_kernel<fk::REV_TPW>, rs.total));
     {
       KernelScope ks(RACE_KT_BWD_REV, s);
-      fk::bwd_rev_kernel<<<grid, fk::NTHR, rs.total, s>>>(mQ, mK, mV, mO, mB, b);
+      fk::bwd_rev_kernel<fk::REV_TPW><<<grid, 32 * (16 / fk::REV_TPW + 1), rs.total, s>>>(mQ, mK, mV, mO, mB, b);
       ks.stop();
     }
     RACE_TRY(check_launch("fast bwd_rev"));
