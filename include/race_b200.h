@@ -200,6 +200,25 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype,
 
 /* ---- sequence-sharded phases (one rank's contiguous slice of T) ---------- */
 
+/* The fused layer on activations laid out [B, T, H, D] (the layout attention modules
+ * produce before any transpose; stream n = b*H + h, N = B*H), forward with the chunk
+ * states kept in `saved` (race_saved_bytes(B*H, ...), may be NULL) and backward reusing
+ * them.  Workspace sizes as race_fwd_qkv / race_bwd_qkv with N = B*H.  No reference
+ * counterpart: chat/nanochat/gpt.py:133-139 transposes q, k, v to [B, H, T, D] and the
+ * output back around the RACE call.  tcgen05 path only (bf16, D = 64, P = 4, L in {8, 16});
+ * other configurations return RACE_ERR_UNSUPPORTED. */
+int race_fwd_bthd(const void *Q, const void *K, const void *V, int dtype,
+                  const float *planes_T, void *out, void *saved, size_t saved_bytes,
+                  int64_t B, int64_t T, int64_t H, int64_t D, int64_t L, int64_t P,
+                  float eps, float logit_scale,
+                  void *workspace, size_t workspace_bytes, void *stream);
+int race_bwd_bthd(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                  const float *planes_T, const void *saved, size_t saved_bytes,
+                  void *dQ, void *dK, void *dV,
+                  int64_t B, int64_t T, int64_t H, int64_t D, int64_t L, int64_t P,
+                  float eps, float logit_scale,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
 /* Forward of a shard in two calls on ONE workspace (RACE_OP_FWD_SPLIT size):
  * race_fwd_local writes this shard's state totals A_tot[N,S], B_tot[N,S,D]
  * (what race_state_from_prefill with A0 = B0 = NULL writes) and keeps its

@@ -46,6 +46,9 @@ SIGNATURES = {
                      _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
     "race_state_from_prefill": [_P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
     "race_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P],
+    "race_fwd_bthd": [_P, _P, _P, _I, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
+    "race_bwd_bthd": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _P,
+                      _SZ, _P],
     "race_fwd_local": [_P, _P, _I, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
     "race_fwd_finish": [_P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ,
                         _P],

@@ -35,6 +35,7 @@ constexpr int GW = 64;  // buckets per backward group
 
 struct BwdArgs {
   int N, T, L, LP, S, ngroups;  // ngroups = S / 64
+  int H;                        // heads of the activation layout (act_row); dVloc follows it too
   int nseg, seg_chunks, nchunks;
   float eps, scale;
   int poly;                 // plane sigmoids by series (2|scale| <= 1/2)
@@ -221,6 +222,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int hn = n % a.H, bn = n / a.H;  // head and batch of stream n in the activation layout
   const int c_begin = seg * a.seg_chunks;
   const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
   const int S = a.S, NG = a.ngroups, nblk = (NG + 1) / 2;
@@ -257,14 +259,14 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
     auto load_qk = [=, &tmQ, &tmK](int c) {
       const int t0 = (c_begin + c) * C;
       tc::mbar_arrive_expect_tx(&bars[V3_QK], 2 * TILE);
-      tc::tma_load_3d(sm + oq, &tmQ, &bars[V3_QK], 0, t0, n);
-      tc::tma_load_3d(sm + ok_, &tmK, &bars[V3_QK], 0, t0, n);
+      tc::tma_load_4d(sm + oq, &tmQ, &bars[V3_QK], 0, hn, t0, bn);
+      tc::tma_load_4d(sm + ok_, &tmK, &bars[V3_QK], 0, hn, t0, bn);
     };
     auto load_vo = [=, &tmV, &tmO](int c) {
       const int t0 = (c_begin + c) * C;
       tc::mbar_arrive_expect_tx(&bars[V3_VO], 2 * TILE);
-      tc::tma_load_3d(sm + ov, &tmV, &bars[V3_VO], 0, t0, n);
-      tc::tma_load_3d(sm + oo, &tmO, &bars[V3_VO], 0, t0, n);
+      tc::tma_load_4d(sm + ov, &tmV, &bars[V3_VO], 0, hn, t0, bn);
+      tc::tma_load_4d(sm + oo, &tmO, &bars[V3_VO], 0, hn, t0, bn);
     };
     auto load_bst = [=, &tmB](int c, int g) {
       const int row = (int)(((size_t)n * nchunks + c_begin + c) * S + g * GW);
@@ -732,7 +734,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         tmem_ldn<TB>(tmem + lane_off + T_DV + TB * hq, vv);
         tc::tmem_wait_ld();
         if (t < nt) {
-          __nv_bfloat16 *dv = a.dV + ((size_t)n * a.T + tok0 + t) * HD + TB * hq;
+          __nv_bfloat16 *dv = a.dV + act_row(bn, hn, tok0 + t, a.T, a.H) + TB * hq;
 #pragma unroll
           for (int ch = 0; ch < TB / 8; ++ch) st_bf16x8_global(dv + 8 * ch, vv + 8 * ch);
         }
@@ -841,6 +843,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int hn = n % a.H, bn = n / a.H;  // head and batch of stream n in the activation layout
   const int c_begin = seg * a.seg_chunks;
   const int nch = min(a.nchunks, c_begin + a.seg_chunks) - c_begin;
   const int S = a.S, LP = a.LP;
@@ -869,19 +872,19 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
     auto load = [=, &tmK, &tmV, &tmDQ](int c) {
       const int t0 = (c_begin + c) * C;
       tc::mbar_arrive_expect_tx(&bars[VF_KV], 3 * TILE);
-      tc::tma_load_3d(sm + ok_, &tmK, &bars[VF_KV], 0, t0, n);
-      tc::tma_load_3d(sm + ov, &tmV, &bars[VF_KV], 0, t0, n);
-      tc::tma_load_3d(sm + oq, &tmDQ, &bars[VF_KV], 0, t0, n);
+      tc::tma_load_4d(sm + ok_, &tmK, &bars[VF_KV], 0, hn, t0, bn);
+      tc::tma_load_4d(sm + ov, &tmV, &bars[VF_KV], 0, hn, t0, bn);
+      tc::tma_load_3d(sm + oq, &tmDQ, &bars[VF_KV], 0, t0, n);  // d proj_Q: [N, T, 64] workspace
     };
     auto load_dvl = [=, &tmVL](int c) {
       tc::mbar_arrive_expect_tx(&bars[VF_DVL], TILE);
-      tc::tma_load_3d(sm + P.dvl, &tmVL, &bars[VF_DVL], 0, (c_begin + c) * C, n);
+      tc::tma_load_4d(sm + P.dvl, &tmVL, &bars[VF_DVL], 0, hn, (c_begin + c) * C, bn);
     };
     auto store_out = [=, &tmOK, &tmOV, &tmOQ](int c) {
       const int t0 = (c_begin + c) * C;
-      tc::tma_store_3d(&tmOK, sm + P.dp, 0, t0, n);
-      tc::tma_store_3d(&tmOV, sm + P.dvl, 0, t0, n);
-      tc::tma_store_3d(&tmOQ, sm + P.dplo, 0, t0, n);
+      tc::tma_store_4d(&tmOK, sm + P.dp, 0, hn, t0, bn);
+      tc::tma_store_4d(&tmOV, sm + P.dvl, 0, hn, t0, bn);
+      tc::tma_store_4d(&tmOQ, sm + P.dplo, 0, hn, t0, bn);
       tc::bulk_commit();
     };
     auto issue_proj = [=]() {  // proj = K planes for the chunk in the tiles

@@ -43,8 +43,18 @@ constexpr uint32_t TILE = C * 128;  // one [128 x 64] bf16 tile = 16 KB
 // TMEM column map of the forward kernel (512 columns allocated)
 constexpr uint32_t T_PK = 0, T_PQ = 64, T_G = 128, T_OUT = 256, T_B = 320;
 
+// Activations (Q, K, V, out; dO, dQ, dK, dV) are [B, T, H, 64] bf16 with N = B H streams,
+// stream n = b H + h: H = 1 is the [N, T, 64] layout, H = heads the [B, T, H, 64] layout
+// attention modules produce.  TMA reads and writes them through 4-D maps (64, H, T, B),
+// box (64, 1, 128, 1); act_row gives the element offset of token t of stream (b, h) for
+// plain loads/stores.
+__host__ __device__ __forceinline__ size_t act_row(int b, int h, int t, int T, int H) {
+  return ((size_t)b * T + t) * H * 64 + (size_t)h * 64;
+}
+
 struct FwdArgs {
   int N, T, L, LP, S, ngroups;
+  int H;                  // heads of the activation layout (see act_row)
   int nseg, seg_chunks, nchunks;  // chunks per segment; total chunks per stream
   float eps, scale;
   int poly;               // plane sigmoids by series (2|scale| <= 1/2)
@@ -225,6 +235,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int hn = n % a.H, bn = n / a.H;  // head and batch of stream n in the activation layout
   const int c_begin = seg * a.seg_chunks;
   const int c_end = min(a.nchunks, c_begin + a.seg_chunks);
   const int nch = c_end - c_begin;
@@ -251,13 +262,13 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
     auto load_qk = [=, &tmQ, &tmK](int c) {
       const int t0 = (c_begin + c) * C;
       tc::mbar_arrive_expect_tx(&bars[B_QK], 2 * TILE);
-      tc::tma_load_3d(sm + oq, &tmQ, &bars[B_QK], 0, t0, n);
-      tc::tma_load_3d(sm + ok_, &tmK, &bars[B_QK], 0, t0, n);
+      tc::tma_load_4d(sm + oq, &tmQ, &bars[B_QK], 0, hn, t0, bn);
+      tc::tma_load_4d(sm + ok_, &tmK, &bars[B_QK], 0, hn, t0, bn);
     };
     auto load_v = [=, &tmV](int c) {
       const int st = c & 1;
       tc::mbar_arrive_expect_tx(&bars[B_V0 + st], TILE);
-      tc::tma_load_3d(sm + ov + st * TILE, &tmV, &bars[B_V0 + st], 0, (c_begin + c) * C, n);
+      tc::tma_load_4d(sm + ov + st * TILE, &tmV, &bars[B_V0 + st], 0, hn, (c_begin + c) * C, bn);
     };
     const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
     const uint32_t id_apref = tc::idesc_bf16(C, GB, false, true);
@@ -530,7 +541,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
         tc::tmem_ld16(tmem + lane_off + T_OUT + 16 * hq, ov);
         tc::tmem_wait_ld();
         if (t < nt) {
-          uint4 *dst = reinterpret_cast<uint4 *>(a.out + ((size_t)n * a.T + tok0 + t) * HD + 16 * hq);
+          uint4 *dst = reinterpret_cast<uint4 *>(a.out + act_row(bn, hn, tok0 + t, a.T, a.H) + 16 * hq);
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) {
             uint4 w4;
@@ -594,6 +605,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
+  const int hn = n % a.H, bn = n / a.H;  // head and batch of stream n in the activation layout
   const int c_begin = seg * a.seg_chunks;
   const int c_end = min(a.nchunks, c_begin + a.seg_chunks);
   const int nch = c_end - c_begin;
@@ -626,8 +638,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       tc::prefetch_tmap(&tmV);
       for (int c = 0; c < 2 && c < nch; ++c) {
         tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + c], 2 * TILE);
-        tc::tma_load_3d(sm + P.k + c * TILE, &tmK, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
-        tc::tma_load_3d(sm + P.v + c * TILE, &tmV, &bars[TB_FULL0 + c], 0, (c_begin + c) * C, n);
+        tc::tma_load_4d(sm + P.k + c * TILE, &tmK, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
+        tc::tma_load_4d(sm + P.v + c * TILE, &tmV, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
       }
       const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
       const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
@@ -660,8 +672,10 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           ok = tc::mbar_wait(&bars[TB_DONE], c & 1, abort);
           if (!ok) break;
           tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + st], 2 * TILE);
-          tc::tma_load_3d(sm + P.k + st * TILE, &tmK, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
-          tc::tma_load_3d(sm + P.v + st * TILE, &tmV, &bars[TB_FULL0 + st], 0, (c_begin + c + 2) * C, n);
+          tc::tma_load_4d(sm + P.k + st * TILE, &tmK, &bars[TB_FULL0 + st], 0, hn, (c_begin + c + 2) * C,
+                          bn);
+          tc::tma_load_4d(sm + P.v + st * TILE, &tmV, &bars[TB_FULL0 + st], 0, hn, (c_begin + c + 2) * C,
+                          bn);
         }
       }
       tc::mma_commit(&bars[TB_FINAL]);

@@ -110,6 +110,26 @@ inline bool make_map(CUtensorMap *m, const void *base, int64_t N, int64_t T) {
   return r == CUDA_SUCCESS;
 }
 
+// Activation tensor [B, T, H, 64] bf16 (N = B H streams; H = 1: [N, T, 64]) as a 4-D map
+// (64, H, T, B), box (64, 1, 128, 1): one stream's 128-token tile per copy, rows past T read
+// as zero (loads) or are not written (stores).
+inline bool make_act_map(CUtensorMap *m, const void *base, int64_t N, int64_t T, int64_t H) {
+  EncodeTiledFn enc = encoder();
+  if (!enc || H < 1 || N % H != 0) {
+    last_encode_status() = -1;
+    return false;
+  }
+  cuuint64_t dims[4] = {(cuuint64_t)fk::HD, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)(N / H)};
+  cuuint64_t strides[3] = {(cuuint64_t)fk::HD * 2, (cuuint64_t)H * fk::HD * 2, (cuuint64_t)T * H * fk::HD * 2};
+  cuuint32_t box[4] = {(cuuint32_t)fk::HD, 1, (cuuint32_t)fk::C, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  last_encode_status() = (int)r;
+  return r == CUDA_SUCCESS;
+}
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Backward workspace: status | forward segment records | backward segment

@@ -380,6 +380,7 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
               const float *planes_T, void *ws) {
   a.N = (int)N;
   a.T = (int)T;
+  a.H = 1;
   a.L = (int)L;
   a.LP = (int)(4 * L);
   a.S = (int)(16 * L);
@@ -405,16 +406,17 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
 // Plan, kernel arguments and K/V tensor maps of the forward kernels.
 int fast_prepare(const void *K, const void *V, const float *planes_T, int64_t N, int64_t T, int64_t L, float eps,
                  float scale, void *ws, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, fh::Plan &pl,
-                 size_t rec_off = 0) {
+                 size_t rec_off = 0, int64_t H = 1) {
   const int64_t S = 16 * L;
   if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
   pl = fh::plan(N, T, S, fh::sm_count());
   if (rec_off) pl.rec_off = rec_off;
   fast_args(a, pl, N, T, L, eps, scale, planes_T, ws);
-  if (!fh::make_map(&mK, K, N, T))
+  a.H = (int)H;
+  if (!fh::make_act_map(&mK, K, N, T, H))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(K %p, N=%lld, T=%lld) failed: CUresult %d", K, (long long)N,
                 (long long)T, fh::last_encode_status());
-  if (!fh::make_map(&mV, V, N, T))
+  if (!fh::make_act_map(&mV, V, N, T, H))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(V %p, N=%lld, T=%lld) failed: CUresult %d", V, (long long)N,
                 (long long)T, fh::last_encode_status());
   return RACE_OK;
@@ -422,10 +424,11 @@ int fast_prepare(const void *K, const void *V, const float *planes_T, int64_t N,
 
 int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, const float *A0, const float *B0,
                          float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
-                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, size_t rec_off = 0) {
+                         cudaStream_t s, fk::FwdArgs &a, CUtensorMap &mK, CUtensorMap &mV, size_t rec_off = 0,
+                         int64_t H = 1) {
   const int64_t S = 16 * L;
   fh::Plan pl;
-  RACE_TRY(fast_prepare(K, V, planes_T, N, T, L, eps, scale, ws, a, mK, mV, pl, rec_off));
+  RACE_TRY(fast_prepare(K, V, planes_T, N, T, L, eps, scale, ws, a, mK, mV, pl, rec_off, H));
   cudaError_t e = cudaMemsetAsync(at<int>(ws, pl.status_off), 0, sizeof(int), s);
   if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   const fk::TotSmem ts = fk::tot_smem_plan(a.ngroups, a.LP);
@@ -449,18 +452,18 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
 // earlier shards' state, are added to each as the readout loads it.
 int fast_forward(const void *Q, const void *K, const void *V, const float *planes_T, void *out, const float *A0,
                  const float *B0, float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale,
-                 void *ws, cudaStream_t s, void *saved = nullptr, bool finish = false) {
+                 void *ws, cudaStream_t s, void *saved = nullptr, bool finish = false, int64_t H = 1) {
   fk::FwdArgs a;
   CUtensorMap mQ, mK, mV;
   if (finish) {
     fh::Plan pl;
-    RACE_TRY(fast_prepare(K, V, planes_T, N, T, L, eps, scale, ws, a, mK, mV, pl));
+    RACE_TRY(fast_prepare(K, V, planes_T, N, T, L, eps, scale, ws, a, mK, mV, pl, 0, H));
     a.seedA = A0;
     a.seedB = B0;
   } else {
-    RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV));
+    RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, Af, Bf, N, T, L, eps, scale, ws, s, a, mK, mV, 0, H));
   }
-  if (!fh::make_map(&mQ, Q, N, T))
+  if (!fh::make_act_map(&mQ, Q, N, T, H))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(Q) failed: CUresult %d", fh::last_encode_status());
   a.out = static_cast<__nv_bfloat16 *>(out);
   if (saved != nullptr) {
@@ -486,7 +489,7 @@ enum BwdMode { BWD_FULL = 0, BWD_LOCAL, BWD_FINISH };
 int fast_backward(const void *Q, const void *K, const void *V, const void *dO, const float *planes_T, void *dQ,
                   void *dK, void *dV, const float *A0, const float *B0, const float *gA, const float *gB, float *dA0,
                   float *dB0, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws, cudaStream_t s,
-                  BwdMode mode, const void *saved = nullptr) {
+                  BwdMode mode, const void *saved = nullptr, int64_t H = 1) {
   const int64_t S = 16 * L;
   const fh::BwdPlan bp = fh::bwd_plan(N, T, S, fh::sm_count(), mode != BWD_FULL);
   fk::FwdArgs fa;
@@ -500,10 +503,10 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   if (rebuild) {
     // forward segment prefixes (exclusive, seeded with the carried-in state)
     RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, nullptr, nullptr, N, T, L, eps, scale, ws, s, fa, mK, mV,
-                                  bp.fwd_rec));
+                                  bp.fwd_rec, H));
   } else {
     if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
-    if (!fh::make_map(&mK, K, N, T) || !fh::make_map(&mV, V, N, T))
+    if (!fh::make_act_map(&mK, K, N, T, H) || !fh::make_act_map(&mV, V, N, T, H))
       return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled(K/V) failed: CUresult %d", fh::last_encode_status());
     if (mode != BWD_FINISH) {
       cudaError_t e = cudaMemsetAsync(at<int>(ws, 0), 0, sizeof(int), s);
@@ -511,13 +514,14 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
     }
   }
   if (!fh::make_map(&mP, at<void>(ws, bp.dprojQ), N, T) ||
-      (mode != BWD_FINISH && (!fh::make_map(&mQ, Q, N, T) || !fh::make_map(&mO, dO, N, T) ||
+      (mode != BWD_FINISH && (!fh::make_act_map(&mQ, Q, N, T, H) || !fh::make_act_map(&mO, dO, N, T, H) ||
                               !fh::make_rows_map(&mB, chunkB, N * (int64_t)bp.p.nchunks * S))))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed in the backward: CUresult %d",
                 fh::last_encode_status());
   fk::BwdArgs b;
   b.N = (int)N;
   b.T = (int)T;
+  b.H = (int)H;
   b.L = (int)L;
   b.LP = (int)(4 * L);
   b.S = (int)S;
@@ -591,8 +595,8 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   }
   // tile maps of the walk's dV (read) and of the outputs (written by TMA tile stores)
   CUtensorMap mVL, mOK, mOV, mOQ;
-  if (!fh::make_map(&mVL, b.dVloc ? (void *)b.dVloc : dV, N, T) || !fh::make_map(&mOK, dK, N, T) ||
-      !fh::make_map(&mOV, dV, N, T) || !fh::make_map(&mOQ, dQ, N, T))
+  if (!fh::make_act_map(&mVL, b.dVloc ? (void *)b.dVloc : dV, N, T, H) || !fh::make_act_map(&mOK, dK, N, T, H) ||
+      !fh::make_act_map(&mOV, dV, N, T, H) || !fh::make_act_map(&mOQ, dQ, N, T, H))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fix-up's dV/dK/dQ: CUresult %d",
                 fh::last_encode_status());
   const fk::FixSmem xs = fk::fix_smem_plan(b.LP, b.S);
@@ -813,12 +817,14 @@ int race_soft_hash_bwd(const void *X, int dtype, const float *planes_T, const fl
 static int fwd_qkv_impl(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
                         const float *A0, const float *B0, float *A_final, float *B_final, void *saved,
                         size_t saved_bytes, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
-                        float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+                        float logit_scale, void *workspace, size_t workspace_bytes, void *stream, int64_t H = 1) {
   RACE_NONNULL(Q);
   RACE_NONNULL(K);
   RACE_NONNULL(V);
   RACE_NONNULL(planes_T);
   RACE_NONNULL(out);
+  if (H > 1 && !fh::eligible(dtype, D, L, P))
+    return fail(RACE_ERR_UNSUPPORTED, "the [B, T, H, D] layout needs the tcgen05 path (bf16, D=64, P=4, L in {8,16})");
   RACE_TRY(check_dtype(dtype));
   int64_t S = 0;
   RACE_TRY(check_lp(L, P, &S));
@@ -834,7 +840,7 @@ static int fwd_qkv_impl(const void *Q, const void *K, const void *V, int dtype, 
       if (!fh::aligned16(saved)) return fail(RACE_ERR_ALIGN, "saved-state buffer must be 16-byte aligned");
     }
     RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, A_final, B_final, N, T, L, eps, logit_scale, workspace, s,
-                          saved));
+                          saved, false, H));
     return ok();
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total));
@@ -852,11 +858,13 @@ static int bwd_qkv_impl(const void *Q, const void *K, const void *V, const void 
                         const float *planes_T, const void *saved, size_t saved_bytes, void *dQ, void *dK, void *dV,
                         const float *A0, const float *B0, const float *gA_in, const float *gB_in, float *dA0,
                         float *dB0, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps,
-                        float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+                        float logit_scale, void *workspace, size_t workspace_bytes, void *stream, int64_t H = 1) {
   RACE_NONNULL(Q);
   RACE_NONNULL(K);
   RACE_NONNULL(V);
   RACE_NONNULL(dO);
+  if (H > 1 && !fh::eligible(dtype, D, L, P))
+    return fail(RACE_ERR_UNSUPPORTED, "the [B, T, H, D] layout needs the tcgen05 path (bf16, D=64, P=4, L in {8,16})");
   RACE_NONNULL(planes_T);
   RACE_NONNULL(dQ);
   RACE_NONNULL(dK);
@@ -876,7 +884,7 @@ static int bwd_qkv_impl(const void *Q, const void *K, const void *V, const void 
       if (!fh::aligned16(saved)) return fail(RACE_ERR_ALIGN, "saved-state buffer must be 16-byte aligned");
     }
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, L, eps,
-                           logit_scale, workspace, s, BWD_FULL, saved));
+                           logit_scale, workspace, s, BWD_FULL, saved, H));
     return ok();
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
@@ -906,6 +914,24 @@ int race_bwd_qkv(const void *Q, const void *K, const void *V, const void *dO, in
                  float eps, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
   return bwd_qkv_impl(Q, K, V, dO, dtype, planes_T, nullptr, 0, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, D,
                       L, P, eps, logit_scale, workspace, workspace_bytes, stream);
+}
+
+int race_fwd_bthd(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out,
+                  void *saved, size_t saved_bytes, int64_t B, int64_t T, int64_t H, int64_t D, int64_t L, int64_t P,
+                  float eps, float logit_scale, void *workspace, size_t workspace_bytes, void *stream) {
+  if (B < 1 || H < 1) return fail(RACE_ERR_SHAPE, "B and H must be >= 1");
+  return fwd_qkv_impl(Q, K, V, dtype, planes_T, out, nullptr, nullptr, nullptr, nullptr, saved, saved_bytes, B * H, T,
+                      D, L, P, eps, logit_scale, workspace, workspace_bytes, stream, H);
+}
+
+int race_bwd_bthd(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                  const void *saved, size_t saved_bytes, void *dQ, void *dK, void *dV, int64_t B, int64_t T,
+                  int64_t H, int64_t D, int64_t L, int64_t P, float eps, float logit_scale, void *workspace,
+                  size_t workspace_bytes, void *stream) {
+  if (B < 1 || H < 1) return fail(RACE_ERR_SHAPE, "B and H must be >= 1");
+  return bwd_qkv_impl(Q, K, V, dO, dtype, planes_T, saved, saved_bytes, dQ, dK, dV, nullptr, nullptr, nullptr,
+                      nullptr, nullptr, nullptr, B * H, T, D, L, P, eps, logit_scale, workspace, workspace_bytes,
+                      stream, H);
 }
 
 int race_saved_bytes(int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, int dtype, size_t *bytes) {

@@ -274,6 +274,55 @@ def bwd_qkv(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0
     return (dQ, dK, dV, dA0, dB0) if return_state_grad else (dQ, dK, dV)
 
 
+def _bthd_common(Q, K, V, planes_T, L, P, logit_scale):
+    dev = _check_cuda(Q, K, V, planes_T)
+    if Q.dim() != 4 or not (Q.shape == K.shape == V.shape):
+        raise RuntimeError("Q, K, V must have the same [B,T,H,D] shape")
+    if not (Q.dtype == K.dtype == V.dtype):
+        raise RuntimeError("Q, K, V must have the same dtype")
+    Bn, T, H, D = Q.shape
+    if not fast_path(Q.dtype, D, L, P):
+        raise RuntimeError("the [B,T,H,D] layout needs bf16, D=64, P=4, L in {8,16}")
+    planes_T = planes_T.to(torch.float32).contiguous()
+    if planes_T.shape != (D, L * P):
+        raise RuntimeError(f"planes_T must be [D, L*P] = [{D}, {L * P}]")
+    scale = default_logit_scale(D) if logit_scale is None else float(logit_scale)
+    return dev, Q.contiguous(), K.contiguous(), V.contiguous(), planes_T, Bn, T, H, D, L << P, scale
+
+
+def fwd_bthd(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None):
+    """Fused layer on [B,T,H,D] activations (no transposes): (out [B,T,H,D], saved chunk states)."""
+    dev, Q, K, V, planes_T, Bn, T, H, D, S, scale = _bthd_common(Q, K, V, planes_T, L, P, logit_scale)
+    N = Bn * H
+    out = torch.empty_like(Q)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_FWD_QKV, N, T, S, D, L, P, _dtype_code(Q), dev)
+        sb = saved_bytes(N, T, D, L, P, Q.dtype)
+        saved = torch.empty(max(sb, 1), dtype=torch.uint8, device=dev)
+        _lib.check(lib.race_fwd_bthd(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out), _ptr(saved),
+                                     sb, Bn, T, H, D, L, P, float(eps), scale, _ptr(ws), nb, _stream(dev)),
+                   "race_fwd_bthd")
+        _check_status(ws, "race_fwd_bthd")
+    return out, saved
+
+
+def bwd_bthd(Q, K, V, dO, planes_T, L, P, saved, eps=1e-6, logit_scale=None):
+    """(dQ, dK, dV) [B,T,H,D] of fwd_bthd, reusing its saved chunk states."""
+    dev, Q, K, V, planes_T, Bn, T, H, D, S, scale = _bthd_common(Q, K, V, planes_T, L, P, logit_scale)
+    N = Bn * H
+    dO = dO.to(Q.dtype).contiguous()
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_BWD_QKV, N, T, S, D, L, P, _dtype_code(Q), dev)
+        _lib.check(lib.race_bwd_bthd(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T), _ptr(saved),
+                                     saved.numel(), _ptr(dQ), _ptr(dK), _ptr(dV), Bn, T, H, D, L, P, float(eps), scale,
+                                     _ptr(ws), nb, _stream(dev)), "race_bwd_bthd")
+        _check_status(ws, "race_bwd_bthd")
+    return dQ, dK, dV
+
+
 def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None):
     """(A[N,S], B[N,S,D]) fp32 state after the prefill tokens K, V [N,T,D]."""
     dev, K, _, V, planes_T, N, T, D, S, scale = _qkv_common(K, K, V, planes_T, L, P, logit_scale)

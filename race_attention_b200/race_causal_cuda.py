@@ -86,6 +86,49 @@ def race_causal(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None):
     return RaceQKVFn.apply(Q, K, V, planes_T, L, P, eps, logit_scale)
 
 
+class RaceBTHDFn(Function):
+    """Fused causal RACE on q, k, v laid out [B,T,H,D] (tcgen05 configurations)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, planes_T, L, P, eps, logit_scale):
+        out, saved = ops.fwd_bthd(q, k, v, planes_T, L, P, eps, logit_scale)
+        ctx.save_for_backward(q, k, v, planes_T, saved)
+        ctx.cfg = (L, P, eps, logit_scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dO):
+        q, k, v, planes_T, saved = ctx.saved_tensors
+        L, P, eps, scale = ctx.cfg
+        dq, dk, dv = ops.bwd_bthd(q, k, v, dO, planes_T, L, P, saved, eps, scale)
+        return dq, dk, dv, None, None, None, None, None
+
+
+def race_causal_bthd(q, k, v, planes_T, L, P, eps=1e-6, logit_scale=None):
+    """Causal RACE of q, k, v [B,T,H,D] -> [B,T,H,D], the layout attention modules project
+    into.  bf16 with D = 64, P = 4, L in {8, 16} reads and writes it in place through the
+    kernels' tensor maps; other configurations run race_causal on [B,H,T,D] copies."""
+    D = q.shape[-1]
+    if q.dim() == 4 and q.dtype == k.dtype == v.dtype and ops.fast_path(q.dtype, D, L, P):
+        return RaceBTHDFn.apply(q, k, v, planes_T, L, P, eps, logit_scale)
+    t = lambda x: x.transpose(1, 2).contiguous()  # noqa: E731
+    return race_causal(t(q), t(k), t(v), planes_T, L, P, eps, logit_scale).transpose(1, 2)
+
+
+def nanochat_race_attention(q, k, v, planes_T, race_L, race_K, race_M=1, race_eps=1e-6):
+    """The RACE branch of nanochat's CausalSelfAttention.forward (chat/nanochat/gpt.py:131-142):
+    q, k, v [B,T,H,D] after rotary embedding and QK norm -> y [B,T,H,D] in q's dtype.
+    The reference upcasts to fp32 and transposes to [B,H,T,D] around soft_hash_probs +
+    RaceCausalFn and averages the M members, which with shared planes are identical copies;
+    here bf16 activations stay bf16 (fp32 accumulation and state) and the layout is read in
+    place."""
+    del race_M  # shared planes: every ensemble member is the same computation
+    if q.dtype == torch.bfloat16:
+        return race_causal_bthd(q, k, v, planes_T, race_L, race_K, race_eps)
+    y = race_causal_bthd(q.float(), k.float(), v.float(), planes_T, race_L, race_K, race_eps)
+    return y.to(q.dtype)
+
+
 class RaceCausalCuda(nn.Module):
     """Causal RACE over Q,K,V: [B,H,T,D] -> [B,H,T,D] on the B200 kernels.
 

@@ -103,3 +103,18 @@ def test_kernel_timing_host_side():
     assert ms.value == 0.0 and n.value == 0
     assert lib.race_kernel_time(len(_lib.KERNEL_NAMES), ctypes.byref(ms), ctypes.byref(n)) != 0
     assert lib.race_kernel_timing(0) == 0
+
+
+def test_bthd_layout_needs_tcgen05_path():
+    """The [B,T,H,D] entry points reject configurations the tcgen05 kernels do not run
+    (fp32 here) before any GPU work."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    codes = status_codes()
+    rc = lib.race_fwd_bthd(p, p, p, _lib.RACE_F32, p, p, None, 0, 2, 128, 3, 64, 8, 4, 1e-6, 0.125, p, 1 << 20, None)
+    assert rc == codes["RACE_ERR_UNSUPPORTED"]
+    rc = lib.race_bwd_bthd(p, p, p, p, _lib.RACE_F32, p, None, 0, p, p, p, 2, 128, 3, 64, 8, 4, 1e-6, 0.125, p,
+                           1 << 20, None)
+    assert rc == codes["RACE_ERR_UNSUPPORTED"]
+    assert lib.race_fwd_bthd(p, p, p, _lib.RACE_BF16, p, p, None, 0, 0, 128, 3, 64, 8, 4, 1e-6, 0.125, p, 1 << 20,
+                             None) == codes["RACE_ERR_SHAPE"]

@@ -226,3 +226,47 @@ def test_saved_states_backward(B, H, T, L):
     q, k, v = (x.clone().requires_grad_(True) for x in args)
     rb.race_causal(q, k, v, pc, L, 4).backward(dO.cuda())
     assert relerr(q.grad, g_saved[0]) < 1e-6 and relerr(k.grad, g_saved[1]) < 1e-6
+
+
+@pytest.mark.parametrize("B,H,T,L", [(2, 3, 333, 8), (1, 4, 1200, 16)])
+def test_bthd_layout_matches_bhtd(B, H, T, L):
+    """q, k, v in the attention module's [B,T,H,D] layout (strided tensor maps, no
+    transposes) give exactly the [B,H,T,D] results and gradients: same kernels, same
+    segment plan, only the addressing differs."""
+    import race_attention_b200 as rb
+    D, P = 64, 4
+    g = torch.Generator().manual_seed(B * 100 + T)
+    q, k, v, do = (torch.randn(B, T, H, D, generator=g).mul_(0.125).to(torch.bfloat16).cuda() for _ in range(4))
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device="cpu", seed=0)
+    pc = planes.cuda()
+    a = [x.clone().requires_grad_(True) for x in (q, k, v)]
+    y = rb.race_causal_bthd(*a, pc, L, P)
+    y.backward(do)
+    t = lambda x: x.transpose(1, 2).contiguous().requires_grad_(True)  # noqa: E731
+    b = [t(x) for x in (q, k, v)]
+    y2 = rb.race_causal(*b, pc, L, P)
+    y2.backward(do.transpose(1, 2).contiguous())
+    torch.cuda.synchronize()
+    assert y.shape == (B, T, H, D)
+    assert torch.equal(y, y2.transpose(1, 2))
+    for ga, gb in zip(a, b):
+        assert torch.equal(ga.grad, gb.grad.transpose(1, 2))
+
+
+def test_nanochat_attention_branch():
+    """nanochat's RACE branch (fp32 transposes, soft_hash_probs + RaceCausalFn, mean over
+    M) against the drop-in on the same post-rotary q, k, v: fp32 goes through the
+    [B,H,T,D] path (rel 1e-4), bf16 through the in-place layout (rel 2e-2)."""
+    import race_attention_b200 as rb
+    B, T, H, D, L, P, M = 2, 300, 2, 64, 8, 4, 2
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(B, T, H, D, generator=g) for _ in range(3))
+    planes, protos = rb.build_planes_protos(D, P, L, M, device="cpu", seed=0)
+    tr = lambda x: x.transpose(1, 2).contiguous()  # noqa: E731
+    ref, _, _ = O.race_qkv_fwd(tr(q).reshape(B * H, T, D), tr(k).reshape(B * H, T, D), tr(v).reshape(B * H, T, D),
+                               planes, L, P)
+    ref = torch.as_tensor(np.asarray(ref, dtype=np.float64)).reshape(B, H, T, D).transpose(1, 2)
+    y32 = rb.nanochat_race_attention(q.cuda(), k.cuda(), v.cuda(), planes.cuda(), L, P, M, 1e-6)
+    assert y32.dtype == torch.float32 and relerr(y32.cpu(), ref) < 1e-4
+    yb = rb.nanochat_race_attention(*(x.to(torch.bfloat16).cuda() for x in (q, k, v)), planes.cuda(), L, P, M, 1e-6)
+    assert yb.dtype == torch.bfloat16 and relerr(yb.float().cpu(), ref) < 2e-2
