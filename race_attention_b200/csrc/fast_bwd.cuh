@@ -793,12 +793,14 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
 // the d proj tiles, dV rows in the tile the walk's dV came in through), not per-thread
 // 16-byte stores that split every warp instruction into 32 row transactions.
 //   control: [KV] proj = K (planes_hi + planes_lo) -> [PROJ] ;
-//            {OUTFREE} store the previous chunk's dK, dV, dQ tiles, wait until they are read,
-//            load this chunk's dV tile -> [DVL], Dfix = V gB_in^T -> [DPK] ;
-//            dQ = dprojQ planes ; {PK} dV = Pk gB_in ; {DP} dK = dproj planes -> [OUT]
-//   epilogue: [PROJ] Pk {PK} ; [DPK] dproj = softmax bwd of (Dfix + gA_in) {DP} ;
+//            {OUTFREE} store the previous chunk's dK, dV, dQ tiles ; Dfix = V gB_in^T -> [DPK] ;
+//            dQ = dprojQ planes -> [TFREE] ; once the stores have read the tiles: this chunk's
+//            dV tile -> [DVL], d proj tiles free -> [SFREE] ;
+//            {PK} dV = Pk gB_in ; {DP} dK = dproj planes -> [OUT]
+//   epilogue: [PROJ] Pk {PK} ; [DPK] dproj = softmax bwd of (Dfix + gA_in), [SFREE] into the
+//             d proj tiles {DP} ;
 //             [OUT] [DVL] dK, dV += , dQ rows into the tiles {OUTFREE}
-enum { VF_KV = 0, VF_DVL, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_FINAL, VF_COUNT };
+enum { VF_KV = 0, VF_DVL, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_SFREE, VF_FINAL, VF_COUNT };
 enum { NF_INIT = 1, NF_PK, NF_DP, NF_OUTFREE };
 
 struct FixSmem {
@@ -932,10 +934,6 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
         ok = ok && !*abort;
         if (leader && ok) {
           store_out(c - 1);
-          // the tiles are read out before this chunk's dV rows come in and before the epilogue
-          // rewrites the d proj tiles (it waits for [DPK], committed after this)
-          tc::bulk_wait_read();
-          load_dvl(c);
           tc::tc_fence_after();
           issue_dfix();
         }
@@ -944,6 +942,13 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
         tc::tc_fence_after();
         issue_planes(T_DQ, P.dq, 0);
         tc::mma_commit(&bars[VF_TFREE]);  // every reader of the K, V, dprojQ tiles issued
+        if (c > 0) {
+          // the stores have read the tiles: this chunk's dV rows may come in and the epilogue
+          // may rewrite the d proj tiles
+          tc::bulk_wait_read();
+          load_dvl(c);
+          tc::mbar_arrive(&bars[VF_SFREE]);
+        }
       }
       tc::named_bar_sync(NF_PK, NTHR);
       ok = ok && !*abort;
@@ -1088,6 +1093,9 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
             bf16r2(dp[2], dp[3], lo[2], lo[3]);
 #pragma unroll
             for (int i = 0; i < 4; ++i) lo[i] = dp[i] - lo[i];
+            // the previous chunk's output stores have read the d proj tiles
+            if (tb == 0 && c > 0) ok = tc::warp_all(tc::mbar_wait(&bars[VF_SFREE], (c - 1) & 1, abort));
+            if (!ok) break;
             tc::st_row_half(sbase + P.dp, t, j >> 3, (j >> 2) & 1, dp);
             tc::st_row_half(sbase + P.dplo, t, j >> 3, (j >> 2) & 1, lo);
           }
