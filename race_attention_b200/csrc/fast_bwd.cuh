@@ -795,12 +795,13 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
 //   control: [KV] proj = K (planes_hi + planes_lo) -> [PROJ] ;
 //            {OUTFREE} store the previous chunk's dK, dV, dQ tiles ; Dfix = V gB_in^T -> [DPK] ;
 //            dQ = dprojQ planes -> [TFREE] ; once the stores have read the tiles: this chunk's
-//            dV tile -> [DVL], d proj tiles free -> [SFREE] ;
+//            dV tile -> [DVL] and the walk's fp32 d proj_K tile into the d proj tiles -> [DPL] ;
 //            {PK} dV = Pk gB_in ; {DP} dK = dproj planes -> [OUT]
-//   epilogue: [PROJ] Pk {PK} ; [DPK] dproj = softmax bwd of (Dfix + gA_in), [SFREE] into the
-//             d proj tiles {DP} ;
+//   epilogue: [PROJ] Pk {PK} ; [DPK] [DPL] dproj = softmax bwd of (Dfix + gA_in) + the walk's,
+//             as hi + lo bf16 into the d proj tiles once every thread read its fp32 values {DP} ;
 //             [OUT] [DVL] dK, dV += , dQ rows into the tiles {OUTFREE}
-enum { VF_KV = 0, VF_DVL, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_SFREE, VF_FINAL, VF_COUNT };
+enum { VF_KV = 0, VF_DVL, VF_PROJ, VF_DPK, VF_OUT, VF_TFREE, VF_DPL, VF_FINAL, VF_COUNT };
+enum { NF_ESYNC = 5 };  // epilogue-only barrier
 enum { NF_INIT = 1, NF_PK, NF_DP, NF_OUTFREE };
 
 struct FixSmem {
@@ -835,7 +836,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap tmVL,
                                                           const __grid_constant__ CUtensorMap tmOK,
                                                           const __grid_constant__ CUtensorMap tmOV,
-                                                          const __grid_constant__ CUtensorMap tmOQ, BwdArgs a) {
+                                                          const __grid_constant__ CUtensorMap tmOQ,
+                                                          const __grid_constant__ CUtensorMap tmPK, BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   const FixSmem P = fix_smem_plan(a.LP, a.S);
@@ -882,6 +884,14 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       tc::mbar_arrive_expect_tx(&bars[VF_DVL], TILE);
       tc::tma_load_4d(sm + P.dvl, &tmVL, &bars[VF_DVL], 0, hn, (c_begin + c) * C, bn);
     };
+    // the walk's fp32 d proj_K rows of chunk c into the (free) d proj tiles: columns [0, 32)
+    // in the hi tile, [32, 64) in the lo tile
+    auto load_dpl = [=, &tmPK](int c) {
+      const int t0 = (c_begin + c) * C;
+      tc::mbar_arrive_expect_tx(&bars[VF_DPL], 2 * TILE);
+      tc::tma_load_3d(sm + P.dp, &tmPK, &bars[VF_DPL], 0, t0, n);
+      tc::tma_load_3d(sm + P.dplo, &tmPK, &bars[VF_DPL], 32, t0, n);
+    };
     auto store_out = [=, &tmOK, &tmOV, &tmOQ](int c) {
       const int t0 = (c_begin + c) * C;
       tc::tma_store_4d(&tmOK, sm + P.dp, 0, hn, t0, bn);
@@ -918,6 +928,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
     if (leader && nch > 0) {
       load(0);
       load_dvl(0);
+      load_dpl(0);
     }
     tc::named_bar_sync(NF_INIT, NTHR);  // planes, gB_in, gA_in in shared memory
     if (leader && nch > 0) {
@@ -943,11 +954,10 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
         issue_planes(T_DQ, P.dq, 0);
         tc::mma_commit(&bars[VF_TFREE]);  // every reader of the K, V, dprojQ tiles issued
         if (c > 0) {
-          // the stores have read the tiles: this chunk's dV rows may come in and the epilogue
-          // may rewrite the d proj tiles
+          // the stores have read the tiles: this chunk's dV rows and d proj_K tile may come in
           tc::bulk_wait_read();
           load_dvl(c);
-          tc::mbar_arrive(&bars[VF_SFREE]);
+          load_dpl(c);
         }
       }
       tc::named_bar_sync(NF_PK, NTHR);
@@ -1062,15 +1072,17 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       tc::tc_fence_before();
       tc::named_bar_arrive(NF_PK, NTHR);
       // ---- dproj_fix = softmax bwd of (V gB_in^T + gA_in) + the walk's segment-local d proj_K
-      const bool live = t < nt;
-      const size_t row = ((size_t)n * a.T + tok0 + (live ? t : 0)) * HD;
-      float4 loc[4];  // issued before the wait: the loads are in flight meanwhile
-#pragma unroll
-      for (int tb = 0; tb < 4; ++tb)
-        loc[tb] = tb < tq && live ? *reinterpret_cast<const float4 *>(a.dprojK + row + 4 * (tq * hq + tb))
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_DPK], c & 1, abort));
+      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_DPL], c & 1, abort));
       tc::tc_fence_after();
+      float4 loc[4];  // the walk's d proj_K of this slot's tables (fp32 tile: 32-column halves)
+#pragma unroll
+      for (int tb = 0; tb < 4; ++tb) {
+        const int col = 4 * (tq * hq + tb);
+        loc[tb] = ok && tb < tq ? tc::ld_shared_f4(sbase + ((col >> 5) ? P.dplo : P.dp) + tc::sw128_off(t, (col & 31) >> 2))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      tc::named_bar_sync(NF_ESYNC, NEPI_T);  // every fp32 value read before the tiles are rewritten
       if (ok) {
 #pragma unroll
         for (int tb = 0; tb < 4; ++tb) {
@@ -1093,9 +1105,6 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
             bf16r2(dp[2], dp[3], lo[2], lo[3]);
 #pragma unroll
             for (int i = 0; i < 4; ++i) lo[i] = dp[i] - lo[i];
-            // the previous chunk's output stores have read the d proj tiles
-            if (tb == 0 && c > 0) ok = tc::warp_all(tc::mbar_wait(&bars[VF_SFREE], (c - 1) & 1, abort));
-            if (!ok) break;
             tc::st_row_half(sbase + P.dp, t, j >> 3, (j >> 2) & 1, dp);
             tc::st_row_half(sbase + P.dplo, t, j >> 3, (j >> 2) & 1, lo);
           }
