@@ -48,7 +48,9 @@ struct BwdArgs {
   __nv_bfloat16 *chunkB;    // [N, nchunks, S, 64]    bf16 B at chunk start
   __nv_bfloat16 *dQ, *dK, *dV;  // [N, T, 64]
   __nv_bfloat16 *dprojQ;        // [N, T, 64] d proj_Q (columns >= LP unused), reverse walk -> fix-up
-  float *dprojK;                // [N, T, 64] segment-local d proj_K (fp32), reverse walk -> fix-up
+  float *dprojK;                // segment-local d proj_K (fp32), reverse walk -> fix-up, table-major per
+                                //   chunk: [N, nchunks, LP/4 tables, 128 tokens, 4] (one 16-byte row
+                                //   per token and table: a warp's rows are one contiguous 512 bytes)
   const float *seedA, *seedB;   // fix-up: suffix of later shards added to every segment's ([N,S], [N,S,64])
   const __nv_bfloat16 *dVloc;   // fix-up: the walk's dV when it is not in dV itself (split backward)
   int *err;
@@ -691,9 +693,11 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
             for (int i = 0; i < 16; ++i) dpk[i] += inv[16 * tb + i];  // + the fp32 diagonal term
             corner_probs(qK + 4 * tb, pk);
             table_probs_bwd(pk, dpk, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
-            if (t < nt)  // segment-local d proj_K of table 4g + TPW hq + tb, fp32, to the fix-up
-              *reinterpret_cast<float4 *>(a.dprojK + ((size_t)n * a.T + tok0 + t) * HD + 16 * g +
-                                          4 * (TPW * hq + tb)) = make_float4(dp[0], dp[1], dp[2], dp[3]);
+            // segment-local d proj_K of table 4g + TPW hq + tb, fp32, to the fix-up (rows past
+            // the end too: the chunk's block is read whole)
+            *reinterpret_cast<float4 *>(a.dprojK +
+                                        (((size_t)n * a.nchunks + cg) * (a.LP / 4) + 4 * g + TPW * hq + tb) * (C * 4) +
+                                        4 * t) = make_float4(dp[0], dp[1], dp[2], dp[3]);
           }
         }
       }
@@ -836,8 +840,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
                                                           const __grid_constant__ CUtensorMap tmVL,
                                                           const __grid_constant__ CUtensorMap tmOK,
                                                           const __grid_constant__ CUtensorMap tmOV,
-                                                          const __grid_constant__ CUtensorMap tmOQ,
-                                                          const __grid_constant__ CUtensorMap tmPK, BwdArgs a) {
+                                                          const __grid_constant__ CUtensorMap tmOQ, BwdArgs a) {
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   const FixSmem P = fix_smem_plan(a.LP, a.S);
@@ -884,13 +887,12 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       tc::mbar_arrive_expect_tx(&bars[VF_DVL], TILE);
       tc::tma_load_4d(sm + P.dvl, &tmVL, &bars[VF_DVL], 0, hn, (c_begin + c) * C, bn);
     };
-    // the walk's fp32 d proj_K rows of chunk c into the (free) d proj tiles: columns [0, 32)
-    // in the hi tile, [32, 64) in the lo tile
-    auto load_dpl = [=, &tmPK](int c) {
-      const int t0 = (c_begin + c) * C;
-      tc::mbar_arrive_expect_tx(&bars[VF_DPL], 2 * TILE);
-      tc::tma_load_3d(sm + P.dp, &tmPK, &bars[VF_DPL], 0, t0, n);
-      tc::tma_load_3d(sm + P.dplo, &tmPK, &bars[VF_DPL], 32, t0, n);
+    // the walk's fp32 d proj_K block of chunk c (LP/4 tables x 128 tokens x 16 bytes, contiguous)
+    // into the (free, adjacent) d proj tiles
+    auto load_dpl = [=](int c) {
+      const uint32_t bytes = (uint32_t)LP * C * 4;
+      tc::mbar_arrive_expect_tx(&bars[VF_DPL], bytes);
+      tc::bulk_load(sm + P.dp, a.dprojK + ((size_t)n * a.nchunks + c_begin + c) * LP * C, bytes, &bars[VF_DPL]);
     };
     auto store_out = [=, &tmOK, &tmOV, &tmOQ](int c) {
       const int t0 = (c_begin + c) * C;
@@ -1075,13 +1077,11 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_DPK], c & 1, abort));
       if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[VF_DPL], c & 1, abort));
       tc::tc_fence_after();
-      float4 loc[4];  // the walk's d proj_K of this slot's tables (fp32 tile: 32-column halves)
+      float4 loc[4];  // the walk's d proj_K of this slot's tables (table-major block, 16 B per row)
 #pragma unroll
-      for (int tb = 0; tb < 4; ++tb) {
-        const int col = 4 * (tq * hq + tb);
-        loc[tb] = ok && tb < tq ? tc::ld_shared_f4(sbase + ((col >> 5) ? P.dplo : P.dp) + tc::sw128_off(t, (col & 31) >> 2))
+      for (int tb = 0; tb < 4; ++tb)
+        loc[tb] = ok && tb < tq ? tc::ld_shared_f4(sbase + P.dp + (uint32_t)((tq * hq + tb) * C + t) * 16)
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
       tc::named_bar_sync(NF_ESYNC, NEPI_T);  // every fp32 value read before the tiles are rewritten
       if (ok) {
 #pragma unroll

@@ -130,25 +130,6 @@ inline bool make_act_map(CUtensorMap *m, const void *base, int64_t N, int64_t T,
   return r == CUDA_SUCCESS;
 }
 
-// [N, T, 64] fp32 workspace rows as a 3-D map (64, T, N), box (32, 128, 1): a 128-token
-// tile in two 128-byte-wide halves (x = 0, 32), 128-byte swizzle.
-inline bool make_f32_map(CUtensorMap *m, const void *base, int64_t N, int64_t T) {
-  EncodeTiledFn enc = encoder();
-  if (!enc) {
-    last_encode_status() = -1;
-    return false;
-  }
-  cuuint64_t dims[3] = {(cuuint64_t)fk::HD, (cuuint64_t)T, (cuuint64_t)N};
-  cuuint64_t strides[2] = {(cuuint64_t)fk::HD * 4, (cuuint64_t)T * fk::HD * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)fk::C, 1};
-  cuuint32_t es[3] = {1, 1, 1};
-  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void *>(base), dims, strides, box, es,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  last_encode_status() = (int)r;
-  return r == CUDA_SUCCESS;
-}
-
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Backward workspace: status | forward segment records | backward segment
@@ -172,7 +153,8 @@ inline BwdPlan bwd_plan(int64_t N, int64_t T, int64_t S, int sms, bool split = f
   b.chunkB = b.chunkA + align_up(sizeof(float) * (size_t)N * b.p.nchunks * S, 256);
   b.dprojQ = b.chunkB + align_up(sizeof(uint16_t) * (size_t)N * b.p.nchunks * S * fk::HD, 256);
   b.dprojK = b.dprojQ + align_up(sizeof(uint16_t) * (size_t)N * T * fk::HD, 256);
-  b.dVloc = b.dprojK + align_up(sizeof(float) * (size_t)N * T * fk::HD, 256);
+  // d proj_K table-major per chunk: [N, nchunks, LP/4 tables, 128 tokens, 4] fp32
+  b.dVloc = b.dprojK + align_up(sizeof(float) * (size_t)N * b.p.nchunks * fk::C * (S / 4), 256);
   b.total = b.dVloc + (split ? align_up(sizeof(uint16_t) * (size_t)N * T * fk::HD, 256) : 0);
   return b;
 }

@@ -594,16 +594,15 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
     b.dVloc = at<__nv_bfloat16>(ws, bp.dVloc);
   }
   // tile maps of the walk's dV (read) and of the outputs (written by TMA tile stores)
-  CUtensorMap mVL, mOK, mOV, mOQ, mPK;
+  CUtensorMap mVL, mOK, mOV, mOQ;
   if (!fh::make_act_map(&mVL, b.dVloc ? (void *)b.dVloc : dV, N, T, H) || !fh::make_act_map(&mOK, dK, N, T, H) ||
-      !fh::make_act_map(&mOV, dV, N, T, H) || !fh::make_act_map(&mOQ, dQ, N, T, H) ||
-      !fh::make_f32_map(&mPK, b.dprojK, N, T))
+      !fh::make_act_map(&mOV, dV, N, T, H) || !fh::make_act_map(&mOQ, dQ, N, T, H))
     return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the fix-up's dV/dK/dQ: CUresult %d",
                 fh::last_encode_status());
   const fk::FixSmem xs = fk::fix_smem_plan(b.LP, b.S);
   RACE_TRY(set_smem(fk::bwd_fix_kernel, xs.total));
   KernelScope ks(RACE_KT_BWD_FIX, s);
-  fk::bwd_fix_kernel<<<grid, fk::NTHR, xs.total, s>>>(mK, mV, mP, mVL, mOK, mOV, mOQ, mPK, b);
+  fk::bwd_fix_kernel<<<grid, fk::NTHR, xs.total, s>>>(mK, mV, mP, mVL, mOK, mOV, mOQ, b);
   ks.stop();
   return check_launch("fast bwd_fix");
 }
