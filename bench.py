@@ -268,19 +268,64 @@ def run_gpt(args):
     return 0
 
 
+def run_noncausal(args):
+    """Non-causal RACE (the reference's BatchedACE, shared planes): forward + backward of one
+    layer through race_noncausal at B=8, H=12, T=4096 (--tokens overrides T), head_dim 64,
+    L=8 x P=4, bf16, inputs N(0,1)/8.  Not the headline line."""
+    import race_attention_b200 as rb
+    from race_attention_b200 import _lib
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, H, T, D, L, P = 8, 12, args.tokens or 4096, 64, 8, 4
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device=dev, seed=0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, k, v, do = (torch.randn(B, H, T, D, device=dev, generator=g).div_(8).bfloat16() for _ in range(4))
+    leaves = [x.requires_grad_(True) for x in (q, k, v)]
+
+    def step():
+        for x in leaves:
+            x.grad = None
+        rb.race_noncausal(*leaves, planes, L, P).backward(do)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    lib = _lib.load()
+    n0 = lib.race_launch_counter()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    line = {"metric": "non-causal RACE layer fwd+bwd tokens/s", "value": B * T / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn / 8)",
+            "config": {"workload": "non-causal RACE (BatchedACE, shared planes) fwd+bwd", "batch": B, "heads": H,
+                       "seq_len": T, "head_dim": D, "tables_L": L, "planes_P": P},
+            "gpu_launches": (lib.race_launch_counter() - n0) // args.steps, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg5"], default="cfg2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg5", "noncausal"], default="cfg2")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (not a headline number)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     if args.config == "cfg5":
         return run_gpt(args)
+    if args.config == "noncausal":
+        return run_noncausal(args)
     cfg = list(CONFIGS[args.config])
     if args.config == "cfg3":
         cfg[2] = cfg[2] // max(1, args.gpus)

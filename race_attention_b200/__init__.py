@@ -10,9 +10,10 @@ from .ext import load_ext  # noqa: F401
 from .race_causal_cuda import (RaceBTHDFn, RaceCausalCuda, RaceCausalFn, RaceQKVFn, fwd_chunk,  # noqa: F401
                                nanochat_race_attention, race_causal, race_causal_bthd, race_cuda_fused)
 from .race_common import build_planes_protos, soft_hash_probs  # noqa: F401
+from .noncausal import BatchedACE, RaceNonCausalFn, race_noncausal  # noqa: F401
 from .sharded import race_causal_sharded  # noqa: F401
 
 __all__ = [
     "build_planes_protos", "soft_hash_probs", "fwd_chunk", "RaceCausalFn", "race_cuda_fused", "RaceCausalCuda",
-    "RaceQKVFn", "race_causal", "RaceBTHDFn", "race_causal_bthd", "nanochat_race_attention", "RaceDecodeState", "prefill_with_state", "race_causal_sharded", "load_ext", "ops",
+    "RaceQKVFn", "race_causal", "race_noncausal", "RaceNonCausalFn", "BatchedACE", "RaceBTHDFn", "race_causal_bthd", "nanochat_race_attention", "RaceDecodeState", "prefill_with_state", "race_causal_sharded", "load_ext", "ops",
 ]

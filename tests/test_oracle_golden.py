@@ -96,3 +96,26 @@ def test_oracle_soft_hash_grad_matches_autograd():
     dX = O.soft_hash_bwd(X.detach(), planes, L, P, gp, 0.25)
     assert relerr(dX, X.grad) < 1e-12
     assert relerr(O.soft_hash(X.detach(), planes, L, P, 0.25), probs.detach()) < 1e-13
+
+
+def _ace_streams(x):
+    """[1, B, T, H, d] (BatchedACE layout) -> [B*H, T, d] streams."""
+    x = np.asarray(x)[0]
+    B, T, H, d = x.shape
+    return np.ascontiguousarray(x.transpose(0, 2, 1, 3).reshape(B * H, T, d))
+
+
+def test_oracle_noncausal_matches_reference_module():
+    """ace_fwd / ace_bwd against the reference's own BatchedACE (shared planes, float64,
+    tests/golden/make_golden_ace.py): output and all three input gradients."""
+    import os
+    G = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_ace.npz"))
+    for i, (B, T, H, dk, K, L, seed) in enumerate(G["cases"]):
+        planes = G[f"c{i}_planes_T"]
+        Q, Kx, V, dO = (_ace_streams(G[f"c{i}_{n}"]) for n in ("Q", "K", "V", "dO"))
+        out, _, _ = O.ace_fwd(Q, Kx, V, planes, int(L), int(K), 1e-6, 1.0)
+        assert O.relerr(out, _ace_streams(G[f"c{i}_out"])) < 1e-10
+        dQ, dK, dV = O.ace_bwd(Q, Kx, V, dO, planes, int(L), int(K), 1e-6, 1.0)
+        assert O.relerr(dQ, _ace_streams(G[f"c{i}_dQ"])) < 1e-9
+        assert O.relerr(dK, _ace_streams(G[f"c{i}_dK"])) < 1e-9
+        assert O.relerr(dV, _ace_streams(G[f"c{i}_dV"])) < 1e-10
