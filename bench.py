@@ -311,13 +311,60 @@ def run_noncausal(args):
     return 0
 
 
+def run_hybrid(args):
+    """Config 4: hybrid decode, Llama-3.2-1B architecture with random-init bf16 weights (std
+    0.02), odd layers RACE (L=8 x P=4) through the fused decode step, even layers softmax GQA
+    (SDPA over a KV cache): batch 64, a 32,768-token prefill of uniform token ids (--tokens
+    overrides), then --steps greedy decode steps (default 512 when --steps is left at 10).
+    Not the headline line."""
+    from race_attention_b200 import _lib
+    from race_attention_b200.hybrid import HybridConfig, HybridLlama
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = HybridConfig()
+    B, T = 64, args.tokens or 32768
+    n_dec = 512 if args.steps == 10 else args.steps
+    torch.manual_seed(0)
+    model = HybridLlama(cfg).to(dev)
+    model.init_weights(0.02)
+    model = model.to(torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(1)
+    idx = torch.randint(0, cfg.vocab_size, (B, T), device=dev, generator=g)
+    lib = _lib.load()
+    s0, s1, s2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    with ClockSampler(local) as clk:
+        s0.record()
+        tok = model.prefill(idx, t_max=T + n_dec)
+        s1.record()
+        n0 = lib.race_launch_counter()
+        for _ in range(n_dec):
+            tok = model.step(tok)
+        s2.record()
+        torch.cuda.synchronize()
+    prefill_ms, decode_ms = s0.elapsed_time(s1), s1.elapsed_time(s2)
+    line = {"metric": "hybrid decode tokens/s (cfg4)", "value": B * n_dec / (decode_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": n_dec, "warmup": 0, "ms_per_step": decode_ms / n_dec, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (token ids uniform over the vocabulary, seeded; random-init weights)",
+            "config": {"workload": "cfg4: Llama-3.2-1B architecture, odd layers RACE, prefill then greedy decode",
+                       "batch": B, "prefill_tokens": T, "decode_steps": n_dec, "n_layer": cfg.n_layer,
+                       "hidden": cfg.hidden, "heads": cfg.n_head, "kv_heads": cfg.n_kv_head, "tables_L": cfg.race_L,
+                       "planes_P": cfg.race_P},
+            "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * T / (prefill_ms / 1e3),
+            "race_decode_launches_per_step": (lib.race_launch_counter() - n0) // max(1, n_dec),
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg5", "noncausal"], default="cfg2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg4", "cfg5", "noncausal"], default="cfg2")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (not a headline number)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -326,6 +373,8 @@ def main():
         return run_gpt(args)
     if args.config == "noncausal":
         return run_noncausal(args)
+    if args.config == "cfg4":
+        return run_hybrid(args)
     cfg = list(CONFIGS[args.config])
     if args.config == "cfg3":
         cfg[2] = cfg[2] // max(1, args.gpus)

@@ -87,3 +87,29 @@ def test_sequence_shard_phases_emulated(world, dtype, tol):
     assert relerr(cat([x[0] for x in grads]), dQ_r) < tol
     assert relerr(cat([x[1] for x in grads]), dK_r) < tol
     assert relerr(cat([x[2] for x in grads]), dV_r) < tol
+
+
+def test_hybrid_decode_matches_prefill():
+    """The config-4 harness at toy size (fp32): after a prefill of T tokens, k greedy decode
+    steps (fused RACE decode step in the odd layers, SDPA over the KV cache in the even
+    ones) give the same next-token logits as a plain causal forward over the T + k tokens."""
+    from race_attention_b200.hybrid import HybridConfig, HybridLlama
+    torch.manual_seed(0)
+    cfg = HybridConfig(vocab_size=1000, n_layer=4, hidden=256, n_head=4, n_kv_head=2, mlp_hidden=512)
+    model = HybridLlama(cfg).cuda()
+    model.init_weights(0.05)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    idx = torch.randint(0, cfg.vocab_size, (3, 150), device="cuda", generator=g)
+    tok = model.prefill(idx, t_max=160, micro_batch=2)
+    seq = torch.cat([idx, tok[:, None]], 1)
+    for _ in range(4):
+        x = model.embed(tok[:, None])
+        pos = model.layers[0].length
+        cos, sin = model._angles(pos, 1, tok.device, x.dtype)
+        for layer in model.layers:
+            x = layer.step(x, cos, sin)
+        logits_step = model._logits(x[:, -1])
+        full = model.logits_full(seq)
+        assert relerr(logits_step, full) < 1e-3
+        tok = logits_step.argmax(-1)
+        seq = torch.cat([seq, tok[:, None]], 1)
