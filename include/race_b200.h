@@ -198,6 +198,27 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype,
                      int64_t Nq, int64_t Nkv, int64_t D, int64_t L, int64_t P,
                      float eps, float logit_scale, void *stream);
 
+/* Softmax grouped-query attention for one decode token over a bf16 KV cache,
+ * for the softmax layers of a hybrid decoder whose other layers are RACE
+ * (no reference counterpart; the hybrid decode configuration's softmax half).
+ * q[B,Hq,64], k_new/v_new[B,Hkv,64], k_cache/v_cache[B,Hkv,Tmax,64], all bf16
+ * and contiguous; *len (int32, device memory) = tokens already cached.  The
+ * call stores (k_new, v_new) at cache position *len, then writes
+ *   out[b,i] = softmax_j(softmax_scale * q[b,i].K[b,i/G,j]) V[b,i/G,j], j <= *len,
+ * G = Hq/Hkv <= 8.  It does not advance *len (the caller does, once
+ * per step for all layers), so one launch can be captured in a CUDA graph and
+ * replayed every step.  workspace: race_gqa_decode_workspace_bytes(B, Hq, Hkv,
+ * n_splits) bytes, zero-filled before its first use and reused as is (the
+ * kernel leaves it ready for the next call); one workspace per concurrently
+ * running call.  n_splits in [1,64] = key ranges per (b, kv head) processed in
+ * parallel.  *len outside [0, Tmax) stores nothing, leaves out unwritten and
+ * sets the workspace's last int32 to 1. */
+size_t race_gqa_decode_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int n_splits);
+int race_gqa_decode_attn(const void *q, const void *k_new, const void *v_new,
+                         void *k_cache, void *v_cache, const int32_t *len, void *out,
+                         void *workspace, int64_t B, int64_t Hq, int64_t Hkv, int64_t Tmax,
+                         int64_t D, int n_splits, float softmax_scale, void *stream);
+
 /* ---- sequence-sharded phases (one rank's contiguous slice of T) ---------- */
 
 /* The fused layer on activations laid out [B, T, H, D] (the layout attention modules

@@ -46,6 +46,8 @@ SIGNATURES = {
                      _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
     "race_state_from_prefill": [_P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
     "race_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P],
+    "race_gqa_decode_workspace_bytes": [_I64, _I64, _I64, _I],
+    "race_gqa_decode_attn": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _F, _P],
     "race_fwd_bthd": [_P, _P, _P, _I, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
     "race_bwd_bthd": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _P,
                       _SZ, _P],
@@ -64,7 +66,7 @@ SIGNATURES = {
                            _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
 }
 _RESTYPES = {"race_status_string": ctypes.c_char_p, "race_last_error": ctypes.c_char_p,
-             "race_launch_counter": ctypes.c_ulonglong}
+             "race_launch_counter": ctypes.c_ulonglong, "race_gqa_decode_workspace_bytes": ctypes.c_size_t}
 
 
 def library_path() -> str:

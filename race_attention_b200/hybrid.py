@@ -5,10 +5,13 @@ The reference has no decode path for RACE (chat/nanochat/gpt.py:143-146 raises);
 harness is where the library's fused decode step (race_decode_step through RaceDecodeState)
 meets a real model loop: a batched prefill that leaves each RACE layer's (A, B) state and
 each softmax layer's KV cache, then greedy decode steps, each one fused RACE state update +
-readout per RACE layer (grouped-query: 32 query heads read 8 kv states) and one SDPA call
-over the cache per softmax layer.  Architecture: 16 layers, hidden 2048, 32 / 8 heads,
-head_dim 64, SwiGLU MLP 8192, RMSNorm (eps 1e-5), RoPE theta 500000, vocabulary 128256 with
-the LM head tied to the embedding.
+readout per RACE layer (grouped-query: 32 query heads read 8 kv states) and one
+race_gqa_decode_attn launch per softmax layer (appends the token's key/value to the cache
+and attends over it; the cache length lives in device memory).  Because no launch of a
+decode step depends on host-side position values, DecodeGraph captures one whole step as a
+CUDA graph and replays it.  Architecture: 16 layers, hidden 2048, 32 / 8 heads, head_dim 64,
+SwiGLU MLP 8192, RMSNorm (eps 1e-5), RoPE theta 500000, vocabulary 128256 with the LM head
+tied to the embedding.  Decoding runs in bf16 (the softmax layers' kernel is bf16-only).
 """
 from __future__ import annotations
 
@@ -18,6 +21,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import ops
 from .decode import RaceDecodeState, prefill_with_state
 from .race_common import build_planes_protos
 
@@ -74,7 +78,8 @@ class Layer(nn.Module):
             self.register_buffer("planes_T", planes_T)
         self.state = None      # RACE layers: RaceDecodeState
         self.cache = None      # softmax layers: (K, V) [B, Hkv, Tmax, D]
-        self.length = 0
+        self.attn_ws = None    # softmax layers: race_gqa_decode_attn workspace and its split count
+        self.n_splits = 1
 
     def _qkv(self, x, cos, sin):
         B, T, _ = x.shape
@@ -104,29 +109,25 @@ class Layer(nn.Module):
             if b0 == 0:
                 self.cache = tuple(torch.empty(batch, cfg.n_kv_head, t_max, self.hd, dtype=k.dtype, device=k.device)
                                    for _ in range(2))
+                self.n_splits = ops.gqa_decode_splits(batch, cfg.n_kv_head, t_max, k.device)
+                self.attn_ws = ops.gqa_decode_workspace(batch, cfg.n_head, cfg.n_kv_head, self.n_splits, k.device)
             self.cache[0][b0:b0 + mb, :, :T].copy_(k)
             self.cache[1][b0:b0 + mb, :, :T].copy_(v)
             y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
-        self.length = T
         x = x + self.o(y.transpose(1, 2).reshape(mb, T, -1))
         h = self.ln2(x)
         return x + self.down(F.silu(self.gate(h)) * self.up(h))
 
-    def step(self, x, cos, sin):
-        """x [B, 1, hidden] at position self.length."""
+    def step(self, x, cos, sin, pos):
+        """x [B, 1, hidden] at position pos (int32 device tensor [1] = tokens already seen)."""
         B = x.shape[0]
         q, k, v = self._qkv(self.ln1(x), cos, sin)  # [B, H, 1, D]
+        q, k, v = q[:, :, 0].contiguous(), k[:, :, 0].contiguous(), v[:, :, 0].contiguous()
         if self.race:
-            y = self.state.step(q[:, :, 0].contiguous(), k[:, :, 0].contiguous(), v[:, :, 0].contiguous())
-            y = y.unsqueeze(2)
+            y = self.state.step(q, k, v)
         else:
-            t = self.length
-            self.cache[0][:, :, t:t + 1].copy_(k)
-            self.cache[1][:, :, t:t + 1].copy_(v)
-            y = F.scaled_dot_product_attention(q, self.cache[0][:, :, :t + 1], self.cache[1][:, :, :t + 1],
-                                               enable_gqa=True)
-        self.length += 1
-        x = x + self.o(y.transpose(1, 2).reshape(B, 1, -1))
+            y = ops.gqa_decode_attention(q, k, v, self.cache[0], self.cache[1], pos, self.attn_ws, self.n_splits)
+        x = x + self.o(y.reshape(B, 1, -1))
         h = self.ln2(x)
         return x + self.down(F.silu(self.gate(h)) * self.up(h))
 
@@ -138,16 +139,21 @@ class HybridLlama(nn.Module):
         self.embed = nn.Embedding(cfg.vocab_size, cfg.hidden)
         self.layers = nn.ModuleList(Layer(cfg, i) for i in range(cfg.n_layer))
         self.norm = _RMSNorm(cfg.hidden, cfg.norm_eps)
+        self.pos = None        # int32 device tensor [1]: tokens in the decode state / caches
+        self.n_tokens = 0      # the same count on the host
+        self.t_max = 0
 
     def init_weights(self, std=0.02):
         for name, p in self.named_parameters():
             if p.dim() > 1:
                 nn.init.normal_(p, mean=0.0, std=std)
 
-    def _angles(self, pos0, T, device, dtype):
+    def _inv_freq(self, device):
         hd = self.cfg.hidden // self.cfg.n_head
-        inv = self.cfg.rope_theta ** (-torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd)
-        ang = torch.outer(torch.arange(pos0, pos0 + T, device=device, dtype=torch.float32), inv)
+        return self.cfg.rope_theta ** (-torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd)
+
+    def _angles(self, pos0, T, device, dtype):
+        ang = torch.outer(torch.arange(pos0, pos0 + T, device=device, dtype=torch.float32), self._inv_freq(device))
         return ang.cos().to(dtype), ang.sin().to(dtype)
 
     def _logits(self, x):
@@ -165,27 +171,79 @@ class HybridLlama(nn.Module):
             for layer in self.layers:
                 x = layer.prefill(x, cos, sin, t_max, b0, B)
             nxt.append(self._logits(x[:, -1]).argmax(-1))
+        self.pos = torch.full((1,), T, dtype=torch.int32, device=idx.device)
+        self.n_tokens, self.t_max = T, t_max
         return torch.cat(nxt)
 
     @torch.no_grad()
     def logits_full(self, idx):
         """Last-position logits of a plain causal forward over idx [B, T] (no caches kept)."""
         B, T = idx.shape
-        kept = [(layer.state, layer.cache, layer.length) for layer in self.layers]
+        kept = [(layer.state, layer.cache, layer.attn_ws, layer.n_splits) for layer in self.layers]
         cos, sin = self._angles(0, T, idx.device, self.embed.weight.dtype)
         x = self.embed(idx)
         for layer in self.layers:
             x = layer.prefill(x, cos, sin, T, 0, B)
-        for layer, (st, cache, length) in zip(self.layers, kept):  # the decode state stays as it was
-            layer.state, layer.cache, layer.length = st, cache, length
+        for layer, (st, cache, ws, ns) in zip(self.layers, kept):  # the decode state stays as it was
+            layer.state, layer.cache, layer.attn_ws, layer.n_splits = st, cache, ws, ns
         return self._logits(x[:, -1])
+
+    def _step_logits(self, tok):
+        """One decode step on the device: every position-dependent value comes from self.pos,
+        so the launches are the same at every step (capturable)."""
+        ang = self.pos.float()[:, None] * self._inv_freq(tok.device)[None]
+        dtype = self.embed.weight.dtype
+        cos, sin = ang.cos().to(dtype), ang.sin().to(dtype)
+        x = self.embed(tok[:, None])
+        for layer in self.layers:
+            x = layer.step(x, cos, sin, self.pos)
+        self.pos.add_(1)
+        return self._logits(x[:, -1])
+
+    def _advance(self, n):
+        self.n_tokens += n
+        for layer in self.layers:
+            if layer.race:
+                layer.state.tokens = self.n_tokens
+
+    @torch.no_grad()
+    def step_logits(self, tok):
+        """tok [B] -> next-token logits [B, vocab]; appends tok to the decode state."""
+        if self.pos is None or self.n_tokens >= self.t_max:
+            raise RuntimeError(f"decode state full ({self.n_tokens} of {self.t_max} positions) or not prefilled")
+        logits = self._step_logits(tok)
+        self._advance(1)
+        return logits
 
     @torch.no_grad()
     def step(self, tok):
         """tok [B] -> next-token ids [B] (greedy)."""
-        pos = self.layers[0].length
-        cos, sin = self._angles(pos, 1, tok.device, self.embed.weight.dtype)
-        x = self.embed(tok[:, None])
-        for layer in self.layers:
-            x = layer.step(x, cos, sin)
-        return self._logits(x[:, -1]).argmax(-1)
+        return self.step_logits(tok).argmax(-1)
+
+
+class DecodeGraph:
+    """One greedy decode step of a prefilled HybridLlama captured as a CUDA graph.
+
+    replay() feeds the token held in self.tok, advances the model by one position and leaves
+    the next token in self.tok.  Capture runs nothing on the device; call model.step at
+    least once before capturing (first-use initialisation of the libraries must happen
+    outside capture) and do not mix eager steps with replays afterwards unless self.tok is
+    refreshed."""
+
+    def __init__(self, model: HybridLlama, tok):
+        self.model = model
+        self.tok = tok.clone()
+        saved = model.n_tokens
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.tok.copy_(model._step_logits(self.tok).argmax(-1))
+        model.n_tokens = saved
+        model._advance(0)
+
+    def replay(self):
+        m = self.model
+        if m.n_tokens >= m.t_max:
+            raise RuntimeError(f"decode state full ({m.n_tokens} of {m.t_max} positions)")
+        self.graph.replay()
+        m._advance(1)
+        return self.tok

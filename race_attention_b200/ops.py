@@ -452,3 +452,48 @@ def decode_step(q, k, v, planes_T, A, B, L, P, eps=1e-6, logit_scale=None):
                                         _ptr(out), Nq, Nkv, D, L, P, float(eps), scale, _stream(dev)),
                    "race_decode_step")
     return out
+
+
+def gqa_decode_splits(B, Hkv, t_max, device) -> int:
+    """Key ranges per (batch row, kv head) for gqa_decode_attention: about 16 waves of
+    two CTAs per SM over the whole grid, at least 512 cache slots per range, at most 64."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    want = -(-16 * 2 * sms // max(1, B * Hkv))
+    return int(max(1, min(64, want, max(1, t_max // 512))))
+
+
+def gqa_decode_workspace(B, Hq, Hkv, n_splits, device):
+    """Zero-filled workspace for gqa_decode_attention (reused as is across calls)."""
+    nbytes = int(_lib.load().race_gqa_decode_workspace_bytes(B, Hq, Hkv, int(n_splits)))
+    if nbytes == 0:
+        raise RuntimeError("invalid gqa_decode_attention workspace shape")
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
+def gqa_decode_attention(q, k_new, v_new, k_cache, v_cache, length, workspace, n_splits, softmax_scale=None):
+    """Softmax GQA attention of one decode token over a bf16 KV cache (the softmax layers
+    of a hybrid decoder).  q [B,Hq,64], k_new/v_new [B,Hkv,64], caches [B,Hkv,Tmax,64],
+    length = int32 device tensor [1] holding the tokens already cached.  Stores k_new/v_new
+    at position length, returns out [B,Hq,64]; length itself is not advanced."""
+    dev = _check_cuda(q, k_new, v_new, k_cache, v_cache, length, workspace)
+    for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise RuntimeError(f"{name} must be contiguous bfloat16")
+    if length.dtype != torch.int32 or length.numel() != 1:
+        raise RuntimeError("length must be an int32 tensor with one element")
+    B, Hq, D = q.shape
+    Hkv, Tmax = k_cache.shape[1], k_cache.shape[2]
+    if k_new.shape != (B, Hkv, D) or v_new.shape != (B, Hkv, D) or k_cache.shape != (B, Hkv, Tmax, D) \
+            or v_cache.shape != k_cache.shape:
+        raise RuntimeError("gqa_decode_attention: inconsistent shapes")
+    lib = _lib.load()
+    need = int(lib.race_gqa_decode_workspace_bytes(B, Hq, Hkv, int(n_splits)))
+    if workspace.numel() * workspace.element_size() < need:
+        raise RuntimeError(f"gqa_decode_attention workspace needs {need} bytes")
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    out = torch.empty_like(q)
+    with torch.cuda.device(dev):
+        _lib.check(lib.race_gqa_decode_attn(_ptr(q), _ptr(k_new), _ptr(v_new), _ptr(k_cache), _ptr(v_cache),
+                                            _ptr(length), _ptr(out), _ptr(workspace), B, Hq, Hkv, Tmax, D,
+                                            int(n_splits), scale, _stream(dev)), "race_gqa_decode_attn")
+    return out

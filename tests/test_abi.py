@@ -118,3 +118,28 @@ def test_bthd_layout_needs_tcgen05_path():
     assert rc == codes["RACE_ERR_UNSUPPORTED"]
     assert lib.race_fwd_bthd(p, p, p, _lib.RACE_BF16, p, p, None, 0, 0, 128, 3, 64, 8, 4, 1e-6, 0.125, p, 1 << 20,
                              None) == codes["RACE_ERR_SHAPE"]
+
+
+def test_gqa_decode_validation():
+    """race_gqa_decode_attn rejects bad shapes before any CUDA call."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    codes = status_codes()
+    one = ctypes.c_void_p(256)
+    # head dim other than 64
+    assert lib.race_gqa_decode_attn(p, p, p, p, p, one, p, p, 2, 8, 2, 100, 128, 4, 0.1, None) == \
+        codes["RACE_ERR_UNSUPPORTED"]
+    # Hq not a multiple of Hkv
+    assert lib.race_gqa_decode_attn(p, p, p, p, p, one, p, p, 2, 6, 4, 100, 64, 4, 0.1, None) == codes["RACE_ERR_SHAPE"]
+    # query group 9 (> 8) has no kernel
+    assert lib.race_gqa_decode_attn(p, p, p, p, p, one, p, p, 2, 18, 2, 100, 64, 4, 0.1, None) == \
+        codes["RACE_ERR_UNSUPPORTED"]
+    # split count out of range, null pointer, misaligned cache
+    assert lib.race_gqa_decode_attn(p, p, p, p, p, one, p, p, 2, 8, 2, 100, 64, 65, 0.1, None) == codes["RACE_ERR_SHAPE"]
+    assert lib.race_gqa_decode_attn(p, p, p, None, p, one, p, p, 2, 8, 2, 100, 64, 4, 0.1, None) == codes["RACE_ERR_ARG"]
+    bad = ctypes.c_void_p(264)
+    assert lib.race_gqa_decode_attn(p, p, p, bad, p, one, p, p, 2, 8, 2, 100, 64, 4, 0.1, None) == \
+        codes["RACE_ERR_ALIGN"]
+    # workspace: fp32 partials (64 dims + max + sum) per query head and split, a ticket per kv stream, a status word
+    assert lib.race_gqa_decode_workspace_bytes(2, 8, 2, 4) == 4 * 2 * 8 * 4 * 66 + 4 * 4 + 4
+    assert lib.race_gqa_decode_workspace_bytes(0, 8, 2, 4) == 0
