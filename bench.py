@@ -242,7 +242,7 @@ def run_gpt(args):
         e.record()
         torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
-    launches = (lib.race_launch_counter() - n0) // args.steps
+    launches = lib.race_launch_counter() - n0  # library kernels launched in the timed region
     kernels = kernel_times(lib, args.steps)
     lib.race_kernel_timing(0)
     race_ms = sum(v["ms_per_step"] for v in kernels.values())
@@ -260,7 +260,8 @@ def run_gpt(args):
                            "n_embd": cfg.n_embd, "n_head": cfg.n_head, "vocab": cfg.vocab_size,
                            "tables_L": cfg.race_L, "planes_P": cfg.race_P,
                            "parallelism": f"dp{world}" if world > 1 else "single"},
-                "loss_first": float(losses[0]), "loss_last": float(losses[-1]), "gpu_launches": launches,
+                "loss_first": float(losses[0]), "loss_last": float(losses[-1]), "gpu_launches": int(launches),
+                "gpu_launches_per_step": int(launches) // args.steps,
                 "race_kernels_ms_per_step": race_ms, "kernels": kernels,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
@@ -307,7 +308,8 @@ def run_noncausal(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn / 8)",
             "config": {"workload": "non-causal RACE (BatchedACE, shared planes) fwd+bwd", "batch": B, "heads": H,
                        "seq_len": T, "head_dim": D, "tables_L": L, "planes_P": P},
-            "gpu_launches": (lib.race_launch_counter() - n0) // args.steps, "clocks": clk.summary()}
+            "gpu_launches": int(lib.race_launch_counter() - n0),
+            "gpu_launches_per_step": int(lib.race_launch_counter() - n0) // args.steps, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -464,7 +466,7 @@ def run_ours(args, cfg):
         end.record()
         torch.cuda.synchronize()
     barrier()
-    launches = (lib.race_launch_counter() - n0) // args.steps
+    launches = lib.race_launch_counter() - n0  # library kernels launched in the timed region
     kernels = kernel_times(lib, args.steps)
     lib.race_kernel_timing(0)
     ms = start.elapsed_time(end) / args.steps
@@ -498,7 +500,7 @@ def run_ours(args, cfg):
                 "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
                 "data": "synthetic (seeded randn, BASELINE shapes)", "config": config_dict(args, cfg),
                 "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": int(launches),
+                "gpu_launches": int(launches), "gpu_launches_per_step": int(launches) // args.steps,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -66,12 +66,11 @@ class Layer(nn.Module):
         self.hd = hd
         self.ln1 = _RMSNorm(cfg.hidden, cfg.norm_eps)
         self.ln2 = _RMSNorm(cfg.hidden, cfg.norm_eps)
-        self.q = nn.Linear(cfg.hidden, cfg.n_head * hd, bias=False)
-        self.k = nn.Linear(cfg.hidden, cfg.n_kv_head * hd, bias=False)
-        self.v = nn.Linear(cfg.hidden, cfg.n_kv_head * hd, bias=False)
+        # q, k, v projections as one [(Hq + 2 Hkv) * hd, hidden] weight and gate/up as one
+        # [2 * mlp, hidden] weight: one GEMM each (the split is a view of the output)
+        self.qkv = nn.Linear(cfg.hidden, (cfg.n_head + 2 * cfg.n_kv_head) * hd, bias=False)
         self.o = nn.Linear(cfg.n_head * hd, cfg.hidden, bias=False)
-        self.gate = nn.Linear(cfg.hidden, cfg.mlp_hidden, bias=False)
-        self.up = nn.Linear(cfg.hidden, cfg.mlp_hidden, bias=False)
+        self.gate_up = nn.Linear(cfg.hidden, 2 * cfg.mlp_hidden, bias=False)
         self.down = nn.Linear(cfg.mlp_hidden, cfg.hidden, bias=False)
         if self.race:
             planes_T, _ = build_planes_protos(hd, cfg.race_P, cfg.race_L, 1, device="cpu", seed=idx)
@@ -84,10 +83,14 @@ class Layer(nn.Module):
     def _qkv(self, x, cos, sin):
         B, T, _ = x.shape
         cfg, hd = self.cfg, self.hd
-        q = self.q(x).view(B, T, cfg.n_head, hd).transpose(1, 2)
-        k = self.k(x).view(B, T, cfg.n_kv_head, hd).transpose(1, 2)
-        v = self.v(x).view(B, T, cfg.n_kv_head, hd).transpose(1, 2)
+        q, k, v = self.qkv(x).view(B, T, cfg.n_head + 2 * cfg.n_kv_head, hd).split(
+            [cfg.n_head, cfg.n_kv_head, cfg.n_kv_head], dim=2)
+        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         return _rope(q, cos, sin), _rope(k, cos, sin), v
+
+    def _mlp(self, x):
+        g, u = self.gate_up(x).chunk(2, dim=-1)
+        return self.down(F.silu(g) * u)
 
     def prefill(self, x, cos, sin, t_max, b0, batch):
         """x [mb, T, hidden]: sequences [b0, b0 + mb) of a batch of `batch`, from position 0;
@@ -115,8 +118,7 @@ class Layer(nn.Module):
             self.cache[1][b0:b0 + mb, :, :T].copy_(v)
             y = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         x = x + self.o(y.transpose(1, 2).reshape(mb, T, -1))
-        h = self.ln2(x)
-        return x + self.down(F.silu(self.gate(h)) * self.up(h))
+        return x + self._mlp(self.ln2(x))
 
     def step(self, x, cos, sin, pos):
         """x [B, 1, hidden] at position pos (int32 device tensor [1] = tokens already seen)."""
@@ -128,8 +130,7 @@ class Layer(nn.Module):
         else:
             y = ops.gqa_decode_attention(q, k, v, self.cache[0], self.cache[1], pos, self.attn_ws, self.n_splits)
         x = x + self.o(y.reshape(B, 1, -1))
-        h = self.ln2(x)
-        return x + self.down(F.silu(self.gate(h)) * self.up(h))
+        return x + self._mlp(self.ln2(x))
 
 
 class HybridLlama(nn.Module):
