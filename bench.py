@@ -314,6 +314,53 @@ def run_noncausal(args):
     return 0
 
 
+def decode_kernel_times(model, cfg, B, dev, reps=50):
+    """The two attention kernels of a decode step timed alone, as a CUDA graph of `reps`
+    launches, after the decode run (they overwrite one RACE layer's state and the last cache
+    slot of one softmax layer), with their HBM bytes per launch: the RACE decode step reads
+    and writes its whole state (A [B*Hkv, S], B [B*Hkv, S, D] fp32), the softmax kernel reads
+    the cached K and V rows."""
+    from race_attention_b200 import ops
+    hbm, _, src = _peaks()
+    race_layer = next(l for l in model.layers if l.race)
+    soft_layer = next(l for l in model.layers if not l.race)
+    g = torch.Generator(device=dev).manual_seed(3)
+    hd, hq, hkv = cfg.hidden // cfg.n_head, cfg.n_head, cfg.n_kv_head
+    q = torch.randn(B, hq, hd, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, hkv, hd, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, hkv, hd, device=dev, generator=g).to(torch.bfloat16)
+    st = race_layer.state
+    length = torch.tensor([model.n_tokens - 1], dtype=torch.int32, device=dev)
+    runs = {
+        "race_decode_step": (lambda: st.step(q, k, v), 2 * (st.S + st.S * hd) * 4 * B * hkv),
+        "gqa_decode_attn": (lambda: ops.gqa_decode_attention(q, k, v, soft_layer.cache[0], soft_layer.cache[1],
+                                                             length, soft_layer.attn_ws, soft_layer.n_splits),
+                            B * hkv * model.n_tokens * hd * 2 * 2),
+    }
+    out = {}
+    for name, (fn, nbytes) in runs.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()  # device time only: `reps` launches back to back, no host gaps
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del graph
+        us = a.elapsed_time(b) / reps * 1e3
+        out[name] = {"us_per_launch": us, "hbm_bytes_per_launch": nbytes, "achieved_gbs": nbytes / us / 1e3,
+                     "frac_of_hbm": nbytes / us / 1e3 / hbm, "peak_gbs": hbm, "peak_source": src,
+                     "launches_timed": reps}
+    return out
+
+
 def run_hybrid(args):
     """Config 4: hybrid decode, Llama-3.2-1B architecture with random-init bf16 weights (std
     0.02), odd layers RACE (L=8 x P=4) through the fused decode step, even layers softmax GQA
@@ -356,6 +403,7 @@ def run_hybrid(args):
         s4.record()
         torch.cuda.synchronize()
     prefill_ms, eager_ms, decode_ms = s0.elapsed_time(s1), s1.elapsed_time(s2), s3.elapsed_time(s4)
+    kern = decode_kernel_times(model, cfg, B, dev)
     line = {"metric": "hybrid decode tokens/s (cfg4)", "value": B * n_dec / (decode_ms / 1e3), "unit": "tokens/s",
             "n_gpus": 1, "steps": n_dec, "warmup": n_eager, "ms_per_step": decode_ms / n_dec, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -365,7 +413,7 @@ def run_hybrid(args):
                        "hidden": cfg.hidden, "heads": cfg.n_head, "kv_heads": cfg.n_kv_head, "tables_L": cfg.race_L,
                        "planes_P": cfg.race_P, "decode_step": "one CUDA graph replay per token"},
             "prefill_ms": prefill_ms, "prefill_tokens_per_s": B * T / (prefill_ms / 1e3),
-            "eager_ms_per_step": eager_ms / n_eager,
+            "eager_ms_per_step": eager_ms / n_eager, "decode_kernels": kern,
             "gpu_launches": int(lib_launches) * n_dec,
             "library_launches_per_step": int(lib_launches),
             "clocks": clk.summary()}

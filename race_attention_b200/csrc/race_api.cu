@@ -15,6 +15,7 @@
 #include <cstring>
 #include <initializer_list>
 #include <mutex>
+#include <set>
 #include <utility>
 #include <vector>
 
@@ -194,12 +195,31 @@ T *at(void *ws, size_t off) {
   return reinterpret_cast<T *>(static_cast<char *>(ws) + off);
 }
 
+// All of the unified L1/shared array as shared memory, so that as many CTAs fit as
+// their shared-memory needs allow (the driver's default split can leave room for
+// fewer).  Set once per kernel and device: the first launch happens outside any
+// stream capture, later ones (possibly inside a capture) make no runtime call.
+int set_carveout(const void *kernel) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaGetDevice failed");
+  static std::mutex mu;
+  static std::set<std::pair<const void *, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return RACE_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaFuncSetAttribute(carveout): %s", cudaGetErrorString(e));
+  done.insert({kernel, dev});
+  return RACE_OK;
+}
+
 template <typename K>
 int set_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaFuncSetAttribute(%zu B smem): %s", bytes, cudaGetErrorString(e));
   }
+  return RACE_OK;
   return RACE_OK;
 }
 
@@ -1119,16 +1139,25 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype, con
   if (D < 1 || D > race::dec::NT) return fail(RACE_ERR_SHAPE, "D=%lld out of range [1,%d]", (long long)D, race::dec::NT);
   const size_t sm = sizeof(float) * race::dec::smem_floats((int)D, (int)S, (int)(L * P), (int)group);
   cudaStream_t s = as_stream(stream);
+  auto launch = [&](auto kernel, auto *qq, auto *kk, auto *vv, auto *oo) -> int {
+    RACE_TRY(set_smem(kernel, sm));
+    RACE_TRY(set_carveout(reinterpret_cast<const void *>(kernel)));  // 4 CTAs per SM
+    kernel<<<(unsigned)Nkv, race::dec::NT, sm, s>>>(qq, kk, vv, planes_T, A, B, oo, (int)group, (int)D, (int)L,
+                                                    (int)P, eps, logit_scale);
+    return RACE_OK;
+  };
+  using bf = __nv_bfloat16;
+  constexpr int MAXG = race::dec::MAX_GROUP;
   if (dtype == RACE_F32) {
-    RACE_TRY(set_smem(race::dec::decode_step<float>, sm));
-    race::dec::decode_step<float><<<(unsigned)Nkv, race::dec::NT, sm, s>>>(
-        (const float *)q, (const float *)k, (const float *)v, planes_T, A, B, (float *)out, (int)group, (int)D,
-        (int)L, (int)P, eps, logit_scale);
+    RACE_TRY(group <= 4 ? launch(race::dec::decode_step<float, 4>, (const float *)q, (const float *)k,
+                                 (const float *)v, (float *)out)
+                        : launch(race::dec::decode_step<float, MAXG>, (const float *)q, (const float *)k,
+                                 (const float *)v, (float *)out));
   } else {
-    RACE_TRY(set_smem(race::dec::decode_step<__nv_bfloat16>, sm));
-    race::dec::decode_step<__nv_bfloat16><<<(unsigned)Nkv, race::dec::NT, sm, s>>>(
-        (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, (const __nv_bfloat16 *)v, planes_T, A, B,
-        (__nv_bfloat16 *)out, (int)group, (int)D, (int)L, (int)P, eps, logit_scale);
+    RACE_TRY(group <= 4 ? launch(race::dec::decode_step<bf, 4>, (const bf *)q, (const bf *)k, (const bf *)v,
+                                 (bf *)out)
+                        : launch(race::dec::decode_step<bf, MAXG>, (const bf *)q, (const bf *)k, (const bf *)v,
+                                 (bf *)out));
   }
   RACE_TRY(check_launch("decode_step"));
   return ok();

@@ -36,6 +36,27 @@ def test_prefill_then_decode(dtype, tol, Hq, Hkv):
     assert st.tokens == T
 
 
+@pytest.mark.parametrize("D,Hq,Hkv,L,P", [(30, 16, 2, 4, 3), (32, 12, 2, 4, 3), (64, 10, 2, 8, 4)])
+def test_decode_generic_shapes(D, Hq, Hkv, L, P):
+    """Decode steps for head dims off the float4 path (D % 4 != 0) and query groups above
+    4 (the wide-accumulator kernel), fp32, against the oracle's rows."""
+    import race_attention_b200 as rb
+    B, T0, steps = 2, 20, 5
+    g = torch.Generator().manual_seed(D + Hq)
+    T = T0 + steps
+    Q = torch.randn(B, Hq, T, D, generator=g)
+    K = torch.randn(B, Hkv, T, D, generator=g)
+    V = torch.randn(B, Hkv, T, D, generator=g)
+    planes = torch.randn(D, L * P, generator=g)
+    grp = Hq // Hkv
+    ref, _, _ = O.race_qkv_fwd(Q, K.repeat_interleave(grp, 1), V.repeat_interleave(grp, 1), planes, L, P)
+    ref = ref.reshape(B, Hq, T, D)
+    _, st = rb.prefill_with_state(Q[:, :, :T0].cuda(), K[:, :, :T0].cuda(), V[:, :, :T0].cuda(), planes.cuda(), L, P)
+    for t in range(T0, T):
+        o = st.step(Q[:, :, t].cuda(), K[:, :, t].cuda(), V[:, :, t].cuda())
+        assert relerr(o, ref[:, :, t]) < 1e-5, t
+
+
 def test_state_from_prefill_with_initial_state():
     import race_attention_b200 as rb
     g = torch.Generator().manual_seed(0)
