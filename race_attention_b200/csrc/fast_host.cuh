@@ -40,14 +40,40 @@ inline int sm_count() {
   return cached[dev];
 }
 
-// One CTA (one SM) per (stream, segment); about four waves of CTAs.
+// Largest segment count a plan may use: four waves at 256 SMs (the workspace bound).
+inline int64_t max_segments(int64_t N, int64_t nchunks) {
+  int64_t m = (4 * (int64_t)256) / N;
+  if (m < 1) m = 1;
+  return m < nchunks ? m : nchunks;
+}
+
+// One CTA (one SM) per (stream, segment), from about four waves of CTAs: among the
+// segment counts between that and the workspace bound, the one with the smallest
+// waves x (chunks per segment + 2), the 2 standing for a segment's fixed start and end
+// work (the last wave of a launch is otherwise partly idle: 32 streams on 148 SMs give
+// 576 CTAs = 3.89 waves at 18 segments, 736 = 4.97 at 23).
 inline Plan plan(int64_t N, int64_t T, int64_t S, int sms) {
   Plan p;
   p.nchunks = (int)((T + fk::C - 1) / fk::C);
   int64_t want = (4 * (int64_t)sms) / N;
   if (want < 1) want = 1;
   if (want > p.nchunks) want = p.nchunks;
-  p.seg_chunks = (int)((p.nchunks + want - 1) / want);
+  const int64_t cap = max_segments(N, p.nchunks);
+  auto cost = [&](int64_t cand, int64_t *nseg) {
+    const int64_t sc = (p.nchunks + cand - 1) / cand;
+    *nseg = (p.nchunks + sc - 1) / sc;
+    return ((N * *nseg + sms - 1) / sms) * (sc + 2);
+  };
+  int64_t best_seg = 0, best = cost(want, &best_seg);
+  for (int64_t cand = want + 1; cand <= cap; ++cand) {
+    int64_t ns = 0;
+    const int64_t c = cost(cand, &ns);
+    if (c < best) {
+      best = c;
+      best_seg = ns;
+    }
+  }
+  p.seg_chunks = (int)((p.nchunks + best_seg - 1) / best_seg);
   p.nseg = (p.nchunks + p.seg_chunks - 1) / p.seg_chunks;
   const size_t E = (size_t)S + (size_t)S * fk::HD;
   p.status_off = 0;
