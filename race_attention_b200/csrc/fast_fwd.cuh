@@ -644,19 +644,33 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
       const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
       const uint32_t id_ones = tc::idesc_bf16(GB, 16, true, true);
-      bool ok = tc::mbar_wait(&bars[TB_INIT], 0, abort);  // planes + ones column written
-      for (int c = 0; c < nch && ok; ++c) {
-        const int st = c & 1;
-        ok = tc::mbar_wait(&bars[TB_FULL0 + st], (c >> 1) & 1, abort);
-        if (!ok) break;
-        tc::tc_fence_after();
+      auto issue_proj = [&](int st) {
         for (int k0 = 0; k0 < HD; k0 += 16)
           tc::mma_bf16(tmem + 0, tc::desc_kmajor(sbase + P.k + st * TILE, k0, TILE),
                        tc::desc_kmajor(sbase + P.planes, k0, 0), id_proj, k0 > 0);
         tc::mma_commit(&bars[TB_PROJ]);
+      };
+      bool ok = tc::mbar_wait(&bars[TB_INIT], 0, abort);  // planes + ones column written
+      if (ok) ok = tc::mbar_wait(&bars[TB_FULL0], 0, abort);
+      if (ok) {
+        tc::tc_fence_after();
+        issue_proj(0);
+      }
+      // Per chunk c: [PK c] the next chunk's projection first (its K tile is in the other
+      // stage; the epilogue has read proj c), then the sums for c.  MMAs complete in issue
+      // order, so proj c+1 is ready while the sums of c run and the epilogue's soft hash of
+      // c+1 overlaps them; the stage of c refills once the sums complete.
+      for (int c = 0; c < nch && ok; ++c) {
+        const int st = c & 1;
         ok = tc::mbar_wait(&bars[TB_PK], c & 1, abort);
         if (!ok) break;
         tc::tc_fence_after();
+        if (c + 1 < nch) {
+          ok = tc::mbar_wait(&bars[TB_FULL0 + (st ^ 1)], ((c + 1) >> 1) & 1, abort);
+          if (!ok) break;
+          tc::tc_fence_after();
+          issue_proj(st ^ 1);
+        }
         for (int g = 0; g < a.ngroups; ++g) {
           const uint32_t pk = sbase + P.pk + (uint32_t)g * 2 * TILE;
           for (int k0 = 0; k0 < C; k0 += 16) {
@@ -718,7 +732,9 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     for (int c = 0; c < nch && ok; ++c) {
       const int nt = min(C, a.T - (c_begin + c) * C);
       ok = tc::warp_wait(&bars[TB_PROJ], c & 1, abort);
-      if (ok && c > 0) ok = tc::warp_wait(&bars[TB_DONE], (c - 1) & 1, abort);  // Pk buffers free
+      // the states pass reads the accumulators, which hold this chunk's start state once the
+      // previous chunk's sums are complete
+      if (ok && c > 0 && states) ok = tc::warp_wait(&bars[TB_DONE], (c - 1) & 1, abort);
       if (!ok) break;
       __syncwarp();
       tc::tc_fence_after();
@@ -742,20 +758,36 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           if (hq == 0) a.chunkA[row] = av + a.eps;
         }
       }
-      for (int g = 0; g < a.ngroups; ++g) {
-        const int j0 = (g * 8 + hq * 2) * 4;
-        float pj[8], pr[32];
-        tc::tmem_ld8(tmem + lane_off + j0, pj);
-        tc::tmem_wait_ld();
+      // Pk of this row for every group in registers (overlapping the previous chunk's sums),
+      // then into the shared tiles once those sums, their readers, are complete
+      float pr[2][32];  // ngroups <= 2 (S <= 256)
 #pragma unroll
-        for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pr + 16 * i);
-        if (t >= nt) {
+      for (int g = 0; g < 2; ++g) {
+        if (g < a.ngroups) {
+          const int j0 = (g * 8 + hq * 2) * 4;
+          float pj[8];
+          tc::tmem_ld8(tmem + lane_off + j0, pj);
+          tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) pr[i] = 0.f;
+          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pr[g] + 16 * i);
+          if (t >= nt) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) pr[g][i] = 0.f;
+          }
         }
+      }
+      if (c > 0 && !states) {
+        ok = tc::warp_wait(&bars[TB_DONE], (c - 1) & 1, abort);
+        if (!ok) break;
+        __syncwarp();
+      }
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch)
-          tc::st_row_chunk(sbase + P.pk + (g * 2 + (hq >> 1)) * TILE, t, (hq & 1) * 4 + ch, pr + 8 * ch);
+      for (int g = 0; g < 2; ++g) {
+        if (g < a.ngroups) {
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch)
+            tc::st_row_chunk(sbase + P.pk + (g * 2 + (hq >> 1)) * TILE, t, (hq & 1) * 4 + ch, pr[g] + 8 * ch);
+        }
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
