@@ -143,3 +143,21 @@ def test_gqa_decode_validation():
     # workspace: fp32 partials (64 dims + max + sum) per query head and split, a ticket per kv stream, a status word
     assert lib.race_gqa_decode_workspace_bytes(2, 8, 2, 4) == 4 * 2 * 8 * 4 * 66 + 4 * 4 + 4
     assert lib.race_gqa_decode_workspace_bytes(0, 8, 2, 4) == 0
+
+
+def test_ops_refuse_host_tensors():
+    """The torch-level ops run only on the CUDA library: host tensors raise (no CPU
+    fallback), as the reference's extension does for non-CUDA inputs."""
+    import torch
+    from race_attention_b200 import ops
+    q = torch.zeros(2, 8, 64, dtype=torch.bfloat16)
+    kv = torch.zeros(2, 2, 64, dtype=torch.bfloat16)
+    cache = torch.zeros(2, 2, 16, 64, dtype=torch.bfloat16)
+    length = torch.zeros(1, dtype=torch.int32)
+    ws = torch.zeros(1024, dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.gqa_decode_attention(q, kv, kv, cache, cache, length, ws, 1)
+    planes = torch.zeros(64, 32)
+    A, B = torch.zeros(2, 128), torch.zeros(2, 128, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.decode_step(q.reshape(-1, 64), kv.reshape(-1, 64), kv.reshape(-1, 64), planes, A, B, 8, 4)
