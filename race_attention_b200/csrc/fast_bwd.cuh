@@ -504,39 +504,6 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       // chunk-start A + eps (stored by the forward walk)
       for (int s = threadIdx.x; s < S; s += NET) sA[s] = a.chunkA[((size_t)n * a.nchunks + cg) * S + s];
       tc::named_bar_sync(N3_ESYNC, NET);  // sA visible to all epilogue threads
-      // ---- P1m = tril-masked dO V^T
-      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_P1], k & 1, abort));
-      tc::tc_fence_after();
-      if (ok) {
-        // 32 columns at a time; column runs all at or above the diagonal store zeros without
-        // reading TMEM
-#pragma unroll
-        for (int h = 0; h < CW / 32; ++h) {
-          const int col0 = CW * hq + 32 * h;  // first token column of this run
-          float v[32];
-          if (col0 < 32 * q4 + 32) {
-            tc::tmem_ld32(tmem + lane_off + B3_X + col0, v);
-            tc::tmem_wait_ld();
-            if (col0 + 32 > 32 * q4) {  // the run holds this row's diagonal (col0 == 32 q4)
-              float dg = 0.f;
-#pragma unroll
-              for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
-              sDiag[t] = dg;  // fp32 diagonal P1[t][t] (the exact-diagonal terms below)
-#pragma unroll
-              for (int i = 0; i < 32; ++i)  // strictly lower: the diagonal term is added in fp32
-                if (i >= lane) v[i] = 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          }
-#pragma unroll
-          for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + 4 * h + ch, v + 8 * ch);
-        }
-      }
-      tc::fence_async_smem();
-      tc::tc_fence_before();
-      tc::named_bar_arrive(N3_P1M, NT);
       for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
         // tanh, plane sigmoids of the slot's tables ; 1/(A + eps), then dpq, then the diagonal terms
@@ -595,8 +562,46 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::named_bar_arrive(N3_PK, NT);
+        if (g == 0) {
+          // P1m after the first group's Pk: the Pk work overlaps the chunk's V / dO loads and
+          // the dO V^T MMA (the control warp takes {PK} before {P1M})
+          // ---- P1m = tril-masked dO V^T
+          if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_P1], k & 1, abort));
+          tc::tc_fence_after();
+          if (ok) {
+            // 32 columns at a time; column runs all at or above the diagonal store zeros without
+            // reading TMEM
+#pragma unroll
+            for (int h = 0; h < CW / 32; ++h) {
+              const int col0 = CW * hq + 32 * h;  // first token column of this run
+              float v[32];
+              if (col0 < 32 * q4 + 32) {
+                tc::tmem_ld32(tmem + lane_off + B3_X + col0, v);
+                tc::tmem_wait_ld();
+                if (col0 + 32 > 32 * q4) {  // the run holds this row's diagonal (col0 == 32 q4)
+                  float dg = 0.f;
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) dg = i == lane ? v[i] : dg;
+                  sDiag[t] = dg;  // fp32 diagonal P1[t][t] (the exact-diagonal terms below)
+#pragma unroll
+                  for (int i = 0; i < 32; ++i)  // strictly lower: the diagonal term is added in fp32
+                    if (i >= lane) v[i] = 0.f;
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+              }
+#pragma unroll
+              for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.p1m + blk, t, ch0 + 4 * h + ch, v + 8 * ch);
+            }
+          }
+          tc::fence_async_smem();
+          tc::tc_fence_before();
+          tc::named_bar_arrive(N3_P1M, NT);
+        }
         // sGA (double-buffered by group parity: a warp may write the next group's
-        // copy while a slower one still reads this one) complete before any read
+        // copy while a slower one still reads this one), and at the first group the fp32
+        // diagonal, complete before any read
         tc::named_bar_sync(N3_GSYNC, NET);
         // ---- W = pq / (A + eps)
         if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_APREF], u & 1, abort));
