@@ -2,7 +2,7 @@
 
 Run once where the reference tree exists (it never exists on a GPU box):
 
-    CXX=/usr/bin/g++ python tests/golden/make_golden.py [--ref /root/reference]
+    CXX=/usr/bin/g++ python tests/golden/make_golden.py [--ref <path of the reference checkout>]
 
 It imports the reference's own modules from ``<ref>/scaling``:
   * build_planes_protos / soft_hash_probs / race_prefix_ref (race_common.py)

@@ -2,7 +2,7 @@
 
 Run once where the reference tree exists (it never exists on a GPU box):
 
-    python tests/golden/make_golden_ace.py [--ref /root/reference]
+    python tests/golden/make_golden_ace.py [--ref <path of the reference checkout>]
 
 It imports ``BatchedACE`` from ``<ref>/scaling/benchmark_time.py`` (shared planes; the
 module's plotting import is replaced by an empty stand-in, it is not used), runs it in
