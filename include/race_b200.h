@@ -89,6 +89,14 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D,
                          int64_t L, int64_t P, int dtype, int64_t chunk,
                          size_t *bytes);
 
+/* The tcgen05 path's work split for N streams of T tokens on a device with `sms`
+ * SMs (pure host function): *nseg segments of *seg_chunks 128-token chunks per
+ * stream, one CTA each, and *max_nseg, the segment count the workspace from
+ * race_workspace_bytes() has room for (a plan never exceeds it).  For
+ * inspection and tests; the library plans by itself on the current device. */
+int race_plan_segments(int64_t N, int64_t T, int64_t S, int sms, int *nseg, int *seg_chunks,
+                       int *max_nseg);
+
 /* ---- probability-level operator -----------------------------------------
  * Replaces race_fused_fwd (kernels/gpu/forward_kernel.cu:110-137), bound by
  * pybind at kernels/gpu/race_cuda_binding.cpp:12-17.  out[N,T,D] fp32 is fully

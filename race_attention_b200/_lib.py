@@ -47,6 +47,7 @@ SIGNATURES = {
     "race_state_from_prefill": [_P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
     "race_decode_step": [_P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P],
     "race_gqa_decode_workspace_bytes": [_I64, _I64, _I64, _I],
+    "race_plan_segments": [_I64, _I64, _I64, _I, _P, _P, _P],
     "race_gqa_decode_attn": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _F, _P],
     "race_fwd_bthd": [_P, _P, _P, _I, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
     "race_bwd_bthd": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _F, _P,

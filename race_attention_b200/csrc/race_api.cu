@@ -711,6 +711,19 @@ int race_kernel_time(int kernel, double *total_ms, long long *launches) {
   return ok();
 }
 
+int race_plan_segments(int64_t N, int64_t T, int64_t S, int sms, int *nseg, int *seg_chunks, int *max_nseg) {
+  RACE_NONNULL(nseg);
+  RACE_NONNULL(seg_chunks);
+  RACE_NONNULL(max_nseg);
+  if (N < 1 || T < 1 || S < 1) return fail(RACE_ERR_SHAPE, "N, T, S must be >= 1");
+  if (sms < 1 || sms > 256) return fail(RACE_ERR_ARG, "sms=%d not in [1, 256]", sms);
+  const fh::Plan p = fh::plan(N, T, S, sms);
+  *nseg = p.nseg;
+  *seg_chunks = p.seg_chunks;
+  *max_nseg = fh::plan(N, T, S, 256).nseg;
+  return ok();
+}
+
 int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int64_t L, int64_t P, int dtype,
                          int64_t chunk, size_t *bytes) {
   (void)chunk;

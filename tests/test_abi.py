@@ -161,3 +161,25 @@ def test_ops_refuse_host_tensors():
     A, B = torch.zeros(2, 128), torch.zeros(2, 128, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.decode_step(q.reshape(-1, 64), kv.reshape(-1, 64), kv.reshape(-1, 64), planes, A, B, 8, 4)
+
+
+def test_segment_plan_stays_within_the_workspace():
+    """The tcgen05 path's segment planner never picks more segments than the workspace
+    (sized for 256 SMs) holds, covers every chunk with no empty segment, and at the
+    config-2 geometry on 148 SMs picks 23 segments (4.97 waves instead of 3.89)."""
+    lib = _lib.load()
+    nseg, sc, mx = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    for N in (1, 2, 3, 8, 32, 96, 200, 1024, 5000):
+        for T in (1, 127, 128, 129, 4096, 32768, 1 << 20, 12582912):
+            for S in (128, 256):
+                for sms in (1, 80, 132, 148, 160, 256):
+                    rc = lib.race_plan_segments(N, T, S, sms, ctypes.byref(nseg), ctypes.byref(sc), ctypes.byref(mx))
+                    assert rc == 0
+                    nch = (T + 127) // 128
+                    assert 1 <= nseg.value <= mx.value, (N, T, S, sms)
+                    assert sc.value >= 1 and nseg.value * sc.value >= nch > (nseg.value - 1) * sc.value
+    assert lib.race_plan_segments(32, 1 << 20, 256, 148, ctypes.byref(nseg), ctypes.byref(sc), ctypes.byref(mx)) == 0
+    assert (nseg.value, sc.value) == (23, 357)
+    codes = status_codes()
+    assert lib.race_plan_segments(32, 1 << 20, 256, 0, ctypes.byref(nseg), ctypes.byref(sc),
+                                  ctypes.byref(mx)) == codes["RACE_ERR_ARG"]
