@@ -121,6 +121,23 @@ def make_inputs(cfg, device, seed):
     return xs
 
 
+def sample_length(H, S, D, want=16384):
+    """Tokens per stream of the CPU sample: `want` (the planned T = 16,384) unless the
+    reference CPU path's host memory does not fit in half of what is available.  That
+    path expands V x S into [N*S, T, D] float32 and keeps about five tensors of that
+    size alive (scaling/race_causal_cpu.py:33-38, 53, 66-71)."""
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        avail = None
+    Ts = want
+    while avail is not None and Ts > 1024 and 5 * 4 * H * S * Ts * D > avail // 2:
+        Ts //= 2
+    why = "" if Ts == want else f"; T capped at {Ts} by host memory, {avail / 2**30:.0f} GiB available"
+    return Ts, why
+
+
 def cpu_reference_sample(cfg, steps, warmup):
     """Reference CPU path on a bounded sample of cfg: all heads, T_s tokens.
 
@@ -129,7 +146,7 @@ def cpu_reference_sample(cfg, steps, warmup):
     import race_attention_b200.race_common as rc
     B, H, T, D, L, P, dtype, scale = cfg
     torch.set_num_threads(os.cpu_count() or 1)
-    Ts = 1024 if L * (1 << P) >= 256 else 2048
+    Ts, why = sample_length(H, L << P, D)
     g = torch.Generator().manual_seed(0)
     Q, K, V, dO = (torch.randn(1, H, Ts, D, generator=g) for _ in range(4))
     Q, K, V = Q * scale, K * scale, V * scale
@@ -155,7 +172,7 @@ def cpu_reference_sample(cfg, steps, warmup):
     cores = torch.get_num_threads() if kind == "reference" else 1
     meta = {"kind": kind, "cores": cores,
             "sample": f"B=1 H={H} T={Ts} D={D} L={L} P={P} fp32 fwd+bwd (1/{B * T // Ts} of the tokens; "
-                      f"path is linear in T), median of {steps} after {warmup} warm-up, "
+                      f"path is linear in T{why}), median of {steps} after {warmup} warm-up, "
                       f"{os.cpu_count()} host threads available",
             "sec_per_step": med}
     return Ts / med, meta

@@ -82,6 +82,34 @@ unsigned long long race_launch_counter(void);
 #define RACE_KT_COUNT 5
 int race_kernel_timing(int enable);
 int race_kernel_time(int kernel, double *total_ms, long long *launches);
+/* (The timing state is process-wide: one event list per kernel id, shared by
+ * every host thread and stream.  Two threads timing at once mix their totals;
+ * it is a measurement aid for one timing thread, not a per-stream facility.) */
+
+/* Bounded device-side waits (no counterpart in the reference, whose kernels
+ * launch with no error check: kernels/gpu/forward_kernel.cu:128-135).  Every
+ * wait of the tcgen05 kernels on an mbarrier gives up after a poll limit.  A
+ * kernel whose wait gave up stops working (every thread still takes every
+ * barrier step), waits for its own tensor-core work in flight, frees its
+ * tensor memory, returns, and leaves a non-zero status word at the head of
+ * the call's workspace; that call's outputs are then invalid.  These settings
+ * are process-wide and apply to calls made after them, from any thread.
+ *
+ * race_set_wait_limit: polls before a wait gives up (0 restores the default,
+ *   2^26 polls, about a second on a B200).
+ * race_set_status_check: 1 makes every later tcgen05-path call wait for its
+ *   stream, read the status word and return RACE_ERR_TIMEOUT when a wait gave
+ *   up (this synchronises, so not inside stream capture); 0 (the default)
+ *   leaves the word for race_read_status.
+ * race_read_status: waits for `stream`, then copies the status word of
+ *   `workspace` to *status (0: every wait completed).
+ * race_test_withhold_first_load: test hook.  1 makes the forward kernels
+ *   issue no tile load for the first chunk of each segment, so their first
+ *   waits expire with nothing in flight and the call reports a timeout. */
+int race_set_wait_limit(unsigned int polls);
+int race_set_status_check(int synchronous);
+int race_read_status(const void *workspace, void *stream, int *status);
+int race_test_withhold_first_load(int on);
 
 /* Bytes of device workspace `op` needs for these sizes (pure host function).
  * chunk <= 0 selects the library default. */

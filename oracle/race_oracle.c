@@ -226,3 +226,232 @@ void oracle_race_bwd(const double *pk, const double *pq, const double *V, const 
     free(B);
     free(beta);
 }
+
+/*
+ * ---------------------------------------------------------------------------
+ * Whole-layer oracle for long sequences, one stream at a time, multithreaded
+ * (OpenMP).  Same algorithm and fp64 accumulation as oracle_soft_hash +
+ * oracle_race_fwd / oracle_race_bwd + oracle_soft_hash_bwd above
+ * (scaling/race_common.py:36-90, scaling/race_causal_cpu.py:52-72 over
+ * kernels/cpu/race_pref.cpp:104-220); only the work is split so that T in the
+ * millions finishes in seconds:
+ *   - soft hash and its backward: parallel over tokens;
+ *   - per-bucket scans (A_t, 1/(A_t+eps), dpq, dpk): parallel over buckets s;
+ *   - the D-wide sums (out, dV): parallel over d, each thread carrying the
+ *     bucket states of its own d columns.
+ * The [T,S] intermediates (pk, W = pq/(A+eps), 1/(A+eps), dpk, dpq) are
+ * stored as float (a rounding of 6e-8 relative, far below every tolerance
+ * they are used at) so that T = 4M, S = 128 needs about 10 GB of host memory;
+ * every sum is accumulated in double.  Inputs are float (bf16 inputs convert
+ * exactly).
+ */
+#include <omp.h>
+
+static void hash_rows_f(const float *X, long T, long D, const double *planes_T, long L, long P,
+                        double scale, float *probs, double *th_out /* [T,LP] or NULL */)
+{
+    const long LP = L * P, R = 1L << P, S = L * R;
+#pragma omp parallel
+    {
+        double *a = (double *)malloc(sizeof(double) * LP);
+        double *lg = (double *)malloc(sizeof(double) * R);
+#pragma omp for schedule(static)
+        for (long t = 0; t < T; ++t) {
+            const float *x = X + t * D;
+            for (long j = 0; j < LP; ++j) {
+                double acc = 0.0;
+                for (long d = 0; d < D; ++d) acc += (double)x[d] * planes_T[d * LP + j];
+                const double th = tanh(acc);
+                if (th_out) th_out[t * LP + j] = th;
+                a[j] = th * scale;
+            }
+            for (long l = 0; l < L; ++l) {
+                double mx = -INFINITY;
+                for (long r = 0; r < R; ++r) {
+                    double v = 0.0;
+                    for (long p = 0; p < P; ++p) v += a[l * P + p] * corner_sign(r, p, P);
+                    lg[r] = v;
+                    if (v > mx) mx = v;
+                }
+                double z = 0.0;
+                for (long r = 0; r < R; ++r) { lg[r] = exp(lg[r] - mx); z += lg[r]; }
+                for (long r = 0; r < R; ++r) probs[t * S + l * R + r] = (float)(lg[r] / z);
+            }
+        }
+        free(a);
+        free(lg);
+    }
+}
+
+/* dX[t] = gradient of <dprobs[t], soft_hash(X[t])>, from the token's tanh values. */
+static void hash_rows_bwd_f(long T, long D, const double *planes_T, long L, long P, double scale,
+                            const float *probs, const double *th, const float *dprobs, double *dX)
+{
+    const long LP = L * P, R = 1L << P, S = L * R;
+#pragma omp parallel
+    {
+        double *da = (double *)malloc(sizeof(double) * LP);
+#pragma omp for schedule(static)
+        for (long t = 0; t < T; ++t) {
+            const float *pr = probs + t * S;
+            const float *g = dprobs + t * S;
+            for (long l = 0; l < L; ++l) {
+                double c = 0.0;
+                for (long r = 0; r < R; ++r) c += (double)pr[l * R + r] * g[l * R + r];
+                for (long p = 0; p < P; ++p) {
+                    double acc = 0.0;
+                    for (long r = 0; r < R; ++r)
+                        acc += (double)pr[l * R + r] * ((double)g[l * R + r] - c) * corner_sign(r, p, P);
+                    const double tj = th[t * LP + l * P + p];
+                    da[l * P + p] = acc * scale * (1.0 - tj * tj);
+                }
+            }
+            for (long d = 0; d < D; ++d) {
+                double acc = 0.0;
+                for (long j = 0; j < LP; ++j) acc += da[j] * planes_T[d * LP + j];
+                dX[t * D + d] = acc;
+            }
+        }
+        free(da);
+    }
+}
+
+/*
+ * One stream of the full layer: Q, K, V, dO [T,D] float; planes_T [D, L*P].
+ * Forward: out [T,D], A_fin [S], B_fin [S,D] (any may be NULL except out).
+ * Backward (when dO != NULL): dQ, dK, dV [T,D] (double).
+ */
+int oracle_layer_stream(const float *Q, const float *K, const float *V, const float *dO,
+                        long T, long D, const double *planes_T, long L, long P,
+                        double logit_scale, double eps,
+                        double *out, double *A_fin, double *B_fin,
+                        double *dQ, double *dK, double *dV)
+{
+    const long LP = L * P, S = L << P;
+    float *pk = (float *)malloc(sizeof(float) * T * S);
+    float *pq = (float *)malloc(sizeof(float) * T * S);   /* becomes W = pq / (A + eps) */
+    float *inv = (float *)malloc(sizeof(float) * T * S);  /* 1 / (A + eps) */
+    double *thK = dO ? (double *)malloc(sizeof(double) * T * LP) : NULL;
+    double *thQ = dO ? (double *)malloc(sizeof(double) * T * LP) : NULL;
+    if (!pk || !pq || !inv || (dO && (!thK || !thQ))) {
+        free(pk); free(pq); free(inv); free(thK); free(thQ);
+        return 1;
+    }
+    hash_rows_f(K, T, D, planes_T, L, P, logit_scale, pk, thK);
+    hash_rows_f(Q, T, D, planes_T, L, P, logit_scale, pq, thQ);
+
+    /* per bucket: A_t, 1/(A_t+eps), W */
+#pragma omp parallel for schedule(static)
+    for (long s = 0; s < S; ++s) {
+        double A = 0.0;
+        for (long t = 0; t < T; ++t) {
+            A += pk[t * S + s];
+            const double iv = 1.0 / (A + eps);
+            inv[t * S + s] = (float)iv;
+            pq[t * S + s] = (float)(pq[t * S + s] * iv);
+        }
+        if (A_fin) A_fin[s] = A;
+    }
+    /* out[t,d] = sum_s W[t,s] B_t[s,d], per column d */
+#pragma omp parallel
+    {
+        double *B = (double *)malloc(sizeof(double) * S);
+#pragma omp for schedule(dynamic, 1)
+        for (long d = 0; d < D; ++d) {
+            for (long s = 0; s < S; ++s) B[s] = 0.0;
+            for (long t = 0; t < T; ++t) {
+                const double v = V[t * D + d];
+                const float *k = pk + t * S, *w = pq + t * S;
+                double o = 0.0;
+                for (long s = 0; s < S; ++s) {
+                    B[s] += (double)k[s] * v;
+                    o += (double)w[s] * B[s];
+                }
+                out[t * D + d] = o;
+            }
+            if (B_fin) for (long s = 0; s < S; ++s) B_fin[s * D + d] = B[s];
+        }
+        free(B);
+    }
+    if (!dO) {
+        free(pk); free(pq); free(inv);
+        return 0;
+    }
+    float *dpk = (float *)malloc(sizeof(float) * T * S);
+    float *dpq = (float *)malloc(sizeof(float) * T * S);
+    if (!dpk || !dpq) {
+        free(pk); free(pq); free(inv); free(thK); free(thQ); free(dpk); free(dpq);
+        return 1;
+    }
+    /* per bucket s: G_t = dO_t . B_t[s], dpq = G/(A+eps), alpha_t = -W G/(A+eps);
+     * then backwards: gA = sum_{t'>=t} alpha, gB = sum_{t'>=t} W dO, dpk = gA + V.gB */
+    int fail = 0;
+#pragma omp parallel
+    {
+        double *B = (double *)malloc(sizeof(double) * D);
+        double *beta = (double *)malloc(sizeof(double) * D);
+        double *alpha = (double *)malloc(sizeof(double) * T);
+        if (!B || !beta || !alpha) {
+#pragma omp atomic write
+            fail = 1;
+        }
+#pragma omp for schedule(dynamic, 1)
+        for (long s = 0; s < S; ++s) {
+            if (fail) continue;
+            for (long d = 0; d < D; ++d) B[d] = 0.0;
+            for (long t = 0; t < T; ++t) {
+                const double w = pk[t * S + s];
+                double G = 0.0;
+                for (long d = 0; d < D; ++d) {
+                    B[d] += w * V[t * D + d];
+                    G += (double)dO[t * D + d] * B[d];
+                }
+                const double iv = inv[t * S + s];
+                dpq[t * S + s] = (float)(G * iv);
+                alpha[t] = -(double)pq[t * S + s] * G * iv;
+            }
+            double gA = 0.0;
+            for (long d = 0; d < D; ++d) beta[d] = 0.0;
+            for (long t = T - 1; t >= 0; --t) {
+                const double w = pq[t * S + s];
+                gA += alpha[t];
+                double bv = 0.0;
+                for (long d = 0; d < D; ++d) {
+                    beta[d] += w * dO[t * D + d];
+                    bv += beta[d] * V[t * D + d];
+                }
+                dpk[t * S + s] = (float)(gA + bv);
+            }
+        }
+        free(B); free(beta); free(alpha);
+    }
+    if (!fail) {
+        /* dV[t,d] = sum_s pk[t,s] gB_t[s,d], per column d */
+#pragma omp parallel
+        {
+            double *beta = (double *)malloc(sizeof(double) * S);
+#pragma omp for schedule(dynamic, 1)
+            for (long d = 0; d < D; ++d) {
+                for (long s = 0; s < S; ++s) beta[s] = 0.0;
+                for (long t = T - 1; t >= 0; --t) {
+                    const double g = dO[t * D + d];
+                    const float *k = pk + t * S, *w = pq + t * S;
+                    double acc = 0.0;
+                    for (long s = 0; s < S; ++s) {
+                        beta[s] += (double)w[s] * g;
+                        acc += (double)k[s] * beta[s];
+                    }
+                    dV[t * D + d] = acc;
+                }
+            }
+            free(beta);
+        }
+        /* back to the probabilities of the soft hash: pq = W (A + eps) */
+#pragma omp parallel for schedule(static)
+        for (long i = 0; i < T * S; ++i) pq[i] = (float)((double)pq[i] / (double)inv[i]);
+        hash_rows_bwd_f(T, D, planes_T, L, P, logit_scale, pq, thQ, dpq, dQ);
+        hash_rows_bwd_f(T, D, planes_T, L, P, logit_scale, pk, thK, dpk, dK);
+    }
+    free(pk); free(pq); free(inv); free(thK); free(thQ); free(dpk); free(dpq);
+    return fail;
+}

@@ -36,6 +36,10 @@ SIGNATURES = {
     "race_launch_counter": [],
     "race_kernel_timing": [_I],
     "race_kernel_time": [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)],
+    "race_set_wait_limit": [ctypes.c_uint],
+    "race_set_status_check": [_I],
+    "race_read_status": [_P, _P, ctypes.POINTER(_I)],
+    "race_test_withhold_first_load": [_I],
     "race_workspace_bytes": [_I, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I64, ctypes.POINTER(_SZ)],
     "race_fwd_probs": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _I64, _P, _SZ, _P],
     "race_bwd_probs": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _I64, _P, _SZ, _P],
@@ -93,6 +97,10 @@ def load():
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        if os.environ.get("RACE_B200_CHECK") == "1":
+            # every tcgen05-path call waits for its stream and fails with
+            # RACE_ERR_TIMEOUT if a bounded device-side wait gave up
+            lib.race_set_status_check(1)
         _lib = lib
         return lib
 

@@ -54,6 +54,7 @@ struct BwdArgs {
   const float *seedA, *seedB;   // fix-up: suffix of later shards added to every segment's ([N,S], [N,S,64])
   const __nv_bfloat16 *dVloc;   // fix-up: the walk's dV when it is not in dV itself (split backward)
   int *err;
+  uint32_t wait_limit;          // polls before a bounded wait gives up (tc::kDefaultWaitPolls unless set)
 };
 
 // d proj of one table from the gradient g16 of its 16 corner probabilities.
@@ -218,9 +219,9 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
   const BwdSmem P = bwd_smem_plan(a.LP, a.S);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
   // no static shared memory (it would cost a 1 KB aligned block): the TMEM base
-  // and the abort flag live after the barriers
+  // and the wait control (abort flag, poll limit) live after the barriers
   uint32_t &s_tmem = *reinterpret_cast<uint32_t *>(sm + P.bars + 8 * V3_COUNT);
-  int &s_abort = *reinterpret_cast<int *>(sm + P.bars + 8 * V3_COUNT + 4);
+  int *s_abort = reinterpret_cast<int *>(sm + P.bars + 8 * V3_COUNT + 8);
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
@@ -232,7 +233,8 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
   const uint32_t T_GB = B3_ST, T_GA = B3_ST + 64 * nblk, T_DV = B3_ST + 80 * nblk;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    s_abort[0] = 0;
+    s_abort[1] = (int)a.wait_limit;
     for (int i = 0; i < V3_COUNT; ++i) tc::mbar_init(&bars[i], 1);
     tc::fence_mbar_init();
   }
@@ -241,7 +243,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
-  volatile int *abort = &s_abort;
+  volatile int *abort = s_abort;
 
   if (warp == NE) {
     // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
@@ -778,7 +780,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
   tc::tc_fence_before();
   __syncthreads();
   if (warp == NE) {
-    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    if (s_abort[0] && lane == 0) atomicExch(a.err, 1);
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -851,7 +853,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
   const FixSmem P = fix_smem_plan(a.LP, a.S);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
   __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
+  __shared__ int s_abort[2];  // wait control: abort flag, poll limit
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
@@ -863,7 +865,8 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
   const uint32_t T_DQ = FX_D + S, T_DK = T_DQ + 64, T_DV = T_DK + 64;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    s_abort[0] = 0;
+    s_abort[1] = (int)a.wait_limit;
     for (int i = 0; i < VF_COUNT; ++i) tc::mbar_init(&bars[i], 1);
     tc::fence_mbar_init();
   }
@@ -872,7 +875,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
-  volatile int *abort = &s_abort;
+  volatile int *abort = s_abort;
 
   if (warp == NEPI) {
     // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
@@ -1154,7 +1157,7 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
   tc::tc_fence_before();
   __syncthreads();
   if (warp == NEPI) {
-    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    if (s_abort[0] && lane == 0) atomicExch(a.err, 1);
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }

@@ -69,6 +69,9 @@ struct FwdArgs {
   const float *seedA;      // readout of a sequence shard: the earlier shards' state ([N,S], [N,S,64])
   const float *seedB;      // added to every segment's prefix (nullptr: none)
   int *err;
+  uint32_t wait_limit;     // polls before a bounded wait gives up (tc::kDefaultWaitPolls unless set)
+  int withhold_first_load;  // test hook: issue no tile load for the first chunk, so the first waits
+                            // expire with nothing in flight (the call then reports a timeout)
 };
 
 __device__ __forceinline__ float tanh_fast(float x) {
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   const FwdSmem P = fwd_smem_plan(a.ngroups, a.LP);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
   __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
+  __shared__ int s_abort[2];  // wait control: abort flag, poll limit
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
@@ -244,7 +247,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   const float *state0 = a.seg_state + ((size_t)n * a.nseg + seg) * E;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    s_abort[0] = 0;
+    s_abort[1] = (int)a.wait_limit;
     for (int i = 0; i < B_COUNT; ++i) tc::mbar_init(&bars[i], 1);
     tc::fence_mbar_init();
   }
@@ -253,7 +257,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
-  volatile int *abort = &s_abort;
+  volatile int *abort = s_abort;
 
   if (warp == NEPI) {
     // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
       tc::mma_commit(&bars[B_PROJ]);
     };
     bool ok = true;
-    if (leader && nch > 0) {
+    if (leader && nch > 0 && !a.withhold_first_load) {
       tc::prefetch_tmap(&tmQ);
       tc::prefetch_tmap(&tmK);
       tc::prefetch_tmap(&tmV);
@@ -560,7 +564,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
   tc::tc_fence_before();
   __syncthreads();
   if (warp == NEPI) {
-    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    if (s_abort[0] && lane == 0) atomicExch(a.err, 1);
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -601,7 +605,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
   const TotSmem P = tot_smem_plan(a.ngroups, a.LP);
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bars);
   __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
+  __shared__ int s_abort[2];  // wait control: abort flag, poll limit
   const uint32_t sbase = tc::smem_u32(sm);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x / a.nseg, seg = blockIdx.x % a.nseg;
@@ -615,7 +619,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
   const bool states = a.chunkA != nullptr;
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
+    s_abort[0] = 0;
+    s_abort[1] = (int)a.wait_limit;
     tc::mbar_init(&bars[TB_FULL0], 1);
     tc::mbar_init(&bars[TB_FULL1], 1);
     tc::mbar_init(&bars[TB_PROJ], 1);
@@ -630,13 +635,13 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
-  volatile int *abort = &s_abort;
+  volatile int *abort = s_abort;
 
   if (warp == NEPI) {
     if (lane == 0 && nch > 0) {
       tc::prefetch_tmap(&tmK);
       tc::prefetch_tmap(&tmV);
-      for (int c = 0; c < 2 && c < nch; ++c) {
+      for (int c = a.withhold_first_load ? 2 : 0; c < 2 && c < nch; ++c) {
         tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + c], 2 * TILE);
         tc::tma_load_4d(sm + P.k + c * TILE, &tmK, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
         tc::tma_load_4d(sm + P.v + c * TILE, &tmV, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
@@ -817,7 +822,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
   tc::tc_fence_before();
   __syncthreads();
   if (warp == NEPI) {
-    if (s_abort && lane == 0) atomicExch(a.err, 1);
+    if (s_abort[0] && lane == 0) atomicExch(a.err, 1);
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 256);
   }

@@ -55,10 +55,12 @@ inline int64_t max_segments(int64_t N, int64_t nchunks) {
 inline Plan plan(int64_t N, int64_t T, int64_t S, int sms) {
   Plan p;
   p.nchunks = (int)((T + fk::C - 1) / fk::C);
+  // (a device with more than 256 SMs plans within the same workspace bound: the
+  // segment count never exceeds max_segments, which the workspace is sized for)
+  const int64_t cap = max_segments(N, p.nchunks);
   int64_t want = (4 * (int64_t)sms) / N;
   if (want < 1) want = 1;
-  if (want > p.nchunks) want = p.nchunks;
-  const int64_t cap = max_segments(N, p.nchunks);
+  if (want > cap) want = cap;
   auto cost = [&](int64_t cand, int64_t *nseg) {
     const int64_t sc = (p.nchunks + cand - 1) / cand;
     *nseg = (p.nchunks + sc - 1) / sc;

@@ -19,6 +19,8 @@
 #include <utility>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "common.cuh"
 #include "decode.cuh"
 #include "fast_host.cuh"
@@ -46,6 +48,18 @@ int ok() {
 
 std::atomic<unsigned long long> g_launches{0};
 
+// Bounded-wait controls of the tcgen05 kernels (race_set_wait_limit,
+// race_set_status_check, race_test_withhold_first_load): process-wide
+// settings read when a call launches its kernels.
+std::atomic<uint32_t> g_wait_limit{0};  // 0: tc::kDefaultWaitPolls
+std::atomic<int> g_status_check{0};
+std::atomic<int> g_withhold_first_load{0};
+
+uint32_t wait_limit() {
+  const uint32_t v = g_wait_limit.load(std::memory_order_relaxed);
+  return v ? v : race::tc::kDefaultWaitPolls;
+}
+
 int check_launch(const char *what) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();
@@ -68,9 +82,25 @@ KernelTimer &ktimer() {
   return t;
 }
 
+// NVTX range over a host-side phase (a profiler shows each tcgen05 launch and each
+// forward / backward call by name; without a profiler attached these are no-ops).
+class NvtxRange {
+ public:
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
+
+const char *kernel_range_name(int id) {
+  static const char *names[RACE_KT_COUNT] = {"race fwd_totals_kernel", "race fwd_readout_kernel",
+                                             "race bwd_rev_kernel", "race chunk_scan", "race bwd_fix_kernel"};
+  return id >= 0 && id < RACE_KT_COUNT ? names[id] : "race kernel";
+}
+
 class KernelScope {
  public:
-  KernelScope(int id, cudaStream_t s) : id_(id), s_(s) {
+  KernelScope(int id, cudaStream_t s) : id_(id), s_(s), range_(kernel_range_name(id)) {
     KernelTimer &t = ktimer();
     std::lock_guard<std::mutex> g(t.mu);
     if (!t.on) return;
@@ -100,6 +130,7 @@ class KernelScope {
   }
   int id_;
   cudaStream_t s_;
+  NvtxRange range_;
   cudaEvent_t e0_ = nullptr, e1_ = nullptr;
 };
 
@@ -420,6 +451,8 @@ int fast_args(fk::FwdArgs &a, const fh::Plan &pl, int64_t N, int64_t T, int64_t 
   a.chunkB = nullptr;
   a.seedA = a.seedB = nullptr;
   a.err = at<int>(ws, pl.status_off);
+  a.wait_limit = wait_limit();
+  a.withhold_first_load = g_withhold_first_load.load(std::memory_order_relaxed);
   return RACE_OK;
 }
 
@@ -473,6 +506,7 @@ int fast_totals_and_scan(const void *K, const void *V, const float *planes_T, co
 int fast_forward(const void *Q, const void *K, const void *V, const float *planes_T, void *out, const float *A0,
                  const float *B0, float *Af, float *Bf, int64_t N, int64_t T, int64_t L, float eps, float scale,
                  void *ws, cudaStream_t s, void *saved = nullptr, bool finish = false, int64_t H = 1) {
+  NvtxRange range(finish ? "race forward (finish)" : "race forward");
   fk::FwdArgs a;
   CUtensorMap mQ, mK, mV;
   if (finish) {
@@ -510,6 +544,8 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
                   void *dK, void *dV, const float *A0, const float *B0, const float *gA, const float *gB, float *dA0,
                   float *dB0, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws, cudaStream_t s,
                   BwdMode mode, const void *saved = nullptr, int64_t H = 1) {
+  NvtxRange range(mode == BWD_FULL ? "race backward" : mode == BWD_LOCAL ? "race backward (local)"
+                                                                          : "race backward (finish)");
   const int64_t S = 16 * L;
   const fh::BwdPlan bp = fh::bwd_plan(N, T, S, fh::sm_count(), mode != BWD_FULL);
   fk::FwdArgs fa;
@@ -567,6 +603,7 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   b.seedA = b.seedB = nullptr;
   b.dVloc = nullptr;
   b.err = at<int>(ws, 0);
+  b.wait_limit = wait_limit();
   const unsigned grid = (unsigned)(N * bp.p.nseg);
   gen::Dims p = make_dims(N, T, S, fk::HD, eps);
   p.G = bp.p.nseg;
@@ -625,6 +662,22 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
   fk::bwd_fix_kernel<<<grid, fk::NTHR, xs.total, s>>>(mK, mV, mP, mVL, mOK, mOV, mOQ, b);
   ks.stop();
   return check_launch("fast bwd_fix");
+}
+
+// End of a tcgen05-path call: with race_set_status_check(1), wait for the stream
+// and turn a non-zero status word (a bounded device-side wait gave up) into
+// RACE_ERR_TIMEOUT; otherwise the word stays at the head of the workspace for
+// race_read_status.
+int fast_status(const void *ws, cudaStream_t s, const char *what) {
+  if (!g_status_check.load(std::memory_order_relaxed)) return ok();
+  int st = 0;
+  cudaError_t e = cudaMemcpyAsync(&st, ws, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "%s: status read: %s", what, cudaGetErrorString(e));
+  if (st != 0)
+    return fail(RACE_ERR_TIMEOUT, "%s: a bounded device-side wait gave up (status %d); outputs are invalid", what,
+                st);
+  return ok();
 }
 
 int check_fast_ptrs(std::initializer_list<const void *> ptrs) {
@@ -711,12 +764,39 @@ int race_kernel_time(int kernel, double *total_ms, long long *launches) {
   return ok();
 }
 
+int race_set_wait_limit(unsigned int polls) {
+  g_wait_limit.store(polls, std::memory_order_relaxed);
+  return ok();
+}
+
+int race_set_status_check(int synchronous) {
+  g_status_check.store(synchronous ? 1 : 0, std::memory_order_relaxed);
+  return ok();
+}
+
+int race_read_status(const void *workspace, void *stream, int *status) {
+  RACE_NONNULL(workspace);
+  RACE_NONNULL(status);
+  cudaStream_t s = as_stream(stream);
+  int st = 0;
+  cudaError_t e = cudaMemcpyAsync(&st, workspace, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "race_read_status: %s", cudaGetErrorString(e));
+  *status = st;
+  return ok();
+}
+
+int race_test_withhold_first_load(int on) {
+  g_withhold_first_load.store(on ? 1 : 0, std::memory_order_relaxed);
+  return ok();
+}
+
 int race_plan_segments(int64_t N, int64_t T, int64_t S, int sms, int *nseg, int *seg_chunks, int *max_nseg) {
   RACE_NONNULL(nseg);
   RACE_NONNULL(seg_chunks);
   RACE_NONNULL(max_nseg);
   if (N < 1 || T < 1 || S < 1) return fail(RACE_ERR_SHAPE, "N, T, S must be >= 1");
-  if (sms < 1 || sms > 256) return fail(RACE_ERR_ARG, "sms=%d not in [1, 256]", sms);
+  if (sms < 1 || sms > 65536) return fail(RACE_ERR_ARG, "sms=%d not in [1, 65536]", sms);
   const fh::Plan p = fh::plan(N, T, S, sms);
   *nseg = p.nseg;
   *seg_chunks = p.seg_chunks;
@@ -874,7 +954,7 @@ static int fwd_qkv_impl(const void *Q, const void *K, const void *V, int dtype, 
     }
     RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, A_final, B_final, N, T, L, eps, logit_scale, workspace, s,
                           saved, false, H));
-    return ok();
+    return fast_status(workspace, s, "forward");
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_FWD_QKV, N, T, S, D).total));
   if (dtype == RACE_F32)
@@ -918,7 +998,7 @@ static int bwd_qkv_impl(const void *Q, const void *K, const void *V, const void 
     }
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, dA0, dB0, N, T, L, eps,
                            logit_scale, workspace, s, BWD_FULL, saved, H));
-    return ok();
+    return fast_status(workspace, s, "backward");
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_QKV, N, T, S, D).total));
   if (dtype == RACE_F32)
@@ -1015,7 +1095,7 @@ int race_state_from_prefill(const void *K, const void *V, int dtype, const float
     CUtensorMap mK, mV;
     RACE_TRY(fast_totals_and_scan(K, V, planes_T, A0, B0, A_out, B_out, N, T, L, 0.f, logit_scale, workspace, s, a,
                                   mK, mV));
-    return ok();
+    return fast_status(workspace, s, "state from prefill");
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_STATE, N, T, S, D).total));
   if (dtype == RACE_F32)
@@ -1056,7 +1136,7 @@ int race_fwd_finish(const void *Q, const void *K, const void *V, int dtype, cons
       return fail(RACE_ERR_WORKSPACE, "saved-state buffer too small");
     RACE_TRY(fast_forward(Q, K, V, planes_T, out, A0, B0, nullptr, nullptr, N, T, L, eps, logit_scale, workspace,
                           as_stream(stream), saved_bytes ? saved : nullptr, true));
-    return ok();
+    return fast_status(workspace, as_stream(stream), "forward finish");
   }
   if (saved_bytes) return fail(RACE_ERR_UNSUPPORTED, "saved chunk states need the tcgen05 path");
   return race_fwd_qkv(Q, K, V, dtype, planes_T, out, A0, B0, nullptr, nullptr, N, T, D, L, P, eps, logit_scale,
@@ -1087,7 +1167,7 @@ int race_bwd_local(const void *Q, const void *K, const void *V, const void *dO, 
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, nullptr, nullptr, nullptr, A0, B0, nullptr, nullptr, gA_tot,
                            gB_tot, N, T, L, eps, logit_scale, workspace, s, BWD_LOCAL,
                            saved_bytes ? saved : nullptr));
-    return ok();
+    return fast_status(workspace, s, "backward local");
   }
   RACE_TRY(check_ws(workspace, workspace_bytes, generic_layout(RACE_OP_BWD_TOTALS, N, T, S, D).total));
   if (dtype == RACE_F32)
@@ -1123,7 +1203,7 @@ int race_bwd_finish(const void *Q, const void *K, const void *V, const void *dO,
     RACE_TRY(check_fast_ptrs({K, V, dQ, dK, dV}));
     RACE_TRY(fast_backward(Q, K, V, dO, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, nullptr, nullptr, N, T, L, eps,
                            logit_scale, workspace, s, BWD_FINISH, saved_bytes ? saved : nullptr));
-    return ok();
+    return fast_status(workspace, s, "backward finish");
   }
   // generic path: the whole backward again, with the later shards' suffix
   return race_bwd_qkv(Q, K, V, dO, dtype, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, nullptr, nullptr, N, T, D, L,

@@ -17,7 +17,8 @@
 //    is looked up once per device with cudaGetSymbolAddress (with that device
 //    current) and passed to the kernels as an ordinary pointer.  The first
 //    call on a device performs that lookup, so make the first call outside any
-//    stream capture.
+//    stream capture (a lookup that failed is not remembered: the next call
+//    on that device tries again).
 //  * Every call reuses the same bytes and they keep the previous call's
 //    contents.  Nothing here relies on them being zero: the chunk-totals
 //    kernel writes every record the scan and readout later read.
@@ -43,12 +44,11 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[RACE_NOALLOC_SC
 
 constexpr int kMaxDevices = 128;
 
-struct DeviceScratch {
-  std::once_flag once;
-  void *ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
-DeviceScratch g_dev[kMaxDevices];
+// Address of the array on each device, looked up on first use.  Only a
+// successful lookup is kept: a lookup that failed (for example one attempted
+// during a stream capture) is retried by the next call.
+std::mutex g_dev_mu;
+void *g_dev_ptr[kMaxDevices] = {};
 
 int err(int code, const char *fmt, long long a = 0, long long b = 0) {
   char buf[256];
@@ -61,11 +61,17 @@ int scratch_for_current_device(void **out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return err(RACE_ERR_CUDA, "cudaGetDevice failed (%lld)", (long long)e);
   if (dev < 0 || dev >= kMaxDevices) return err(RACE_ERR_UNSUPPORTED, "device ordinal %lld >= %lld", dev, kMaxDevices);
-  DeviceScratch &d = g_dev[dev];
-  std::call_once(d.once, [&d]() { d.err = cudaGetSymbolAddress(&d.ptr, g_noalloc_scratch); });
-  if (d.err != cudaSuccess || d.ptr == nullptr)
-    return err(RACE_ERR_CUDA, "cudaGetSymbolAddress of the scratch array failed (%lld)", (long long)d.err);
-  *out = d.ptr;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (g_dev_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();  // the next call on this device tries again
+      return err(RACE_ERR_CUDA, "cudaGetSymbolAddress of the scratch array failed (%lld)", (long long)e);
+    }
+    g_dev_ptr[dev] = p;
+  }
+  *out = g_dev_ptr[dev];
   return RACE_OK;
 }
 

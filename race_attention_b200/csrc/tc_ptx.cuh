@@ -45,10 +45,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and raises *abort) after `limit` polls, or as
-// soon as another thread has raised *abort.  Never spins forever.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                          uint32_t limit = (1u << 26)) {
+// Default poll limit of a bounded wait (about a second on a B200); a launch
+// may carry another one (race_set_wait_limit).
+constexpr uint32_t kDefaultWaitPolls = 1u << 26;
+
+// Bounded wait: returns false (and raises the abort flag) after abort[1]
+// polls, or as soon as another thread has raised the flag.  `abort` points at
+// the CTA's wait-control pair in shared memory, {abort flag, poll limit},
+// which the kernel initialises from its launch arguments before any wait.
+// Never spins forever.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  const uint32_t limit = (uint32_t)abort[1];
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023) == 1023 && *abort) return false;

@@ -10,7 +10,6 @@ from __future__ import annotations
 
 import ctypes
 import math
-import os
 
 import torch
 
@@ -86,16 +85,6 @@ def fast_path(dtype, D, L, P) -> bool:
     """Whether the library runs the tcgen05 kernels for this configuration
     (same rule as csrc/fast_host.cuh: bf16, D=64, P=4, L in {8,16})."""
     return dtype == torch.bfloat16 and D == 64 and P == 4 and L in (8, 16)
-
-
-def _check_status(ws, what):
-    """With RACE_B200_CHECK=1, read the device status word the tcgen05 kernels
-    keep at the head of their workspace (non-zero = a bounded wait expired).
-    Call only for tcgen05-path launches."""
-    if os.environ.get("RACE_B200_CHECK") == "1" and ws.numel() >= 4:
-        st = int(ws[:4].view(torch.int32).item())
-        if st != 0:
-            raise RuntimeError(f"{what}: device status {st} (a bounded device-side wait expired)")
 
 
 def default_logit_scale(D: int) -> float:
@@ -242,8 +231,6 @@ def fwd_qkv(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0=Non
         _lib.check(lib.race_fwd_qkv_save(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out),
                                          _ptr(A0), _ptr(B0), _ptr(Af), _ptr(Bf), _ptr(saved), sb, N, T, D, L, P,
                                          float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_fwd_qkv")
-        if fast_path(Q.dtype, D, L, P):
-            _check_status(ws, "race_fwd_qkv")
     res = (out, Af, Bf) if return_state else (out,)
     if save:
         res = res + (saved,)
@@ -269,8 +256,6 @@ def bwd_qkv(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, B0
                                           _ptr(saved), sb, _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(A0), _ptr(B0),
                                           _ptr(gA), _ptr(gB), _ptr(dA0), _ptr(dB0), N, T, D, L, P, float(eps), scale,
                                           _ptr(ws), nb, _stream(dev)), "race_bwd_qkv")
-        if fast_path(Q.dtype, D, L, P):
-            _check_status(ws, "race_bwd_qkv")
     return (dQ, dK, dV, dA0, dB0) if return_state_grad else (dQ, dK, dV)
 
 
@@ -303,7 +288,6 @@ def fwd_bthd(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None):
         _lib.check(lib.race_fwd_bthd(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out), _ptr(saved),
                                      sb, Bn, T, H, D, L, P, float(eps), scale, _ptr(ws), nb, _stream(dev)),
                    "race_fwd_bthd")
-        _check_status(ws, "race_fwd_bthd")
     return out, saved
 
 
@@ -319,7 +303,6 @@ def bwd_bthd(Q, K, V, dO, planes_T, L, P, saved, eps=1e-6, logit_scale=None):
         _lib.check(lib.race_bwd_bthd(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T), _ptr(saved),
                                      saved.numel(), _ptr(dQ), _ptr(dK), _ptr(dV), Bn, T, H, D, L, P, float(eps), scale,
                                      _ptr(ws), nb, _stream(dev)), "race_bwd_bthd")
-        _check_status(ws, "race_bwd_bthd")
     return dQ, dK, dV
 
 
@@ -335,8 +318,6 @@ def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None)
         _lib.check(lib.race_state_from_prefill(_ptr(K), _ptr(V), _dtype_code(K), _ptr(planes_T), _ptr(A0), _ptr(B0),
                                                _ptr(A), _ptr(B), N, T, D, L, P, scale, _ptr(ws), nb, _stream(dev)),
                    "race_state_from_prefill")
-        if fast_path(K.dtype, D, L, P):
-            _check_status(ws, "race_state_from_prefill")
     return A, B
 
 
@@ -358,8 +339,6 @@ def fwd_local(K, V, planes_T, L, P, logit_scale=None):
         ws, nb = _workspace(_lib.OP_FWD_SPLIT, N, T, S, D, L, P, _dtype_code(K), dev)
         _lib.check(lib.race_fwd_local(_ptr(K), _ptr(V), _dtype_code(K), _ptr(planes_T), _ptr(A), _ptr(B), N, T, D,
                                       L, P, scale, _ptr(ws), nb, _stream(dev)), "race_fwd_local")
-        if fast_path(K.dtype, D, L, P):
-            _check_status(ws, "race_fwd_local")
     return A, B, FwdSplit(K=K, V=V, planes_T=planes_T, L=L, P=P, scale=scale, ws=ws, nb=nb, dev=dev)
 
 
@@ -378,8 +357,6 @@ def fwd_finish(h, Q, A0=None, B0=None, eps=1e-6, save=False):
         _lib.check(lib.race_fwd_finish(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out),
                                        _ptr(saved), sb, _ptr(A0), _ptr(B0), N, T, D, h.L, h.P, float(eps), h.scale,
                                        _ptr(h.ws), h.nb, _stream(dev)), "race_fwd_finish")
-        if fast_path(Q.dtype, D, h.L, h.P):
-            _check_status(h.ws, "race_fwd_finish")
     return (out, saved) if save else out
 
 
@@ -405,8 +382,6 @@ def bwd_local(Q, K, V, dO, planes_T, L, P, eps=1e-6, logit_scale=None, A0=None, 
         _lib.check(lib.race_bwd_local(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T),
                                       _ptr(saved), sb, _ptr(A0), _ptr(B0), _ptr(gA), _ptr(gB), N, T, D, L, P,
                                       float(eps), scale, _ptr(ws), nb, _stream(dev)), "race_bwd_local")
-        if fast_path(Q.dtype, D, L, P):
-            _check_status(ws, "race_bwd_local")
     h = BwdSplit(Q=Q, K=K, V=V, dO=dO, planes_T=planes_T, L=L, P=P, eps=eps, scale=scale, A0=A0, B0=B0,
                  saved=saved, ws=ws, nb=nb, dev=dev)
     return gA, gB, h
@@ -425,8 +400,6 @@ def bwd_finish(h, gA=None, gB=None):
                                        _ptr(h.planes_T), _ptr(h.saved), sb, _ptr(h.A0), _ptr(h.B0), _ptr(gA),
                                        _ptr(gB), _ptr(dQ), _ptr(dK), _ptr(dV), N, T, D, h.L, h.P, float(h.eps),
                                        h.scale, _ptr(h.ws), h.nb, _stream(h.dev)), "race_bwd_finish")
-        if fast_path(h.Q.dtype, D, h.L, h.P):
-            _check_status(h.ws, "race_bwd_finish")
     return dQ, dK, dV
 
 

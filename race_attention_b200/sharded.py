@@ -13,10 +13,14 @@ backward  A. the slice's gradients with a zero suffix at its end, and their
           -> all_gather -> suffix = sum of ranks > r
           B. that suffix's (linear) share added to the gradients
 
-The exchange is one all_gather of N*(S + S*D) float32 per rank and direction
-(266 KB at N=8, S=128, D=64).  The compute backend defaults to the CUDA
-library; anything with the same four methods can stand in (the CPU tests use
-this to run the exchange logic on gloo ranks).
+The exchange is one all_gather_into_tensor of N*(S + S*D) float32 per rank and
+direction (266 KB at N=8, S=128, D=64) into one [W, ...] buffer, then one
+fixed-order float64 reduction over the earlier (or later) ranks.  Every message
+carries a checksum of its exact bits (an integer sum and a position-weighted
+integer sum of the float32 words, order independent and exact); a receiver that
+finds a mismatch raises instead of using the corrupted state.  The compute
+backend defaults to the CUDA library; anything with the same four methods can
+stand in (the CPU tests use this to run the exchange logic on gloo ranks).
 """
 from __future__ import annotations
 
@@ -24,6 +28,15 @@ import torch
 import torch.distributed as dist
 
 from . import ops
+
+try:
+    from torch.cuda import nvtx as _nvtx
+except ImportError:  # pragma: no cover
+    _nvtx = None
+
+# Test hook (CPU tests only): called with the outgoing message after its checksum
+# is computed, to stand for a transport that corrupts it.
+_tamper_outgoing = None
 
 
 class CudaShardBackend:
@@ -43,28 +56,57 @@ class CudaShardBackend:
         return ops.bwd_finish(handle, gA, gB)
 
 
-def _pack(A, B):
-    return torch.cat([A.reshape(A.shape[0], -1), B.reshape(B.shape[0], -1)], 1).float().contiguous()
+_CS_WORDS = 4  # two int64 checksums as float32 words
 
 
-def _unpack(buf, N, S, D):
-    return buf[:, :S].contiguous(), buf[:, S:].reshape(N, S, D).contiguous()
+def _checksums(words):
+    """[..., n] float32 -> [..., 2] int64: sum of the bit patterns and a
+    position-weighted sum (weights 1..65521), both exact in wrapping int64."""
+    bits = words.view(torch.int32).to(torch.int64)
+    w = torch.arange(bits.shape[-1], device=bits.device, dtype=torch.int64) % 65521 + 1
+    return torch.stack([bits.sum(-1), (bits * w).sum(-1)], -1)
+
+
+class ExchangeCorrupted(RuntimeError):
+    """A rank's exchanged state did not match its checksum."""
+
+
+def _message(A, B):
+    """This rank's message: (A, B) flattened to float32, then its checksum words."""
+    body = torch.cat([A.reshape(-1), B.reshape(-1)]).float()
+    return torch.cat([body, _checksums(body).view(torch.float32)]).contiguous()
 
 
 def exchange(A, B, group=None, direction="prefix"):
-    """Sum of the (A, B) totals of ranks before ('prefix') or after ('suffix') this one."""
+    """Sum of the (A, B) totals of ranks before ('prefix') or after ('suffix') this one,
+    in float64 and a fixed rank order (deterministic); every rank's message is
+    checked against its checksum."""
     W = dist.get_world_size(group)
     r = dist.get_rank(group)
     N, S = A.shape
     D = B.shape[-1]
-    buf = _pack(A, B)
-    parts = [torch.empty_like(buf) for _ in range(W)]
-    dist.all_gather(parts, buf, group=group)
-    idx = range(0, r) if direction == "prefix" else range(r + 1, W)
-    acc = torch.zeros(buf.shape, dtype=torch.float64, device=buf.device)
-    for i in idx:
-        acc += parts[i].double()
-    return _unpack(acc.float(), N, S, D)
+    if _nvtx is not None and A.is_cuda:
+        _nvtx.range_push(f"race exchange ({direction})")
+    try:
+        msg = _message(A, B)
+        if _tamper_outgoing is not None:
+            msg = _tamper_outgoing(msg)
+        flat = torch.empty(W * msg.numel(), dtype=msg.dtype, device=msg.device)
+        dist.all_gather_into_tensor(flat, msg, group=group)
+        allm = flat.view(W, msg.numel())
+        body, cs = allm[:, :-_CS_WORDS], allm[:, -_CS_WORDS:].contiguous().view(torch.int64)
+        bad = (_checksums(body) != cs).any(-1)
+        if bool(bad.any()):
+            raise ExchangeCorrupted(
+                f"rank {r}: exchanged state of rank(s) {bad.nonzero().flatten().tolist()} fails its checksum")
+        part = body[:r] if direction == "prefix" else body[r + 1:]
+        acc = part.double().sum(0) if part.shape[0] else torch.zeros(body.shape[1], dtype=torch.float64,
+                                                                       device=body.device)
+        acc = acc.float()
+        return acc[:N * S].reshape(N, S).contiguous(), acc[N * S:].reshape(N, S, D).contiguous()
+    finally:
+        if _nvtx is not None and A.is_cuda:
+            _nvtx.range_pop()
 
 
 class ShardedRaceFn(torch.autograd.Function):

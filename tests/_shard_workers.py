@@ -87,3 +87,37 @@ def dropped_rank_worker(rank, world, port, outdir, _):
     with open(os.path.join(outdir, "rank0.status"), "w") as f:
         f.write(f"{status} {time.time() - t0:.1f}")
     os._exit(0)
+
+
+def delayed_rank_worker(rank, world, port, outdir, delay_s):
+    """The last rank starts its step `delay_s` late (well inside the process-group
+    timeout); every rank must still finish with the exact result."""
+    if rank == world - 1:
+        time.sleep(delay_s)
+    sharded_worker(rank, world, port, outdir, "oracle")
+
+
+def corrupted_message_worker(rank, world, port, outdir, _):
+    """Rank 1's outgoing forward message has one bit flipped after its checksum was
+    taken (a corrupting transport); every rank must refuse the exchanged state."""
+    import race_attention_b200.sharded as sh
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    if rank == 1:
+        def flip(msg):
+            bad = msg.clone()
+            bad.view(torch.int32)[3] ^= 1 << 20
+            return bad
+        sh._tamper_outgoing = flip
+    Q, K, V, dO, planes = make_problem()
+    status = "no-error"
+    try:
+        sh.race_causal_sharded(Q[:, :24], K[:, :24], V[:, :24], planes, 2, 3, 1e-6, None, None,
+                               OracleShardBackend())
+    except sh.ExchangeCorrupted as e:
+        status = f"corrupted:{e}"
+    except Exception as e:  # any other failure is a test failure
+        status = f"other:{type(e).__name__}:{e}"
+    with open(os.path.join(outdir, f"rank{rank}.status"), "w") as f:
+        f.write(status)
+    dist.destroy_process_group()

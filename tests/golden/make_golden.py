@@ -2,7 +2,7 @@
 
 Run once where the reference tree exists (it never exists on a GPU box):
 
-    CXX=/usr/bin/g++ python tests/golden/make_golden.py [--ref <path of the reference checkout>]
+    CXX=/usr/bin/g++ python tests/golden/make_golden.py --ref <path of the reference checkout>
 
 It imports the reference's own modules from ``<ref>/scaling``:
   * build_planes_protos / soft_hash_probs / race_prefix_ref (race_common.py)
@@ -24,9 +24,12 @@ import numpy as np
 import torch
 
 ap = argparse.ArgumentParser()
-ap.add_argument("--ref", default=os.environ.get("RACE_REF_ROOT", "/root/reference"))
+ap.add_argument("--ref", default=os.environ.get("RACE_REF_ROOT"),
+                help="path of the reference checkout (or set RACE_REF_ROOT)")
 ap.add_argument("--out", default=os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.npz"))
 args = ap.parse_args()
+if not args.ref:
+    ap.error("give --ref <path of the reference checkout> or set RACE_REF_ROOT")
 
 os.environ.setdefault("TORCH_EXTENSIONS_DIR", tempfile.mkdtemp(prefix="race_golden_ext_"))
 sys.path.insert(0, os.path.join(args.ref, "scaling"))

@@ -2,7 +2,7 @@
 
 Run once where the reference tree exists (it never exists on a GPU box):
 
-    python tests/golden/make_golden_ace.py [--ref <path of the reference checkout>]
+    python tests/golden/make_golden_ace.py --ref <path of the reference checkout>
 
 It imports ``BatchedACE`` from ``<ref>/scaling/benchmark_time.py`` (shared planes; the
 module's plotting import is replaced by an empty stand-in, it is not used), runs it in
@@ -19,9 +19,12 @@ import numpy as np
 import torch
 
 ap = argparse.ArgumentParser()
-ap.add_argument("--ref", default=os.environ.get("RACE_REF_ROOT", "/root/reference"))
+ap.add_argument("--ref", default=os.environ.get("RACE_REF_ROOT"),
+                help="path of the reference checkout (or set RACE_REF_ROOT)")
 ap.add_argument("--out", default=os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_ace.npz"))
 args = ap.parse_args()
+if not args.ref:
+    ap.error("give --ref <path of the reference checkout> or set RACE_REF_ROOT")
 
 mpl = types.ModuleType("matplotlib")
 mpl.pyplot = types.ModuleType("matplotlib.pyplot")

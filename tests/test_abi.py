@@ -165,14 +165,15 @@ def test_ops_refuse_host_tensors():
 
 def test_segment_plan_stays_within_the_workspace():
     """The tcgen05 path's segment planner never picks more segments than the workspace
-    (sized for 256 SMs) holds, covers every chunk with no empty segment, and at the
-    config-2 geometry on 148 SMs picks 23 segments (4.97 waves instead of 3.89)."""
+    (sized for 256 SMs) holds -- also for devices with more SMs than that -- covers every
+    chunk with no empty segment, and at the config-2 geometry on 148 SMs picks 23
+    segments (4.97 waves instead of 3.89)."""
     lib = _lib.load()
     nseg, sc, mx = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     for N in (1, 2, 3, 8, 32, 96, 200, 1024, 5000):
         for T in (1, 127, 128, 129, 4096, 32768, 1 << 20, 12582912):
             for S in (128, 256):
-                for sms in (1, 80, 132, 148, 160, 256):
+                for sms in (1, 80, 132, 148, 160, 256, 320, 1024):
                     rc = lib.race_plan_segments(N, T, S, sms, ctypes.byref(nseg), ctypes.byref(sc), ctypes.byref(mx))
                     assert rc == 0
                     nch = (T + 127) // 128
@@ -183,3 +184,16 @@ def test_segment_plan_stays_within_the_workspace():
     codes = status_codes()
     assert lib.race_plan_segments(32, 1 << 20, 256, 0, ctypes.byref(nseg), ctypes.byref(sc),
                                   ctypes.byref(mx)) == codes["RACE_ERR_ARG"]
+
+
+def test_wait_controls_validate_on_the_host():
+    """The bounded-wait controls are host-only settings; reading a status word needs a
+    workspace pointer and somewhere to put the word (checked before any CUDA call)."""
+    lib = _lib.load()
+    codes = status_codes()
+    assert lib.race_set_wait_limit(1 << 20) == 0
+    assert lib.race_set_wait_limit(0) == 0
+    assert lib.race_test_withhold_first_load(0) == 0
+    st = ctypes.c_int(0)
+    assert lib.race_read_status(None, None, ctypes.byref(st)) == codes["RACE_ERR_ARG"]
+    assert lib.race_read_status(ctypes.c_void_p(256), None, None) == codes["RACE_ERR_ARG"]

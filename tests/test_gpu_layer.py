@@ -151,7 +151,8 @@ def test_fast_forward_segments(B, H, T, L):
     assert lib.race_launch_counter() - n0 == 3
     ref, Ar, Br = O.race_qkv_fwd(Q, K, V, planes, L, 4)
     assert relerr(out, ref) < 2e-2
-    assert relerr(Af, Ar) < 1e-2
+    # A: sums of fp32 accumulations of the (bf16) probabilities
+    assert relerr(Af, Ar) < 1e-3
     assert relerr(Bf, Br) < 2e-2
 
 

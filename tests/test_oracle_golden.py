@@ -119,3 +119,34 @@ def test_oracle_noncausal_matches_reference_module():
         assert O.relerr(dQ, _ace_streams(G[f"c{i}_dQ"])) < 1e-9
         assert O.relerr(dK, _ace_streams(G[f"c{i}_dK"])) < 1e-9
         assert O.relerr(dV, _ace_streams(G[f"c{i}_dV"])) < 1e-10
+
+
+def test_build_planes_protos_bit_identical_to_reference(golden):
+    """race_attention_b200.build_planes_protos makes the reference's seeded CPU-generator
+    calls (scaling/race_common.py:14-33): planes_T and protos_T are bit-identical to the
+    reference's for every golden geometry, including the config-2 geometry (64, 4, 16),
+    per-member planes (share_planes=False) and non-zero seeds."""
+    import race_attention_b200 as rb
+    cases = golden["planes_cases"]
+    assert len(cases) == 7
+    for i, (d, kb, L, M, share, seed) in enumerate(cases):
+        pT, prT = rb.build_planes_protos(int(d), int(kb), int(L), int(M), device="cpu",
+                                         share_planes=bool(share), seed=int(seed))
+        want_p, want_c = golden[f"planes{i}_planes_T"], golden[f"planes{i}_protos_T"]
+        assert pT.dtype == torch.float32 and tuple(pT.shape) == want_p.shape, i
+        assert np.array_equal(pT.numpy(), want_p), i
+        assert np.array_equal(prT.numpy(), want_c), i
+
+
+def test_long_sequence_oracle_matches_the_serial_oracle():
+    """oracle.layer_long (multithreaded, one stream at a time, float storage of its
+    [T,S] intermediates) agrees with the serial fp64 oracle it restates."""
+    import race_attention_b200 as rb
+    g = torch.Generator().manual_seed(0)
+    for N, T, L, D in ((2, 300, 8, 64), (1, 129, 16, 64), (3, 50, 4, 32)):
+        Q, K, V, dO = (torch.randn(N, T, D, generator=g) * 0.3 for _ in range(4))
+        planes, _ = rb.build_planes_protos(D, 4, L, 1, device="cpu", seed=1)
+        want = list(O.race_qkv_fwd(Q, K, V, planes, L, 4)) + list(O.race_qkv_bwd(Q, K, V, dO, planes, L, 4)[:3])
+        got = O.layer_long(Q, K, V, planes, L, 4, dO=dO)
+        for a, b in zip(got, want):
+            assert relerr(a, b) < 1e-6
