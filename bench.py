@@ -320,13 +320,26 @@ def run_noncausal(args):
         e.record()
         torch.cuda.synchronize()
     ms = s.elapsed_time(e) / args.steps
+    launches = int(lib.race_launch_counter() - n0)
+    # per-kernel device times in separate steps (the event pairs would sit inside the timed ones)
+    lib.race_kernel_timing(1)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    kernels = kernel_times(lib, args.steps)
+    lib.race_kernel_timing(0)
+    hbm, _, src = _peaks()
+    layer_bytes = 11 * D * 2 * B * H * T  # read Q, K, V, dO; write out, dQ, dK, dV (bf16)
     line = {"metric": "non-causal RACE layer fwd+bwd tokens/s", "value": B * T / (ms / 1e3), "unit": "tokens/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded randn / 8)",
             "config": {"workload": "non-causal RACE (BatchedACE, shared planes) fwd+bwd", "batch": B, "heads": H,
                        "seq_len": T, "head_dim": D, "tables_L": L, "planes_P": P},
-            "gpu_launches": int(lib.race_launch_counter() - n0),
-            "gpu_launches_per_step": int(lib.race_launch_counter() - n0) // args.steps, "clocks": clk.summary()}
+            "roofline": {"bound": "hbm", "unit": "GB/s", "peak": hbm, "peak_source": src,
+                         "step_achieved": layer_bytes / (ms / 1e3) / 1e9,
+                         "step_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm},
+            "kernels": kernels,
+            "gpu_launches": launches, "gpu_launches_per_step": launches // args.steps, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
     return 0
 

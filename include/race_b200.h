@@ -56,6 +56,8 @@ extern "C" {
 #define RACE_OP_STATE 4
 #define RACE_OP_BWD_SPLIT 5  /* race_bwd_local + race_bwd_finish (one workspace) */
 #define RACE_OP_FWD_SPLIT 6  /* race_fwd_local + race_fwd_finish (one workspace) */
+#define RACE_OP_ACE_FWD 7    /* race_ace_fwd (non-causal)                      */
+#define RACE_OP_ACE_BWD 8    /* race_ace_bwd (non-causal)                      */
 
 /* Library ABI version (bumped on any signature change). */
 int race_abi_version(void);
@@ -79,7 +81,8 @@ unsigned long long race_launch_counter(void);
 #define RACE_KT_BWD_REV 2      /* backward reverse walk (segment-local grads)  */
 #define RACE_KT_SCAN 3         /* segment prefix / suffix scans                */
 #define RACE_KT_BWD_FIX 4      /* backward suffix fix-up (dK, dV, dQ)          */
-#define RACE_KT_COUNT 5
+#define RACE_KT_ACE_TILE 5     /* non-causal per-token tile kernel             */
+#define RACE_KT_COUNT 6
 int race_kernel_timing(int enable);
 int race_kernel_time(int kernel, double *total_ms, long long *launches);
 /* (The timing state is process-wide: one event list per kernel id, shared by
@@ -336,6 +339,28 @@ int race_bwd_finish(const void *Q, const void *K, const void *V, const void *dO,
 int race_fwd_probs_noalloc(const float *probsK, const float *probsQ, const float *V2,
                            float *out, int64_t N, int64_t T, int64_t S, int64_t D,
                            float eps, void *stream);
+
+/* ---- non-causal RACE (BatchedACE with shared planes) --------------------------
+ * Replaces the per-token products of the reference's non-causal module
+ * (scaling/benchmark_time.py:129-161, misc/classification.py:282-308; its
+ * autograd backward): every query reads the whole sequence's bucket summary,
+ *   A = sum_t pk_t,  b = sum_t pk_t^T V_t,  out_t = pq_t (b / (A + eps)).
+ * bf16 with D = 64, P = 4, L in {8, 16} (tcgen05 kernels; other configurations
+ * return RACE_ERR_UNSUPPORTED).  No [N, T, S] tensor is formed.
+ * race_ace_fwd writes out [N,T,64] and the summaries A [N,S], B (= b) [N,S,64]
+ * fp32, which race_ace_bwd takes back to give dQ, dK, dV.  Workspace:
+ * race_workspace_bytes(RACE_OP_ACE_FWD / RACE_OP_ACE_BWD, ...). */
+int race_ace_fwd(const void *Q, const void *K, const void *V, int dtype,
+                 const float *planes_T, void *out, float *A, float *B,
+                 int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                 float eps, float logit_scale,
+                 void *workspace, size_t workspace_bytes, void *stream);
+int race_ace_bwd(const void *Q, const void *K, const void *V, const void *dO, int dtype,
+                 const float *planes_T, const float *A, const float *B,
+                 void *dQ, void *dK, void *dV,
+                 int64_t N, int64_t T, int64_t D, int64_t L, int64_t P,
+                 float eps, float logit_scale,
+                 void *workspace, size_t workspace_bytes, void *stream);
 
 #ifdef __cplusplus
 }

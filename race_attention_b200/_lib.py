@@ -18,9 +18,11 @@ _lib = None
 RACE_OK = 0
 RACE_F32 = 0
 RACE_BF16 = 1
-OP_FWD_PROBS, OP_BWD_PROBS, OP_FWD_QKV, OP_BWD_QKV, OP_STATE, OP_BWD_SPLIT, OP_FWD_SPLIT = range(7)
+OP_FWD_PROBS, OP_BWD_PROBS, OP_FWD_QKV, OP_BWD_QKV, OP_STATE, OP_BWD_SPLIT, OP_FWD_SPLIT, OP_ACE_FWD, OP_ACE_BWD = \
+    range(9)
 # kernel ids of race_kernel_time (include/race_b200.h RACE_KT_*)
-KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_rev_kernel", "chunk_scan", "bwd_fix_kernel")
+KERNEL_NAMES = ("fwd_totals_kernel", "fwd_readout_kernel", "bwd_rev_kernel", "chunk_scan", "bwd_fix_kernel",
+                "ace_tile_kernel")
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -60,6 +62,9 @@ SIGNATURES = {
     "race_fwd_finish": [_P, _P, _P, _I, _P, _P, _P, _SZ, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ,
                         _P],
     "race_fwd_probs_noalloc": [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _F, _P],
+    "race_ace_fwd": [_P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ, _P],
+    "race_ace_bwd": [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F, _P, _SZ,
+                     _P],
     "race_bwd_local": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _F,
                        _P, _SZ, _P],
     "race_bwd_finish": [_P, _P, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,

@@ -25,6 +25,7 @@
 #include "decode.cuh"
 #include "fast_host.cuh"
 #include "generic.cuh"
+#include "noncausal.cuh"
 
 using race::align_up;
 namespace gen = race::gen;
@@ -94,7 +95,8 @@ class NvtxRange {
 
 const char *kernel_range_name(int id) {
   static const char *names[RACE_KT_COUNT] = {"race fwd_totals_kernel", "race fwd_readout_kernel",
-                                             "race bwd_rev_kernel", "race chunk_scan", "race bwd_fix_kernel"};
+                                             "race bwd_rev_kernel", "race chunk_scan", "race bwd_fix_kernel",
+                                             "race ace_tile_kernel"};
   return id >= 0 && id < RACE_KT_COUNT ? names[id] : "race kernel";
 }
 
@@ -680,6 +682,69 @@ int fast_status(const void *ws, cudaStream_t s, const char *what) {
   return ok();
 }
 
+// Non-causal RACE: the per-token tile kernel (noncausal.cuh) in one of its modes.  X, Y: the
+// input activations (Y unused by ACE_OUT); O1, O2: the outputs (O2 only for ACE_KV); totA /
+// totB: the (K, V) totals A, b; totG: the (Q, dO) totals dE (ACE_KV).
+int ace_tiles(int mode, const void *X, const void *Y, void *O1, void *O2, const float *planes_T, const float *totA,
+              const float *totB, const float *totG, int64_t N, int64_t T, int64_t L, float eps, float scale, void *ws,
+              cudaStream_t s) {
+  const int64_t S = 16 * L;
+  if (!fh::bind_current_context()) return fail(RACE_ERR_CUDA, "no current CUDA device/context on this thread");
+  const fh::Plan pl = fh::plan(N, T, S, fh::sm_count());
+  fk::AceArgs a;
+  a.N = (int)N;
+  a.T = (int)T;
+  a.L = (int)L;
+  a.LP = (int)(4 * L);
+  a.S = (int)S;
+  a.H = 1;
+  a.nseg = pl.nseg;
+  a.seg_chunks = pl.seg_chunks;
+  a.nchunks = pl.nchunks;
+  a.eps = eps;
+  a.scale = scale;
+  a.poly = 2.f * std::fabs(scale) <= 0.5f ? 1 : 0;
+  a.planes = planes_T;
+  a.totA = totA;
+  a.totB = totB;
+  a.totG = totG;
+  a.err = at<int>(ws, 0);
+  a.wait_limit = wait_limit();
+  CUtensorMap mX, mY, mO1, mO2;
+  if (!fh::make_act_map(&mX, X, N, T, 1) || !fh::make_act_map(&mO1, O1, N, T, 1) ||
+      (Y && !fh::make_act_map(&mY, Y, N, T, 1)) || (O2 && !fh::make_act_map(&mO2, O2, N, T, 1)))
+    return fail(RACE_ERR_CUDA, "cuTensorMapEncodeTiled failed in the non-causal kernel: CUresult %d",
+                fh::last_encode_status());
+  if (!Y) mY = mX;    // unused by the kernel
+  if (!O2) mO2 = mO1;  // unused by the kernel
+  const fk::AceSmem sp = fk::ace_smem_plan(a.LP, a.S);
+  const unsigned grid = (unsigned)(N * pl.nseg);
+  KernelScope ks(RACE_KT_ACE_TILE, s);
+  switch (mode) {
+    case fk::ACE_OUT:
+      RACE_TRY(set_smem(fk::ace_tile_kernel<fk::ACE_OUT>, sp.total));
+      fk::ace_tile_kernel<fk::ACE_OUT><<<grid, fk::NTHR, sp.total, s>>>(mX, mY, mO1, mO2, a);
+      break;
+    case fk::ACE_KV:
+      RACE_TRY(set_smem(fk::ace_tile_kernel<fk::ACE_KV>, sp.total));
+      fk::ace_tile_kernel<fk::ACE_KV><<<grid, fk::NTHR, sp.total, s>>>(mX, mY, mO1, mO2, a);
+      break;
+    default:
+      RACE_TRY(set_smem(fk::ace_tile_kernel<fk::ACE_Q>, sp.total));
+      fk::ace_tile_kernel<fk::ACE_Q><<<grid, fk::NTHR, sp.total, s>>>(mX, mY, mO1, mO2, a);
+      break;
+  }
+  ks.stop();
+  return check_launch("ace_tile_kernel");
+}
+
+// Workspace of the non-causal backward: the totals kernel's status word and segment records,
+// then the (Q, dO) totals dE [N, S, 64] fp32.
+size_t ace_bwd_dE_offset(int64_t N, int64_t T, int64_t S) { return fh::fwd_workspace_bytes(N, T, S); }
+size_t ace_bwd_workspace_bytes(int64_t N, int64_t T, int64_t S) {
+  return ace_bwd_dE_offset(N, T, S) + align_up(sizeof(float) * (size_t)N * S * fk::HD, 256);
+}
+
 int check_fast_ptrs(std::initializer_list<const void *> ptrs) {
   for (const void *p : ptrs)
     if (p && !fh::aligned16(p)) return fail(RACE_ERR_ALIGN, "bf16 activations must be 16-byte aligned");
@@ -809,6 +874,15 @@ int race_workspace_bytes(int op, int64_t N, int64_t T, int64_t S, int64_t D, int
   (void)chunk;
   RACE_NONNULL(bytes);
   *bytes = 0;
+  if (op == RACE_OP_ACE_FWD || op == RACE_OP_ACE_BWD) {
+    RACE_TRY(check_dtype(dtype));
+    RACE_TRY(check_lp(L, P, &S));
+    RACE_TRY(check_nts(N, T, S, D));
+    if (!fh::eligible(dtype, D, L, P))
+      return fail(RACE_ERR_UNSUPPORTED, "non-causal kernels: bf16, D=64, P=4, L in {8,16} only");
+    *bytes = op == RACE_OP_ACE_FWD ? fh::fwd_workspace_bytes(N, T, S) : ace_bwd_workspace_bytes(N, T, S);
+    return ok();
+  }
   if (op == RACE_OP_FWD_QKV || op == RACE_OP_BWD_QKV || op == RACE_OP_STATE || op == RACE_OP_BWD_SPLIT ||
       op == RACE_OP_FWD_SPLIT) {
     RACE_TRY(check_dtype(dtype));
@@ -1208,6 +1282,72 @@ int race_bwd_finish(const void *Q, const void *K, const void *V, const void *dO,
   // generic path: the whole backward again, with the later shards' suffix
   return race_bwd_qkv(Q, K, V, dO, dtype, planes_T, dQ, dK, dV, A0, B0, gA_in, gB_in, nullptr, nullptr, N, T, D, L,
                       P, eps, logit_scale, workspace, workspace_bytes, stream);
+}
+
+int race_ace_fwd(const void *Q, const void *K, const void *V, int dtype, const float *planes_T, void *out, float *A,
+                 float *B, int64_t N, int64_t T, int64_t D, int64_t L, int64_t P, float eps, float logit_scale,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(out);
+  RACE_NONNULL(A);
+  RACE_NONNULL(B);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  if (!fh::eligible(dtype, D, L, P))
+    return fail(RACE_ERR_UNSUPPORTED, "non-causal kernels: bf16, D=64, P=4, L in {8,16} only");
+  RACE_TRY(check_ws(workspace, workspace_bytes, fh::fwd_workspace_bytes(N, T, S)));
+  RACE_TRY(check_fast_ptrs({Q, K, V, out}));
+  cudaStream_t s = as_stream(stream);
+  NvtxRange range("race non-causal forward");
+  fk::FwdArgs a;
+  CUtensorMap mK, mV;
+  // A = sum_t pk, b = sum_t pk^T V (the totals kernel and the segment scan's finals)
+  RACE_TRY(fast_totals_and_scan(K, V, planes_T, nullptr, nullptr, A, B, N, T, L, 0.f, logit_scale, workspace, s, a,
+                                mK, mV));
+  RACE_TRY(ace_tiles(fk::ACE_OUT, Q, nullptr, out, nullptr, planes_T, A, B, nullptr, N, T, L, eps, logit_scale,
+                     workspace, s));
+  return fast_status(workspace, s, "non-causal forward");
+}
+
+int race_ace_bwd(const void *Q, const void *K, const void *V, const void *dO, int dtype, const float *planes_T,
+                 const float *A, const float *B, void *dQ, void *dK, void *dV, int64_t N, int64_t T, int64_t D,
+                 int64_t L, int64_t P, float eps, float logit_scale, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+  RACE_NONNULL(Q);
+  RACE_NONNULL(K);
+  RACE_NONNULL(V);
+  RACE_NONNULL(dO);
+  RACE_NONNULL(planes_T);
+  RACE_NONNULL(A);
+  RACE_NONNULL(B);
+  RACE_NONNULL(dQ);
+  RACE_NONNULL(dK);
+  RACE_NONNULL(dV);
+  RACE_TRY(check_dtype(dtype));
+  int64_t S = 0;
+  RACE_TRY(check_lp(L, P, &S));
+  RACE_TRY(check_nts(N, T, S, D));
+  if (!fh::eligible(dtype, D, L, P))
+    return fail(RACE_ERR_UNSUPPORTED, "non-causal kernels: bf16, D=64, P=4, L in {8,16} only");
+  RACE_TRY(check_ws(workspace, workspace_bytes, ace_bwd_workspace_bytes(N, T, S)));
+  RACE_TRY(check_fast_ptrs({Q, K, V, dO, dQ, dK, dV}));
+  cudaStream_t s = as_stream(stream);
+  NvtxRange range("race non-causal backward");
+  float *dE = at<float>(workspace, ace_bwd_dE_offset(N, T, S));
+  fk::FwdArgs a;
+  CUtensorMap mQ, mO;
+  // dE = sum_t pq^T dO: the same totals kernel over (Q, dO)
+  RACE_TRY(fast_totals_and_scan(Q, dO, planes_T, nullptr, nullptr, nullptr, dE, N, T, L, 0.f, logit_scale, workspace,
+                                s, a, mQ, mO));
+  RACE_TRY(ace_tiles(fk::ACE_KV, K, V, dK, dV, planes_T, A, B, dE, N, T, L, eps, logit_scale, workspace, s));
+  RACE_TRY(ace_tiles(fk::ACE_Q, Q, dO, dQ, nullptr, planes_T, A, B, nullptr, N, T, L, eps, logit_scale, workspace,
+                     s));
+  return fast_status(workspace, s, "non-causal backward");
 }
 
 int race_decode_step(const void *q, const void *k, const void *v, int dtype, const float *planes_T, float *A,

@@ -7,11 +7,13 @@ Every query reads the whole sequence's bucket summaries:
 and the exact gradients
     dE = sum_t pq_t^T dO_t ; dpq_t = dO_t E^T ; db = dE / (A + eps) ;
     dA = -sum_d dE b / (A + eps)^2 ; dpk_t = dA + V_t db^T ; dV_t = pk_t db.
-The bucket sums (b, A) and dE are single reductions over tokens done by the library's
-state-from-prefill kernels (tcgen05 totals kernel for bf16, D = 64, P = 4, L in {8, 16}:
-b, A from (K, V); dE from (Q, dO)); the soft hash and its backward are the library's
-kernels; the per-token products with the [S, D] summaries are plain batched GEMMs.  Like the
-reference, the forward and backward hold [N, T, S] probability tensors.
+For bf16 with D = 64, P = 4, L in {8, 16} (the tcgen05 path) the whole layer is the
+library's race_ace_fwd / race_ace_bwd: the bucket sums (b, A; dE) are single reductions over
+tokens by the totals kernel, and every per-token product (out, dQ, dK, dV) is one fused
+tile kernel that hashes the token, multiplies by the [S, D] summary on the tensor cores and
+takes the soft-hash backward in its epilogue; no [N, T, S] tensor is formed.  Other
+configurations (fp32, other shapes) compose the library's soft-hash and totals kernels with
+batched GEMMs over [N, T, S] probabilities, as the reference module does.
 """
 from __future__ import annotations
 
@@ -32,6 +34,11 @@ class RaceNonCausalFn(Function):
         shape, dtype = Q.shape, Q.dtype
         Qn, Kn, Vn = _streams(Q), _streams(K), _streams(V)
         scale = ops.default_logit_scale(Qn.shape[-1]) if logit_scale is None else float(logit_scale)
+        if ops.fast_path(dtype, Qn.shape[-1], L, P):
+            out, A, b = ops.ace_fwd(Qn, Kn, Vn, planes_T, L, P, eps, scale)
+            ctx.save_for_backward(Qn, Kn, Vn, planes_T, A, b)
+            ctx.cfg = (L, P, eps, scale, shape)
+            return out.view(shape)
         A, b = ops.state_from_prefill(Kn, Vn, planes_T, L, P, scale)          # sum_t pk, sum_t pk^T V
         E = b / (A + eps).unsqueeze(-1)                                          # [N, S, D]
         pq = ops.soft_hash(Qn, planes_T, L, P, scale)                            # [N, T, S] fp32
@@ -45,6 +52,9 @@ class RaceNonCausalFn(Function):
         Qn, Kn, Vn, planes_T, A, b = ctx.saved_tensors
         L, P, eps, scale, shape = ctx.cfg
         dOn = _streams(dO).to(Qn.dtype)
+        if ops.fast_path(Qn.dtype, Qn.shape[-1], L, P):
+            dQ, dK, dV = ops.ace_bwd(Qn, Kn, Vn, dOn, planes_T, A, b, L, P, eps, scale)
+            return dQ.view(shape), dK.view(shape), dV.view(shape), None, None, None, None, None
         den = (A + eps).unsqueeze(-1)
         E = b / den
         _, dE = ops.state_from_prefill(Qn, dOn, planes_T, L, P, scale)        # sum_t pq^T dO

@@ -321,6 +321,44 @@ def state_from_prefill(K, V, planes_T, L, P, logit_scale=None, A0=None, B0=None)
     return A, B
 
 
+def ace_fwd(Q, K, V, planes_T, L, P, eps=1e-6, logit_scale=None):
+    """Non-causal RACE forward on [N,T,D] (tcgen05 path only: bf16, D=64, P=4, L in {8,16}):
+    (out [N,T,D], A [N,S], B [N,S,D]); A and B are the bucket summaries the backward takes."""
+    dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
+    if not fast_path(Q.dtype, D, L, P):
+        raise RuntimeError("race_ace_fwd: bf16, D=64, P=4, L in {8,16} only")
+    out = torch.empty_like(Q)
+    A = torch.empty((N, S), dtype=torch.float32, device=dev)
+    B = torch.empty((N, S, D), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_ACE_FWD, N, T, S, D, L, P, _dtype_code(Q), dev)
+        _lib.check(lib.race_ace_fwd(_ptr(Q), _ptr(K), _ptr(V), _dtype_code(Q), _ptr(planes_T), _ptr(out), _ptr(A),
+                                    _ptr(B), N, T, D, L, P, float(eps), scale, _ptr(ws), nb, _stream(dev)),
+                   "race_ace_fwd")
+    return out, A, B
+
+
+def ace_bwd(Q, K, V, dO, planes_T, A, B, L, P, eps=1e-6, logit_scale=None):
+    """(dQ, dK, dV) [N,T,D] of ace_fwd, from its summaries A, B."""
+    dev, Q, K, V, planes_T, N, T, D, S, scale = _qkv_common(Q, K, V, planes_T, L, P, logit_scale)
+    if not fast_path(Q.dtype, D, L, P):
+        raise RuntimeError("race_ace_bwd: bf16, D=64, P=4, L in {8,16} only")
+    dO = _as_ntd(dO, "dO").to(Q.dtype)
+    _check_cuda(Q, dO, A, B)
+    A = A.float().reshape(N, S).contiguous()
+    B = B.float().reshape(N, S, D).contiguous()
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws, nb = _workspace(_lib.OP_ACE_BWD, N, T, S, D, L, P, _dtype_code(Q), dev)
+        _lib.check(lib.race_ace_bwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(dO), _dtype_code(Q), _ptr(planes_T), _ptr(A),
+                                    _ptr(B), _ptr(dQ), _ptr(dK), _ptr(dV), N, T, D, L, P, float(eps), scale,
+                                    _ptr(ws), nb, _stream(dev)),
+                   "race_ace_bwd")
+    return dQ, dK, dV
+
+
 class FwdSplit:
     """What race_fwd_local leaves for race_fwd_finish: K, V and the workspace."""
 
