@@ -99,7 +99,8 @@ int race_kernel_time(int kernel, double *total_ms, long long *launches);
  * are process-wide and apply to calls made after them, from any thread.
  *
  * race_set_wait_limit: polls before a wait gives up (0 restores the default,
- *   2^26 polls, about a second on a B200).
+ *   2^26 polls, about a second on a B200; waits that sleep between polls, up
+ *   to 1 us each, count each poll as 32).
  * race_set_status_check: 1 makes every later tcgen05-path call wait for its
  *   stream, read the status word and return RACE_ERR_TIMEOUT when a wait gave
  *   up (this synchronises, so not inside stream capture); 0 (the default)

@@ -185,22 +185,24 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 //   control: {PK} Apref -> [APREF] ; {P1M, first group} ; G = P1m Pk, [BST] + dO Bst^T
 //            -> [G] ; {W} dpk = V gBst^T + P1m^T W (in R) ;
 //            {DA} dpk += tril^T dA -> [DPK] ; next group's Bst load and proj -> [PROJ] ;
-//            gA += dA^T 1 ; gB += W^T dO ; Q2 += Pk W^T ; dV (+)= Pk gBst -> [TF]
-//            (last group: also -> [D2]) ;
-// (critical MMAs first in each handoff: the tensor pipe runs them in order)
+//            Q2 += Pk W^T ; dV (+)= Pk gBst -> [PKFREE] (the last readers of the Pk
+//            tile) ; gB += W^T dO ; gA += dA^T 1 (last group: -> [D2]) ;
+// (critical MMAs first in each handoff: the tensor pipe runs them in order; the
+// next group's Pk phase waits only for [PKFREE], not for the state updates)
 //            chunk end: {Q2} dV += Q2m dO -> [OUT] ; next chunk's proj(0) ;
 //            V/dO/Bst refill once every reader completed.
 // P1m and tril are strictly lower triangular: the tau = t terms of Apref, G and
 // dpk (pk_t, P1[t][t] pk_t, dA_t + P1[t][t] W_t) are added by the epilogue in fp32.
-//   epilogue: [PROJ] Pk, plane sigmoids, [TF] gBst and gA suffix copies {PK} ;
-//            [APREF] W {W} ; [G] dA {DA} ; [DPK] dprojK ;
+//   epilogue: [PROJ] Pk, plane sigmoids, [PKFREE] {PK} ;
+//            [APREF] gB suffix copy (bf16 gBst), W {W} ; [G] gA suffix copy, dA {DA} ;
+//            [DPK] dprojK ;
 //            chunk end: [D2] Q2m {Q2} ; [OUT] dV rows {OUTFREE}.
-enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_TF, V3_D2, V3_OUT, V3_TFREE,
+enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_PKFREE, V3_D2, V3_OUT, V3_TFREE,
        V3_FINAL, V3_COUNT };
 // the reverse walk's epilogue layout (see bwd_rev_kernel): 16 warps measured 3 % faster than 8
 // warps of twice the width (fewer warps beside the MMA issuer, but less latency hiding)
 constexpr int REV_TPW = 1;
-enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC };
+enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC, N3_GASYNC };
 constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_ST = 256;
 
 // TPW: tables per epilogue thread per 64-bucket group (1: 16 epilogue warps, 2: 8 epilogue warps
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
     }
     tc::named_bar_sync(N3_INIT, NT);  // planes, tril and suffix state are in place
     if (leader && nch > 0) {
-      ok = tc::mbar_wait(&bars[V3_QK], 0, abort);
+      ok = tc::mbar_wait_sleep(&bars[V3_QK], 0, abort);
       if (ok) {
         tc::tc_fence_after();
         issue_proj(0);
@@ -308,7 +310,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       if (k > 0) tc::named_bar_sync(N3_OUTFREE, NT);  // dK and dV of the previous chunk are out
       ok = ok && !*abort;
       if (leader && ok) {
-        ok = tc::mbar_wait(&bars[V3_VO], k & 1, abort);
+        ok = tc::mbar_wait_sleep(&bars[V3_VO], k & 1, abort);
         if (ok) {
           tc::tc_fence_after();
 #pragma unroll
@@ -343,7 +345,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
                          tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, k0 > 0);
           // (groups after the first: the Bst tile was waited for at the end of the previous
           // group's {DA} step, off this critical path)
-          if (g == 0) ok = tc::mbar_wait(&bars[V3_BST], u & 1, abort);
+          if (g == 0) ok = tc::mbar_wait_sleep(&bars[V3_BST], u & 1, abort);
           if (ok) {
             tc::tc_fence_after();
 #pragma unroll
@@ -374,11 +376,12 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           tc::tc_fence_after();
           // dpk += tril^T dA -> [DPK] ; the next group's chunk-start state (every epilogue
           // thread saw G complete before {DA}, so the Bst tile is free) ; next group's proj ->
-          // [PROJ] ; then gA += dA^T 1, suffix gB += W^T dO, Q2 (in X, summed over the chunk's
-          // groups) += Pk W^T, dV (+)= Pk gBst -> [TF] (the epilogue reads the next group's
-          // suffix states from the gA/gB blocks and rewrites the Pk and gBst tiles after it);
-          // last group: also -> [D2] (every reader of W and dA: the epilogue then overwrites
-          // them with Q2m)
+          // [PROJ] ; Q2 (in X, summed over the chunk's groups) += Pk W^T and dV (+)= Pk gBst,
+          // the last readers of the Pk tile -> [PKFREE] (the next group's Pk phase waits only
+          // for these) ; then suffix gB += W^T dO and gA += dA^T 1 (the epilogue copies group
+          // g+1's gB state after [APREF] and its gA state after [G] of g+1, by when these have
+          // completed) ; last group: -> [D2] (every reader of W and dA: the epilogue then
+          // overwrites them with Q2m)
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + B3_R, tc::desc_mnmajor(sbase + P.tril, k0, TILE),
@@ -389,14 +392,6 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
             issue_proj(g + 1);
           }
 #pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
-                         tc::desc_kmajor(sbase + P.ones, k0, 16 * 128), id_cs, true);
-#pragma unroll
-          for (int k0 = 0; k0 < C; k0 += 16)
-            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
-                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
-#pragma unroll
           for (int k0 = 0; k0 < GW; k0 += 16)
             tc::mma_bf16(tmem + B3_X, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_kmajor(sbase + P.w, k0, 0),
                          id_q2, g > 0 || k0 > 0);
@@ -404,10 +399,18 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           for (int k0 = 0; k0 < GW; k0 += 16)
             tc::mma_bf16(tmem + T_DV, tc::desc_kmajor(sbase + P.pk, k0, 0), tc::desc_mnmajor(sbase + P.gbst, k0, 0),
                          id_dv, g > 0 || k0 > 0);
-          tc::mma_commit(&bars[V3_TF]);
+          tc::mma_commit(&bars[V3_PKFREE]);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(m64_addr(tmem, T_GB, g, 64), tc::desc_mnmajor(sbase + P.w, k0, 0),
+                         tc::desc_mnmajor(sbase + P.o, k0, 0), id_st, true);
+#pragma unroll
+          for (int k0 = 0; k0 < C; k0 += 16)
+            tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
+                         tc::desc_kmajor(sbase + P.ones, k0, 16 * 128), id_cs, true);
           if (g + 1 == NG) tc::mma_commit(&bars[V3_D2]);
           // the next group's Bst tile, loaded above, while the epilogue works on dpk and Pk
-          if (g + 1 < NG) ok = tc::mbar_wait(&bars[V3_BST], (u + 1) & 1, abort);
+          if (g + 1 < NG) ok = tc::mbar_wait_sleep(&bars[V3_BST], (u + 1) & 1, abort);
         }
       }
       tc::named_bar_sync(N3_Q2, NT);
@@ -423,13 +426,13 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       if (leader && ok) {
         tc::mma_commit(&bars[V3_OUT]);  // dV of the chunk complete
         if (k + 1 < nch) {
-          ok = tc::mbar_wait(&bars[V3_QK], (k + 1) & 1, abort);
+          ok = tc::mbar_wait_sleep(&bars[V3_QK], (k + 1) & 1, abort);
           if (ok) {
             tc::tc_fence_after();
             issue_proj(0);
             // V, dO and the Bst tile are free once every MMA issued so far has completed
             tc::mma_commit(&bars[V3_TFREE]);
-            ok = tc::mbar_wait(&bars[V3_TFREE], k & 1, abort);
+            ok = tc::mbar_wait_sleep(&bars[V3_TFREE], k & 1, abort);
             if (ok) {
               load_vo(c - 1);
               load_bst(c - 1, 0);
@@ -508,11 +511,11 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       tc::named_bar_sync(N3_ESYNC, NET);  // sA visible to all epilogue threads
       for (int g = 0; g < NG; ++g) {
         const int u = k * NG + g;
-        // tanh, plane sigmoids of the slot's tables ; 1/(A + eps), then dpq, then the diagonal terms
-        float thK[4 * TPW], thQ[4 * TPW], qK[4 * TPW], qQ[4 * TPW], inv[TB];
-        // ---- Pk ; suffix gB (bf16) and gA copies of group g (once [TF] of the previous group
-        // says the gA/gB blocks are updated and the Pk and gBst tiles read)
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_PROJ], u & 1, abort));
+        // tanh, plane sigmoids of the slot's tables ; 1/(A + eps), then dpq, then the diagonal terms ;
+        // the K-side corner probabilities (unmasked), computed once and used by every phase
+        float thK[4 * TPW], thQ[4 * TPW], qK[4 * TPW], qQ[4 * TPW], inv[TB], pkc[TB];
+        // ---- Pk (once [PKFREE] of the previous group says the Pk tile is read)
+        if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_PROJ], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
           float loK[4 * TPW], loQ[4 * TPW];  // the residual-plane halves
@@ -530,35 +533,20 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           for (int tb = 0; tb < TPW; ++tb) {
             plane_sigmoids(thK + 4 * tb, a.scale, a.poly, qK + 4 * tb);
             plane_sigmoids(thQ + 4 * tb, a.scale, a.poly, qQ + 4 * tb);
+            corner_probs(qK + 4 * tb, pkc + 16 * tb);
           }
         }
-        if (ok && u > 0) ok = tc::warp_all(tc::mbar_wait(&bars[V3_TF], (u - 1) & 1, abort));
+        if (ok && u > 0) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_PKFREE], (u - 1) & 1, abort));
         tc::tc_fence_after();
         if (ok) {
 #pragma unroll
           for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
-            float pr[16], bv[16];
-            tmem_ldn<16>(tmem + lane_off + T_GB + 64 * (g >> 1) + TB * hq + 16 * tb, bv);
-            corner_probs(qK + 4 * tb, pr);
-            if (t >= nt) {
+            float pr[16];
 #pragma unroll
-              for (int i = 0; i < 16; ++i) pr[i] = 0.f;
-            }
+            for (int i = 0; i < 16; ++i) pr[i] = t < nt ? pkc[16 * tb + i] : 0.f;
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch)
               tc::st_row_chunk(sbase + P.pk, t, 2 * (TPW * hq + tb) + ch, pr + 8 * ch);
-            tc::tmem_wait_ld();
-            if (mpar == (g & 1)) {
-#pragma unroll
-              for (int ch = 0; ch < 2; ++ch)
-                tc::st_row_chunk(sbase + P.gbst, mrow, 2 * (TPW * hq + tb) + ch, bv + 8 * ch);
-            }
-          }
-          if (hq == 0) {
-            float av;
-            tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
-            tc::tmem_wait_ld();
-            if (mpar == (g & 1)) sGA[(g & 1) * GW + mrow] = av;
           }
         }
         tc::fence_async_smem();
@@ -568,7 +556,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           // P1m after the first group's Pk: the Pk work overlaps the chunk's V / dO loads and
           // the dO V^T MMA (the control warp takes {PK} before {P1M})
           // ---- P1m = tril-masked dO V^T
-          if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_P1], k & 1, abort));
+          if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_P1], k & 1, abort));
           tc::tc_fence_after();
           if (ok) {
             // 32 columns at a time; column runs all at or above the diagonal store zeros without
@@ -601,24 +589,32 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           tc::tc_fence_before();
           tc::named_bar_arrive(N3_P1M, NT);
         }
-        // sGA (double-buffered by group parity: a warp may write the next group's
-        // copy while a slower one still reads this one), and at the first group the fp32
-        // diagonal, complete before any read
-        tc::named_bar_sync(N3_GSYNC, NET);
-        // ---- W = pq / (A + eps)
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_APREF], u & 1, abort));
+        // at the first group: the fp32 diagonal complete before any read
+        if (g == 0) tc::named_bar_sync(N3_GSYNC, NET);
+        // ---- suffix gB copy of group g (bf16 gBst: the previous group's MMAs, the last readers
+        // of the gBst tile and writers of the gB blocks, completed before Apref) ; W = pq / (A + eps)
+        if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_APREF], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
+#pragma unroll
+          for (int tb = 0; tb < TPW; ++tb) {
+            float bv[16];
+            tmem_ldn<16>(tmem + lane_off + T_GB + 64 * (g >> 1) + TB * hq + 16 * tb, bv);
+            tc::tmem_wait_ld();
+            if (mpar == (g & 1)) {
+#pragma unroll
+              for (int ch = 0; ch < 2; ++ch)
+                tc::st_row_chunk(sbase + P.gbst, mrow, 2 * (TPW * hq + tb) + ch, bv + 8 * ch);
+            }
+          }
 #pragma unroll
           for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
             float ap[16], w[16];
             tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, ap);
             tc::tmem_wait_ld();
             if (t < nt) {  // the MMA summed tau < t: the diagonal pk_t in fp32
-              float pk[16];
-              corner_probs(qK + 4 * tb, pk);
 #pragma unroll
-              for (int i = 0; i < 16; ++i) ap[i] += pk[i];
+              for (int i = 0; i < 16; ++i) ap[i] += pkc[16 * tb + i];
             }
             corner_probs(qQ + 4 * tb, w);
             const int sb = g * GW + TB * hq + 16 * tb;
@@ -639,9 +635,16 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::named_bar_arrive(N3_W, NT);
-        // ---- dA = -W G / (A + eps)
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_G], u & 1, abort));
+        // ---- suffix gA copy of group g ; dA = -W G / (A + eps)
+        if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_G], u & 1, abort));
         tc::tc_fence_after();
+        if (ok && hq == 0) {
+          // (G of this group completed after the previous group's gA update: the block is settled)
+          float av;
+          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
+          tc::tmem_wait_ld();
+          if (mpar == (g & 1)) sGA[(g & 1) * GW + mrow] = av;
+        }
         if (ok) {
           const bool live = t < nt;
           // Exact diagonal (tau = t), in fp32: the MMAs with P1m and tril cover tau < t only.
@@ -652,11 +655,11 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           uint32_t pw[2 * TPW];  // d proj_Q of the slot's tables, bf16 pairs
 #pragma unroll
           for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
-            float G[16], pq[16], pk[16], dpq[16];
+            float G[16], pq[16], dpq[16];
+            const float *pk = pkc + 16 * tb;
             tmem_ldn<16>(tmem + lane_off + B3_GD + TB * hq + 16 * tb, G);
             tc::tmem_wait_ld();
             corner_probs(qQ + 4 * tb, pq);
-            corner_probs(qK + 4 * tb, pk);
             float *iv = inv + 16 * tb;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -686,20 +689,22 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         tc::fence_async_smem();
         tc::tc_fence_before();
         tc::named_bar_arrive(N3_DA, NT);
+        // sGA (double-buffered by group parity: a warp may write the next group's copy while
+        // a slower one still reads this one) complete before any read
+        tc::named_bar_sync(N3_GASYNC, NET);
         // ---- dpk -> d proj_K
-        if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_DPK], u & 1, abort));
+        if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_DPK], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
 #pragma unroll
           for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
-            float dpk[16], pk[16], dp[4];
+            float dpk[16], dp[4];
             tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, dpk);
             tc::tmem_wait_ld();
             add_shared_row<16>(sbase + P.ga + 4 * ((g & 1) * GW + TB * hq + 16 * tb), dpk);  // + suffix gA
 #pragma unroll
             for (int i = 0; i < 16; ++i) dpk[i] += inv[16 * tb + i];  // + the fp32 diagonal term
-            corner_probs(qK + 4 * tb, pk);
-            table_probs_bwd(pk, dpk, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
+            table_probs_bwd(pkc + 16 * tb, dpk, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
             // segment-local d proj_K of table 4g + TPW hq + tb, fp32, to the fix-up (rows past
             // the end too: the chunk's block is read whole)
             *reinterpret_cast<float4 *>(a.dprojK +
@@ -711,7 +716,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       // ---- Q2m[tau = t][t'] = Q2 (summed over the groups) for t' >= tau ; blocks: w (t' < 64),
       // da (t' >= 64), once Q2 and every reader of w and dA completed
       // (32-column runs all below the diagonal store zeros without reading TMEM)
-      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_D2], k & 1, abort));
+      if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_D2], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
 #pragma unroll
@@ -738,7 +743,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       tc::tc_fence_before();
       tc::named_bar_arrive(N3_Q2, NT);
       // ---- dV rows
-      if (ok) ok = tc::warp_all(tc::mbar_wait(&bars[V3_OUT], k & 1, abort));
+      if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_OUT], k & 1, abort));
       tc::tc_fence_after();
       if (ok) {
         float vv[TB];

@@ -45,20 +45,53 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Default poll limit of a bounded wait (about a second on a B200); a launch
-// may carry another one (race_set_wait_limit).
+// Longest time (ns) one sleeping poll may keep its thread suspended before it
+// looks again: the thread sleeps until the phase completes (or this hint runs
+// out) instead of spinning, so it takes no issue slots from the warps it waits
+// for (the MMA-issuing lane shares an SM sub-partition with four epilogue warps).
+constexpr uint32_t kSuspendNs = 1000;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Default poll limit of a bounded wait (about a second of polling on a B200); a
+// launch may carry another limit (race_set_wait_limit).  A sleeping wait counts
+// each of its polls, which last up to kSuspendNs, as kSleepPollWeight polls.
 constexpr uint32_t kDefaultWaitPolls = 1u << 26;
+constexpr uint32_t kSleepPollWeight = 32;
 
 // Bounded wait: returns false (and raises the abort flag) after abort[1]
 // polls, or as soon as another thread has raised the flag.  `abort` points at
 // the CTA's wait-control pair in shared memory, {abort flag, poll limit},
 // which the kernel initialises from its launch arguments before any wait.
-// Never spins forever.
+// Never spins forever.  Short waits: polls without sleeping.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
   const uint32_t limit = (uint32_t)abort[1];
   for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023) == 1023 && *abort) return false;
+  }
+  *abort = 1;
+  return false;
+}
+
+// The same bound, sleeping between polls: for waits that are long next to the
+// work of the warps they wait for (measured faster in the backward reverse
+// walk, slower in the kernels whose waits are short).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  const uint32_t limit = max((uint32_t)abort[1] / kSleepPollWeight, 1u);
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 15) == 15 && *abort) return false;
   }
   *abort = 1;
   return false;
@@ -91,10 +124,10 @@ __device__ __forceinline__ bool warp_sync(uint64_t *bar, uint32_t parity, volati
 }
 
 // Bounded wait that ignores the abort flag: used to drain this thread's own
-// in-flight MMAs before TMEM is released.
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+// in-flight MMAs before TMEM is released (at most about two seconds).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity, uint32_t limit = (1u << 21)) {
   for (uint32_t i = 0; i < limit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
   return false;
 }
 

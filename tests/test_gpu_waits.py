@@ -18,7 +18,7 @@ from conftest import relerr
 
 pytestmark = pytest.mark.gpu
 
-SHORT_WAIT = 1 << 14  # polls: a few milliseconds at most
+SHORT_WAIT = 1 << 14  # polls: well under a millisecond
 
 
 def _inputs(T=300, H=2, L=8, seed=3):
