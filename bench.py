@@ -344,25 +344,33 @@ def run_noncausal(args):
     return 0
 
 
-def decode_kernel_times(model, cfg, B, dev, reps=50):
+def decode_kernel_times(model, cfg, B, dev, reps=48):
     """The two attention kernels of a decode step timed alone, as a CUDA graph of `reps`
-    launches, after the decode run (they overwrite one RACE layer's state and the last cache
+    launches, after the decode run (they overwrite the RACE layers' states and the last cache
     slot of one softmax layer), with their HBM bytes per launch: the RACE decode step reads
     and writes its whole state (A [B*Hkv, S], B [B*Hkv, S, D] fp32), the softmax kernel reads
-    the cached K and V rows."""
+    the cached K and V rows.  The RACE launches cycle through every RACE layer's state, as a
+    decode step does (8 x 34 MB at config 4, more than the L2), so each launch streams its
+    state from HBM instead of finding it in L2."""
     from race_attention_b200 import ops
     hbm, _, src = _peaks()
-    race_layer = next(l for l in model.layers if l.race)
+    race_states = [l.state for l in model.layers if l.race]
     soft_layer = next(l for l in model.layers if not l.race)
     g = torch.Generator(device=dev).manual_seed(3)
     hd, hq, hkv = cfg.hidden // cfg.n_head, cfg.n_head, cfg.n_kv_head
     q = torch.randn(B, hq, hd, device=dev, generator=g).to(torch.bfloat16)
     k = torch.randn(B, hkv, hd, device=dev, generator=g).to(torch.bfloat16)
     v = torch.randn(B, hkv, hd, device=dev, generator=g).to(torch.bfloat16)
-    st = race_layer.state
+    st = race_states[0]
     length = torch.tensor([model.n_tokens - 1], dtype=torch.int32, device=dev)
+    step_no = [0]
+
+    def race_step():
+        race_states[step_no[0] % len(race_states)].step(q, k, v)
+        step_no[0] += 1
+
     runs = {
-        "race_decode_step": (lambda: st.step(q, k, v), 2 * (st.S + st.S * hd) * 4 * B * hkv),
+        "race_decode_step": (race_step, 2 * (st.S + st.S * hd) * 4 * B * hkv),
         "gqa_decode_attn": (lambda: ops.gqa_decode_attention(q, k, v, soft_layer.cache[0], soft_layer.cache[1],
                                                              length, soft_layer.attn_ws, soft_layer.n_splits),
                             B * hkv * model.n_tokens * hd * 2 * 2),
@@ -386,6 +394,7 @@ def decode_kernel_times(model, cfg, B, dev, reps=50):
         del graph
         us = a.elapsed_time(b) / reps * 1e3
         out[name] = {"us_per_launch": us, "hbm_bytes_per_launch": nbytes, "achieved_gbs": nbytes / us / 1e3,
+                     "states_cycled": len(race_states) if name == "race_decode_step" else 1,
                      "frac_of_hbm": nbytes / us / 1e3 / hbm, "peak_gbs": hbm, "peak_source": src,
                      "launches_timed": reps}
     return out

@@ -16,6 +16,7 @@
 #include <initializer_list>
 #include <mutex>
 #include <set>
+#include <type_traits>
 #include <utility>
 #include <vector>
 
@@ -252,7 +253,6 @@ int set_smem(K kernel, size_t bytes) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return fail(RACE_ERR_CUDA, "cudaFuncSetAttribute(%zu B smem): %s", bytes, cudaGetErrorString(e));
   }
-  return RACE_OK;
   return RACE_OK;
 }
 
@@ -1370,8 +1370,41 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype, con
   if (group > race::dec::MAX_GROUP)
     return fail(RACE_ERR_UNSUPPORTED, "query group %lld > %d", (long long)group, race::dec::MAX_GROUP);
   if (D < 1 || D > race::dec::NT) return fail(RACE_ERR_SHAPE, "D=%lld out of range [1,%d]", (long long)D, race::dec::NT);
-  const size_t sm = sizeof(float) * race::dec::smem_floats((int)D, (int)S, (int)(L * P), (int)group);
   cudaStream_t s = as_stream(stream);
+  using bf = __nv_bfloat16;
+  constexpr int MAXG = race::dec::MAX_GROUP;
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (race::dec::d64_eligible((int)D, (int)L, (int)P, (int)group) && al16(q) && al16(k) && al16(v) && al16(out) &&
+      al16(planes_T) && al16(A) && al16(B)) {
+    // head_dim 64, 4 planes per table: the compile-time-shaped kernel (one CTA per kv stream)
+    namespace d6 = race::dec::d64;
+    auto launch64 = [&](auto kernel, auto lay, auto *qq, auto *kk, auto *vv, auto *oo) -> int {
+      const size_t smb = sizeof(float) * (size_t)decltype(lay)::TOTAL;
+      RACE_TRY(set_smem(kernel, smb));
+      RACE_TRY(set_carveout(reinterpret_cast<const void *>(kernel)));
+      kernel<<<(unsigned)Nkv, d6::NT, smb, s>>>(qq, kk, vv, planes_T, A, B, oo, (int)group, eps, logit_scale);
+      return RACE_OK;
+    };
+    auto by_group = [&](auto tag, auto *qq, auto *kk, auto *vv, auto *oo) -> int {
+      using X = std::remove_const_t<std::remove_pointer_t<decltype(qq)>>;
+      constexpr int Lc = decltype(tag)::value;
+      if (group == 1) return launch64(d6::decode_step_d64<X, Lc, 1>, d6::Layout<Lc, 1>{}, qq, kk, vv, oo);
+      if (group == 2) return launch64(d6::decode_step_d64<X, Lc, 2>, d6::Layout<Lc, 2>{}, qq, kk, vv, oo);
+      if (group <= 4) return launch64(d6::decode_step_d64<X, Lc, 4>, d6::Layout<Lc, 4>{}, qq, kk, vv, oo);
+      return launch64(d6::decode_step_d64<X, Lc, 8>, d6::Layout<Lc, 8>{}, qq, kk, vv, oo);
+    };
+    auto by_l = [&](auto *qq, auto *kk, auto *vv, auto *oo) -> int {
+      return L == 8 ? by_group(std::integral_constant<int, 8>{}, qq, kk, vv, oo)
+                    : by_group(std::integral_constant<int, 16>{}, qq, kk, vv, oo);
+    };
+    if (dtype == RACE_F32)
+      RACE_TRY(by_l((const float *)q, (const float *)k, (const float *)v, (float *)out));
+    else
+      RACE_TRY(by_l((const bf *)q, (const bf *)k, (const bf *)v, (bf *)out));
+    RACE_TRY(check_launch("decode_step_d64"));
+    return ok();
+  }
+  const size_t sm = sizeof(float) * race::dec::smem_floats((int)D, (int)S, (int)(L * P), (int)group);
   auto launch = [&](auto kernel, auto *qq, auto *kk, auto *vv, auto *oo) -> int {
     RACE_TRY(set_smem(kernel, sm));
     RACE_TRY(set_carveout(reinterpret_cast<const void *>(kernel)));  // 4 CTAs per SM
@@ -1379,8 +1412,6 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype, con
                                                     (int)P, eps, logit_scale);
     return RACE_OK;
   };
-  using bf = __nv_bfloat16;
-  constexpr int MAXG = race::dec::MAX_GROUP;
   if (dtype == RACE_F32) {
     RACE_TRY(group <= 4 ? launch(race::dec::decode_step<float, 4>, (const float *)q, (const float *)k,
                                  (const float *)v, (float *)out)
