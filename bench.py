@@ -470,6 +470,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per GPU (not a headline number)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-companions", action="store_true")
     args = ap.parse_args()
     if args.config == "cfg5":
         return run_gpt(args)
@@ -575,6 +576,13 @@ def run_ours(args, cfg):
             t.grad = None
         e2e = run_e2e(layer, cfg, dev, world, barrier, args, planes)
 
+    # the library's other hot paths, measured in the same run on one GPU (not part of `value`)
+    comp = None
+    if world == 1 and args.config == "cfg2" and not args.no_companions:
+        del qv, kv, vv, Q, K, V, dO
+        torch.cuda.empty_cache()
+        comp = companions(dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, meta = cpu_reference_sample(cfg, 3, 1)
@@ -586,13 +594,83 @@ def run_ours(args, cfg):
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16" if dtype == torch.bfloat16 else "f32",
                 "data": "synthetic (seeded randn, BASELINE shapes)", "config": config_dict(args, cfg),
-                "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+                "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "companions": comp,
                 "gpu_launches": int(launches), "gpu_launches_per_step": int(launches) // args.steps,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def companions(dev, steps=10, warmup=3):
+    """Two other hot paths of the library, timed with CUDA events after the headline step:
+    the fused non-causal layer (forward + backward, B=8, H=12, T=4096, L=8, bf16, inputs
+    N(0,1)/8, as `--config noncausal`) and the decode step at the hybrid decode shape (64
+    sequences x 8 kv heads, 32 query heads, head_dim 64, L=8, bf16), a CUDA graph of 48
+    launches cycling through 8 layers' states (272 MB, more than the L2) so each launch
+    streams its state from HBM."""
+    import race_attention_b200 as rb
+    from race_attention_b200 import ops
+    hbm, _, src = _peaks()
+    out = {}
+    # non-causal layer
+    B, H, T, D, L, P = 8, 12, 4096, 64, 8, 4
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device=dev, seed=0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, k, v, do = (torch.randn(B, H, T, D, device=dev, generator=g).div_(8).bfloat16() for _ in range(4))
+    leaves = [x.requires_grad_(True) for x in (q, k, v)]
+
+    def nc_step():
+        for x in leaves:
+            x.grad = None
+        rb.race_noncausal(*leaves, planes, L, P).backward(do)
+
+    for _ in range(warmup):
+        nc_step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        nc_step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    nbytes = 11 * D * 2 * B * H * T
+    out["noncausal_layer"] = {"config": "B=8 H=12 T=4096 D=64 L=8 P=4 bf16, fwd+bwd via race_noncausal",
+                              "ms_per_step": ms, "tokens_per_s": B * T / (ms / 1e3),
+                              "layer_bytes_frac_of_hbm": nbytes / (ms / 1e3) / 1e9 / hbm}
+    del q, k, v, do, leaves
+    # decode step
+    nb, hq, hkv, L = 64, 32, 8, 8
+    S = L << P
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device=dev, seed=0)
+    n_states, reps = 8, 48
+    As = [torch.rand(nb * hkv, S, device=dev, generator=g) * 50 for _ in range(n_states)]
+    Bs = [torch.randn(nb * hkv, S, D, device=dev, generator=g) for _ in range(n_states)]
+    qd = torch.randn(nb * hq, D, device=dev, generator=g).bfloat16()
+    kd, vd = (torch.randn(nb * hkv, D, device=dev, generator=g).bfloat16() for _ in range(2))
+    for i in range(n_states):
+        ops.decode_step(qd, kd, vd, planes, As[i], Bs[i], L, P)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for r in range(reps):
+            ops.decode_step(qd, kd, vd, planes, As[r % n_states], Bs[r % n_states], L, P)
+    graph.replay()
+    torch.cuda.synchronize()
+    s.record()
+    graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    del graph
+    us = s.elapsed_time(e) / reps * 1e3
+    nbytes = 2 * (S + S * D) * 4 * nb * hkv
+    out["decode_step"] = {"config": "64 sequences x 8 kv heads (32 query heads), D=64, L=8, P=4, bf16; "
+                                    "48 launches cycling 8 states", "us_per_launch": us,
+                          "hbm_bytes_per_launch": nbytes, "achieved_gbs": nbytes / us / 1e3,
+                          "frac_of_hbm": nbytes / us / 1e3 / hbm, "peak_source": src}
+    return out
 
 
 # Algorithmic HBM bytes per token-head of each tcgen05 kernel (its own inputs and

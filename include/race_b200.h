@@ -68,14 +68,20 @@ const char *race_status_string(int status);
 const char *race_last_error(void);
 
 /* Diagnostic: number of kernel launches this library has issued in this
- * process (host-side counter; used to report launches per benchmark step). */
+ * process (host-side counter; used to report launches per benchmark step).
+ * One process-wide counter: launches from every thread and stream add to it. */
 unsigned long long race_launch_counter(void);
 
 /* Diagnostic (no counterpart in the reference): device time of the tcgen05
  * kernels.  While enabled, CUDA events are recorded on the launch stream
  * around every launch of the kernels below; race_kernel_time() waits for the
  * events recorded so far and returns the totals since the last enable.
- * Enabling clears the totals.  Not for use inside stream capture. */
+ * Enabling clears the totals.  Not for use inside stream capture.  The event
+ * lists and totals are process-wide (one set for all threads, streams and
+ * devices, guarded by a mutex): time one stream at a time, or the totals mix
+ * the launches of every stream that ran while timing was on.  The compute
+ * entry points keep no data between calls (their only shared settings are the
+ * process-wide wait controls below). */
 #define RACE_KT_FWD_TOTALS 0   /* fused K-hash + segment totals / chunk states */
 #define RACE_KT_FWD_READOUT 1  /* forward readout                              */
 #define RACE_KT_BWD_REV 2      /* backward reverse walk (segment-local grads)  */

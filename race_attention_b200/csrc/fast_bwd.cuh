@@ -67,7 +67,7 @@ __device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g
                                                 float scale, float *out4) {
   float gp[16];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) gp[r] = p16[r] * g16[r];
+  for (int r = 0; r < 16; r += 2) st2(gp, r, __fmul2_rn(ld2(p16, r), ld2(g16, r)));
   float a[8], s3 = 0.f;  // plane 3: bit 0
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -84,8 +84,14 @@ __device__ __forceinline__ void table_probs_bwd(const float *p16, const float *g
   const float s0 = b[2] + b[3];  // plane 0: bit 3
   const float c = (b[0] + b[1]) + s0;
   const float set[4] = {s0, s1, s2, s3};
+  const float2 nc = dup2(-c), s2s = dup2(2.f * scale), one = dup2(1.f);
 #pragma unroll
-  for (int p = 0; p < 4; ++p) out4[p] = fmaf(-q4[p], c, set[p]) * (2.f * scale) * fmaf(-th4[p], th4[p], 1.f);
+  for (int p = 0; p < 4; p += 2) {
+    const float2 th = ld2(th4, p);
+    const float2 d = __ffma2_rn(ld2(q4, p), nc, ld2(set, p));               // set_p - q_p c
+    const float2 sech2 = __ffma2_rn(make_float2(-th.x, -th.y), th, one);   // 1 - tanh^2
+    st2(out4, p, __fmul2_rn(__fmul2_rn(d, s2s), sech2));
+  }
 }
 
 
@@ -524,10 +530,12 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
           tmem_ldn<4 * TPW>(tmem + lane_off + B3_GD + 32 + 4 * TPW * hq, thQ);
           tmem_ldn<4 * TPW>(tmem + lane_off + B3_GD + 48 + 4 * TPW * hq, loQ);
           tc::tmem_wait_ld();
+          vadd<4 * TPW>(thK, loK);
+          vadd<4 * TPW>(thQ, loQ);
 #pragma unroll
           for (int i = 0; i < 4 * TPW; ++i) {
-            thK[i] = tanh_fast(thK[i] + loK[i]);
-            thQ[i] = tanh_fast(thQ[i] + loQ[i]);
+            thK[i] = tanh_fast(thK[i]);
+            thQ[i] = tanh_fast(thQ[i]);
           }
 #pragma unroll
           for (int tb = 0; tb < TPW; ++tb) {
@@ -612,10 +620,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
             float ap[16], w[16];
             tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, ap);
             tc::tmem_wait_ld();
-            if (t < nt) {  // the MMA summed tau < t: the diagonal pk_t in fp32
-#pragma unroll
-              for (int i = 0; i < 16; ++i) ap[i] += pkc[16 * tb + i];
-            }
+            if (t < nt) vadd<16>(ap, pkc + 16 * tb);  // the MMA summed tau < t: the diagonal pk_t in fp32
             corner_probs(qQ + 4 * tb, w);
             const int sb = g * GW + TB * hq + 16 * tb;
             add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
@@ -625,8 +630,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
 #pragma unroll
               for (int i = 0; i < 16; ++i) iv[i] = 0.f;
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] *= iv[i];
+            vmul<16>(w, iv);
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch)
               tc::st_row_chunk(sbase + P.w, t, 2 * (TPW * hq + tb) + ch, w + 8 * ch);
@@ -661,14 +665,16 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
             tc::tmem_wait_ld();
             corner_probs(qQ + 4 * tb, pq);
             float *iv = inv + 16 * tb;
+            const float2 p12 = dup2(p1);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float gg = fmaf(p1, pk[i], G[i]);
-              const float w = pq[i] * iv[i];
-              dpq[i] = gg * iv[i];
-              const float da = -w * dpq[i];
-              G[i] = da;
-              iv[i] = fmaf(p1, w, da);  // the diagonal term, carried to the dpk phase
+            for (int i = 0; i < 16; i += 2) {
+              const float2 v = ld2(iv, i);
+              const float2 w = __fmul2_rn(ld2(pq, i), v);
+              const float2 dq = __fmul2_rn(__ffma2_rn(p12, ld2(pk, i), ld2(G, i)), v);
+              const float2 da = __fmul2_rn(make_float2(-w.x, -w.y), dq);
+              st2(dpq, i, dq);
+              st2(G, i, da);
+              st2(iv, i, __ffma2_rn(p12, w, da));  // the diagonal term, carried to the dpk phase
             }
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch)
@@ -702,8 +708,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
             tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, dpk);
             tc::tmem_wait_ld();
             add_shared_row<16>(sbase + P.ga + 4 * ((g & 1) * GW + TB * hq + 16 * tb), dpk);  // + suffix gA
-#pragma unroll
-            for (int i = 0; i < 16; ++i) dpk[i] += inv[16 * tb + i];  // + the fp32 diagonal term
+            vadd<16>(dpk, inv + 16 * tb);  // + the fp32 diagonal term
             table_probs_bwd(pkc + 16 * tb, dpk, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
             // segment-local d proj_K of table 4g + TPW hq + tb, fp32, to the fix-up (rows past
             // the end too: the chunk's block is read whole)

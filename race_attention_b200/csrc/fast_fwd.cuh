@@ -80,27 +80,49 @@ __device__ __forceinline__ float tanh_fast(float x) {
   return y;
 }
 
-// sigma(z) for |z| <= 1/2, from sigma(z) = (1 + tanh(z/2)) / 2 and the odd
-// Taylor series of tanh(w) = w - w^3/3 + 2w^5/15 - 17w^7/315 + 62w^9/2835 - ...
-// truncated after w^9 (|w| <= 1/4: truncation error < 3e-9).  Five FMA-pipe
-// operations instead of an exponential and a reciprocal on the SFU.
-__device__ __forceinline__ float sigmoid_small(float z) {
-  const float w = 0.5f * z, w2 = w * w;
-  float p = fmaf(w2, 62.f / 2835.f, -17.f / 315.f);
-  p = fmaf(p, w2, 2.f / 15.f);
-  p = fmaf(p, w2, -1.f / 3.f);
-  p = fmaf(p, w2, 1.f);
-  return fmaf(0.5f * w, p, 0.5f);
+// ---- packed fp32 pairs: sm_100 issues one FFMA2 / FMUL2 / FADD2 for two independent
+// lanes of element-wise work, halving the epilogues' arithmetic instruction count
+// (round-to-nearest on each lane: bit-identical to the scalar operations)
+__device__ __forceinline__ float2 ld2(const float *v, int i) { return make_float2(v[i], v[i + 1]); }
+__device__ __forceinline__ void st2(float *v, int i, float2 x) {
+  v[i] = x.x;
+  v[i + 1] = x.y;
+}
+__device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
+// a[i] += b[i], a[i] *= b[i] for n (even) values
+template <int n>
+__device__ __forceinline__ void vadd(float *a, const float *b) {
+#pragma unroll
+  for (int i = 0; i < n; i += 2) st2(a, i, __fadd2_rn(ld2(a, i), ld2(b, i)));
+}
+template <int n>
+__device__ __forceinline__ void vmul(float *a, const float *b) {
+#pragma unroll
+  for (int i = 0; i < n; i += 2) st2(a, i, __fmul2_rn(ld2(a, i), ld2(b, i)));
 }
 
-// q_p = sigma(2 * scale * tanh(proj_p)) of one table's 4 planes, from th = tanh(proj).
-// `poly` (host-chosen: 2|scale| <= 1/2, which bounds |z| since |tanh| <= 1)
-// selects the series above; otherwise the SFU exponential.
+// q_p = sigma(z_p), z_p = 2 * scale * tanh(proj_p), of one table's 4 planes, from
+// th = tanh(proj).  `poly` (host-chosen: 2|scale| <= 1/2, which bounds |z| since
+// |tanh| <= 1) selects sigma(z) = (1 + tanh(z/2)) / 2 with the odd Taylor series
+// tanh(w) = w - w^3/3 + 2w^5/15 - 17w^7/315 + 62w^9/2835 - ... truncated after w^9
+// (|w| <= 1/4: truncation error < 3e-9): FMA-pipe operations on pairs of planes
+// instead of an exponential and a reciprocal on the SFU; otherwise the SFU exponential.
 __device__ __forceinline__ void plane_sigmoids(const float *th4, float scale, bool poly, float *q4) {
+  if (poly) {
+    const float2 c9 = dup2(62.f / 2835.f), c7 = dup2(-17.f / 315.f), c5 = dup2(2.f / 15.f), c3 = dup2(-1.f / 3.f);
+    const float2 one = dup2(1.f), half = dup2(0.5f), sc = dup2(scale);
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const float z = 2.f * scale * th4[p];
-    q4[p] = poly ? sigmoid_small(z) : __fdividef(1.f, 1.f + __expf(-z));
+    for (int p = 0; p < 4; p += 2) {
+      const float2 w = __fmul2_rn(sc, ld2(th4, p)), w2 = __fmul2_rn(w, w);
+      float2 q = __ffma2_rn(w2, c9, c7);
+      q = __ffma2_rn(q, w2, c5);
+      q = __ffma2_rn(q, w2, c3);
+      q = __ffma2_rn(q, w2, one);
+      st2(q4, p, __ffma2_rn(__fmul2_rn(half, w), q, half));
+    }
+  } else {
+#pragma unroll
+    for (int p = 0; p < 4; ++p) q4[p] = __fdividef(1.f, 1.f + __expf(-2.f * scale * th4[p]));
   }
 }
 
@@ -167,10 +189,8 @@ __device__ __forceinline__ void add_shared_row(uint32_t addr, float *den) {
 #pragma unroll
   for (int i = 0; i < n; i += 4) {
     const float4 v = tc::ld_shared_f4(addr + 4 * i);
-    den[i] += v.x;
-    den[i + 1] += v.y;
-    den[i + 2] += v.z;
-    den[i + 3] += v.w;
+    st2(den, i, __fadd2_rn(ld2(den, i), make_float2(v.x, v.y)));
+    st2(den, i + 2, __fadd2_rn(ld2(den, i + 2), make_float2(v.z, v.w)));
   }
 }
 
