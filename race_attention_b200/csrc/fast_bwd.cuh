@@ -1072,18 +1072,19 @@ __global__ void __launch_bounds__(NTHR, 1) bwd_fix_kernel(const __grid_constant_
           for (int i = 8; i < 16; ++i) thK[i] = 0.f;
         }
 #pragma unroll
-        for (int tb = 0; tb < 4; ++tb) {
+        for (int tb = 0; tb < 4; tb += 2) {  // tables in pairs (tq is 2 or 4)
           if (tb < tq) {
             plane_sigmoids(thK + 4 * tb, a.scale, a.poly, qK + 4 * tb);
-            float pr[16];
-            corner_probs(qK + 4 * tb, pr);
+            plane_sigmoids(thK + 4 * tb + 4, a.scale, a.poly, qK + 4 * tb + 4);
+            float pr[32];
+            corner_probs2(qK + 4 * tb, qK + 4 * tb + 4, pr, pr + 16);
             if (t >= nt) {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) pr[i] = 0.f;
+              for (int i = 0; i < 32; ++i) pr[i] = 0.f;
             }
-            const int b0 = 16 * (tq * hq + tb);  // first bucket of the table
+            const int b0 = 16 * (tq * hq + tb);  // first bucket of the table pair
 #pragma unroll
-            for (int ch = 0; ch < 2; ++ch)
+            for (int ch = 0; ch < 4; ++ch)
               tc::st_row_chunk(sbase + P.pk + (uint32_t)(b0 >> 6) * TILE, t, ((b0 & 63) >> 3) + ch, pr + 8 * ch);
           }
         }

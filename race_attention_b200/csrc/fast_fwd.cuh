@@ -146,6 +146,35 @@ __device__ __forceinline__ void corner_probs(const float *q, float *p16) {
   }
 }
 
+// corner_probs of two tables at once, table a in the low lane and table b in the high
+// lane of each packed pair (the same products in the same order: bit-identical)
+__device__ __forceinline__ void corner_probs2(const float *qa, const float *qb, float *pa, float *pb) {
+  float2 q[4], nq[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    q[p] = make_float2(qa[p], qb[p]);
+    nq[p] = __ffma2_rn(q[p], dup2(-1.f), dup2(1.f));  // 1 - q
+  }
+  float2 x[4], y[8];
+#pragma unroll
+  for (int b0 = 0; b0 < 2; ++b0)
+#pragma unroll
+    for (int b1 = 0; b1 < 2; ++b1) x[b0 * 2 + b1] = __fmul2_rn(b0 ? q[0] : nq[0], b1 ? q[1] : nq[1]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    y[2 * i] = __fmul2_rn(x[i], nq[2]);
+    y[2 * i + 1] = __fmul2_rn(x[i], q[2]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 lo = __fmul2_rn(y[i], nq[3]), hi = __fmul2_rn(y[i], q[3]);
+    pa[2 * i] = lo.x;
+    pb[2 * i] = lo.y;
+    pa[2 * i + 1] = hi.x;
+    pb[2 * i + 1] = hi.y;
+  }
+}
+
 // corner probabilities of one table straight from its 4 raw projections
 __device__ __forceinline__ void table_probs(const float *proj4, float scale, bool poly, float *p16) {
   float th[4], q[4];
@@ -153,6 +182,20 @@ __device__ __forceinline__ void table_probs(const float *proj4, float scale, boo
   for (int p = 0; p < 4; ++p) th[p] = tanh_fast(proj4[p]);
   plane_sigmoids(th, scale, poly, q);
   corner_probs(q, p16);
+}
+
+// table_probs of two tables (4 projections each), paired as in corner_probs2
+__device__ __forceinline__ void table_probs2(const float *proj_a, const float *proj_b, float scale, bool poly,
+                                             float *pa, float *pb) {
+  float th[8], q[8];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    th[p] = tanh_fast(proj_a[p]);
+    th[4 + p] = tanh_fast(proj_b[p]);
+  }
+  plane_sigmoids(th, scale, poly, q);
+  plane_sigmoids(th + 4, scale, poly, q + 4);
+  corner_probs2(q, q + 4, pa, pb);
 }
 
 // Reciprocals of 4 values with one SFU operation (Montgomery's simultaneous
@@ -488,6 +531,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
           float pj[8], pr[32];
           tc::tmem_ld8(tmem + lane_off + T_PK + j0, pj);
           tc::tmem_wait_ld();
+          // (one table at a time: the two-table packed form measured slower in this kernel)
 #pragma unroll
           for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pr + 16 * i);
           if (t >= nt) {
@@ -520,8 +564,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
           add_shared_row<32>(aCur + 4 * sb, ap);
           if (t == C - 1) store_shared_row<32>(aNxt + 4 * sb, ap);
           rcp_n<32>(ap, ap, a.batch_rcp);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pq[i] *= ap[i];
+          vmul<32>(pq, ap);
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) tc::st_row_chunk(sbase + P.w + blk, t, ch0 + ch, pq + 8 * ch);
         }
@@ -793,8 +836,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           float pj[8];
           tc::tmem_ld8(tmem + lane_off + j0, pj);
           tc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 2; ++i) table_probs(pj + 4 * i, a.scale, a.poly, pr[g] + 16 * i);
+          table_probs2(pj, pj + 4, a.scale, a.poly, pr[g], pr[g] + 16);
           if (t >= nt) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) pr[g][i] = 0.f;

@@ -296,15 +296,16 @@ __global__ void __launch_bounds__(NTHR, 1) ace_tile_kernel(const __grid_constant
           for (int i = 8; i < 16; ++i) th[i] = 0.f;
         }
 #pragma unroll
-        for (int tb = 0; tb < 4; ++tb) {
+        for (int tb = 0; tb < 4; tb += 2) {  // tables in pairs (tq is 2 or 4)
           if (tb < tq) {
             plane_sigmoids(th + 4 * tb, a.scale, a.poly, q + 4 * tb);
+            plane_sigmoids(th + 4 * tb + 4, a.scale, a.poly, q + 4 * tb + 4);
             if (kP) {
-              float pr[16];
-              corner_probs(q + 4 * tb, pr);
-              const int b0 = 16 * (tq * hq + tb);  // first bucket of the table
+              float pr[32];
+              corner_probs2(q + 4 * tb, q + 4 * tb + 4, pr, pr + 16);
+              const int b0 = 16 * (tq * hq + tb);  // first bucket of the table pair
 #pragma unroll
-              for (int ch = 0; ch < 2; ++ch)
+              for (int ch = 0; ch < 4; ++ch)
                 tc::st_row_chunk(sbase + P.pk + (uint32_t)(b0 >> 6) * TILE, t, ((b0 & 63) >> 3) + ch, pr + 8 * ch);
             }
           }
