@@ -205,9 +205,10 @@ __device__ __forceinline__ uint32_t m64_addr(uint32_t tmem, uint32_t col0, int g
 //            chunk end: [D2] Q2m {Q2} ; [OUT] dV rows {OUTFREE}.
 enum { V3_QK = 0, V3_VO, V3_BST, V3_P1, V3_PROJ, V3_APREF, V3_G, V3_DPK, V3_PKFREE, V3_D2, V3_OUT, V3_TFREE,
        V3_FINAL, V3_COUNT };
-// the reverse walk's epilogue layout (see bwd_rev_kernel): 16 warps measured 3 % faster than 8
-// warps of twice the width (fewer warps beside the MMA issuer, but less latency hiding)
-constexpr int REV_TPW = 1;
+// the reverse walk's epilogue layout (see bwd_rev_kernel): 8 warps of two tables each (fewer
+// warps beside the MMA issuer, each phase's TMEM loads batched over both tables) measured 2 %
+// faster than 16 warps of one table once the element-wise work ran on packed pairs
+constexpr int REV_TPW = 2;
 enum { N3_INIT = 1, N3_PK, N3_P1M, N3_W, N3_DA, N3_Q2, N3_OUTFREE, N3_ESYNC, N3_GSYNC, N3_GASYNC };
 constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_ST = 256;
 
@@ -604,37 +605,27 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_APREF], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
+          // both TMEM loads first, the Q-side corner probabilities while they are in flight
+          float bv[TB], ap[TB], w[TB];
+          tmem_ldn<TB>(tmem + lane_off + T_GB + 64 * (g >> 1) + TB * hq, bv);
+          tmem_ldn<TB>(tmem + lane_off + B3_R + TB * hq, ap);
 #pragma unroll
-          for (int tb = 0; tb < TPW; ++tb) {
-            float bv[16];
-            tmem_ldn<16>(tmem + lane_off + T_GB + 64 * (g >> 1) + TB * hq + 16 * tb, bv);
-            tc::tmem_wait_ld();
-            if (mpar == (g & 1)) {
+          for (int tb = 0; tb < TPW; ++tb) corner_probs(qQ + 4 * tb, w + 16 * tb);
+          tc::tmem_wait_ld();
+          if (mpar == (g & 1)) {
 #pragma unroll
-              for (int ch = 0; ch < 2; ++ch)
-                tc::st_row_chunk(sbase + P.gbst, mrow, 2 * (TPW * hq + tb) + ch, bv + 8 * ch);
-            }
+            for (int ch = 0; ch < 2 * TPW; ++ch) tc::st_row_chunk(sbase + P.gbst, mrow, 2 * TPW * hq + ch, bv + 8 * ch);
           }
+          if (t < nt) vadd<TB>(ap, pkc);  // the MMA summed tau < t: the diagonal pk_t in fp32
+          add_shared_row<TB>(sbase + P.a0 + 4 * (g * GW + TB * hq), ap);  // + (A + eps) at chunk start
+          rcp_n<TB>(ap, inv, a.batch_rcp);
+          if (t >= nt) {  // rows past the end: W, dpq, dA and the diagonal terms below all vanish
 #pragma unroll
-          for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
-            float ap[16], w[16];
-            tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, ap);
-            tc::tmem_wait_ld();
-            if (t < nt) vadd<16>(ap, pkc + 16 * tb);  // the MMA summed tau < t: the diagonal pk_t in fp32
-            corner_probs(qQ + 4 * tb, w);
-            const int sb = g * GW + TB * hq + 16 * tb;
-            add_shared_row<16>(sbase + P.a0 + 4 * sb, ap);  // + (A + eps) at chunk start
-            float *iv = inv + 16 * tb;
-            rcp_n<16>(ap, iv, a.batch_rcp);
-            if (t >= nt) {  // rows past the end: W, dpq, dA and the diagonal terms below all vanish
-#pragma unroll
-              for (int i = 0; i < 16; ++i) iv[i] = 0.f;
-            }
-            vmul<16>(w, iv);
-#pragma unroll
-            for (int ch = 0; ch < 2; ++ch)
-              tc::st_row_chunk(sbase + P.w, t, 2 * (TPW * hq + tb) + ch, w + 8 * ch);
+            for (int i = 0; i < TB; ++i) inv[i] = 0.f;
           }
+          vmul<TB>(w, inv);
+#pragma unroll
+          for (int ch = 0; ch < 2 * TPW; ++ch) tc::st_row_chunk(sbase + P.w, t, 2 * TPW * hq + ch, w + 8 * ch);
         }
         tc::fence_async_smem();
         tc::tc_fence_before();
@@ -642,45 +633,44 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         // ---- suffix gA copy of group g ; dA = -W G / (A + eps)
         if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_G], u & 1, abort));
         tc::tc_fence_after();
-        if (ok && hq == 0) {
-          // (G of this group completed after the previous group's gA update: the block is settled)
-          float av;
-          tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
-          tc::tmem_wait_ld();
-          if (mpar == (g & 1)) sGA[(g & 1) * GW + mrow] = av;
-        }
         if (ok) {
           const bool live = t < nt;
           // Exact diagonal (tau = t), in fp32: the MMAs with P1m and tril cover tau < t only.
           // G gets P1[t][t] pk_t ; dpk gets dA_t + P1[t][t] W_t = W_t (P1[t][t] - dpq_t), which
           // cancels exactly at the first tokens (carried to the dpk phase in inv).
           // (rows past the end have inv = 0, so W, dpq, dA and these terms are zero there)
+          // TMEM loads first (G; the gA suffix copy: G of this group completed after the
+          // previous group's gA update, so the block is settled), pq while they are in flight
+          float G[TB], pq[TB], av = 0.f;
+          tmem_ldn<TB>(tmem + lane_off + B3_GD + TB * hq, G);
+          if (hq == 0) tc::tmem_ld1(tmem + lane_off + T_GA + 16 * (g >> 1), av);
+#pragma unroll
+          for (int tb = 0; tb < TPW; ++tb) corner_probs(qQ + 4 * tb, pq + 16 * tb);
+          tc::tmem_wait_ld();
+          if (hq == 0 && mpar == (g & 1)) sGA[(g & 1) * GW + mrow] = av;
           const float p1 = sDiag[t];
+          const float2 p12 = dup2(p1);
           uint32_t pw[2 * TPW];  // d proj_Q of the slot's tables, bf16 pairs
 #pragma unroll
           for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
-            float G[16], pq[16], dpq[16];
+            float dpq[16];
+            float *Gt = G + 16 * tb, *pqt = pq + 16 * tb, *iv = inv + 16 * tb;
             const float *pk = pkc + 16 * tb;
-            tmem_ldn<16>(tmem + lane_off + B3_GD + TB * hq + 16 * tb, G);
-            tc::tmem_wait_ld();
-            corner_probs(qQ + 4 * tb, pq);
-            float *iv = inv + 16 * tb;
-            const float2 p12 = dup2(p1);
 #pragma unroll
             for (int i = 0; i < 16; i += 2) {
               const float2 v = ld2(iv, i);
-              const float2 w = __fmul2_rn(ld2(pq, i), v);
-              const float2 dq = __fmul2_rn(__ffma2_rn(p12, ld2(pk, i), ld2(G, i)), v);
+              const float2 w = __fmul2_rn(ld2(pqt, i), v);
+              const float2 dq = __fmul2_rn(__ffma2_rn(p12, ld2(pk, i), ld2(Gt, i)), v);
               const float2 da = __fmul2_rn(make_float2(-w.x, -w.y), dq);
               st2(dpq, i, dq);
-              st2(G, i, da);
+              st2(Gt, i, da);
               st2(iv, i, __ffma2_rn(p12, w, da));  // the diagonal term, carried to the dpk phase
             }
 #pragma unroll
             for (int ch = 0; ch < 2; ++ch)
-              tc::st_row_chunk(sbase + P.da, t, 2 * (TPW * hq + tb) + ch, G + 8 * ch);
+              tc::st_row_chunk(sbase + P.da, t, 2 * (TPW * hq + tb) + ch, Gt + 8 * ch);
             float dp[4];
-            table_probs_bwd(pq, dpq, qQ + 4 * tb, thQ + 4 * tb, a.scale, dp);
+            table_probs_bwd(pqt, dpq, qQ + 4 * tb, thQ + 4 * tb, a.scale, dp);
             pw[2 * tb] = tc::pack_bf16(dp[0], dp[1]);
             pw[2 * tb + 1] = tc::pack_bf16(dp[2], dp[3]);
           }
@@ -702,14 +692,17 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         if (ok) ok = tc::warp_all(tc::mbar_wait_sleep(&bars[V3_DPK], u & 1, abort));
         tc::tc_fence_after();
         if (ok) {
+          // the TMEM load first, the suffix gA row from shared memory while it is in flight
+          float dpk[TB], ga[TB];
+          tmem_ldn<TB>(tmem + lane_off + B3_R + TB * hq, dpk);
+          load_shared_row<TB>(sbase + P.ga + 4 * ((g & 1) * GW + TB * hq), ga);
+          tc::tmem_wait_ld();
+          vadd<TB>(dpk, ga);   // + suffix gA
+          vadd<TB>(dpk, inv);  // + the fp32 diagonal term
 #pragma unroll
-          for (int tb = 0; tb < TPW; ++tb) {  // one table at a time (registers)
-            float dpk[16], dp[4];
-            tmem_ldn<16>(tmem + lane_off + B3_R + TB * hq + 16 * tb, dpk);
-            tc::tmem_wait_ld();
-            add_shared_row<16>(sbase + P.ga + 4 * ((g & 1) * GW + TB * hq + 16 * tb), dpk);  // + suffix gA
-            vadd<16>(dpk, inv + 16 * tb);  // + the fp32 diagonal term
-            table_probs_bwd(pkc + 16 * tb, dpk, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
+          for (int tb = 0; tb < TPW; ++tb) {
+            float dp[4];
+            table_probs_bwd(pkc + 16 * tb, dpk + 16 * tb, qK + 4 * tb, thK + 4 * tb, a.scale, dp);
             // segment-local d proj_K of table 4g + TPW hq + tb, fp32, to the fix-up (rows past
             // the end too: the chunk's block is read whole)
             *reinterpret_cast<float4 *>(a.dprojK +

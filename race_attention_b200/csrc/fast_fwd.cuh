@@ -237,6 +237,19 @@ __device__ __forceinline__ void add_shared_row(uint32_t addr, float *den) {
   }
 }
 
+// v[i] = A[i] for n (a multiple of 4) consecutive floats of a shared array
+template <int n>
+__device__ __forceinline__ void load_shared_row(uint32_t addr, float *v) {
+#pragma unroll
+  for (int i = 0; i < n; i += 4) {
+    const float4 x = tc::ld_shared_f4(addr + 4 * i);
+    v[i] = x.x;
+    v[i + 1] = x.y;
+    v[i + 2] = x.z;
+    v[i + 3] = x.w;
+  }
+}
+
 template <int n>
 __device__ __forceinline__ void store_shared_row(uint32_t addr, const float *v) {
 #pragma unroll
