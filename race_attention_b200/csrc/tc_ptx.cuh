@@ -316,14 +316,15 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // ---------------------------------------------------------------- MMA
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1.
 //   start: smem byte address; lbo/sbo: byte offsets (multiples of 16).
+//   Built as its two 32-bit words: lo = start >> 4 (bits 0-13) | lbo >> 4 (bits 16-29);
+//   hi = sbo >> 4 (bits 32-45) | version 1 (bit 46) | SWIZZLE_128B (bits 61-63), a constant
+//   for a given sbo.
+__host__ __device__ constexpr uint32_t sdesc_hi(uint32_t sbo) {
+  return ((sbo >> 4) & 0x3FFF) | (1u << 14) | (2u << 29);
+}
 __device__ __forceinline__ uint64_t sdesc(uint32_t start, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((start >> 4) & 0x3FFF);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;  // descriptor version (sm100)
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
-  return d;
+  const uint32_t lo = ((start >> 4) & 0x3FFF) | (((lbo >> 4) & 0x3FFF) << 16);
+  return ((uint64_t)sdesc_hi(sbo) << 32) | lo;
 }
 
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulation.
@@ -411,17 +412,23 @@ __device__ __forceinline__ void st_row_half(uint32_t tile, int row, int chunk16,
 }
 
 // Operand descriptors for the layouts above.
+// The start-address field is the low 14 bits, address >> 4, and shared addresses
+// stay below 2^18 (tile bases and offsets are multiples of 16): a byte offset from
+// `base` enters as offset >> 4 added to the low word, which never carries out of the
+// field.  The high word is a compile-time constant and the low word's base part is
+// loop-invariant, so with k0 a compile-time constant each K step costs the issuing
+// thread one 32-bit add.  (That thread issues every MMA of the CTA alone: each
+// dependent integer instruction in front of an MMA delays it, and a 64-bit rebuild of
+// the descriptor per MMA measured about 3x slower issue than precomputed words.)
 //   K-major (rows = M or N, 64-wide column blocks along K), K step k0 (multiple of 16):
-// (The start-address field is the low 14 bits, address >> 4, and shared
-// addresses stay below 2^18: a byte offset from `base` is added to the
-// descriptor as offset >> 4, so with k0 a compile-time constant each step is
-// one add on a loop-invariant descriptor.)
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int k0, uint32_t block_bytes) {
-  return sdesc(base, 16, 1024) + (uint64_t)(((uint32_t)(k0 >> 6) * block_bytes + (uint32_t)(k0 & 63) * 2) >> 4);
+  const uint32_t lo = ((base >> 4) | (1u << 16)) + (((uint32_t)(k0 >> 6) * block_bytes + (uint32_t)(k0 & 63) * 2) >> 4);
+  return ((uint64_t)sdesc_hi(1024) << 32) | lo;
 }
 //   MN-major (rows = K, 64-wide column blocks along M/N), K step k0 (multiple of 16):
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int k0, uint32_t block_bytes) {
-  return sdesc(base, block_bytes, 1024) + (uint64_t)(((uint32_t)k0 * 128) >> 4);
+  const uint32_t lo = ((base >> 4) | ((block_bytes >> 4) << 16)) + (uint32_t)k0 * 8;
+  return ((uint64_t)sdesc_hi(1024) << 32) | lo;
 }
 
 }  // namespace tc
