@@ -768,16 +768,46 @@ def roofline(kernels, cfg, ms, fwd_ms, bwd_ms):
     return roof
 
 
+def _gpu_cpus(dev):
+    """The host CPUs NVML reports as local to this GPU (its NUMA node), or None."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(dev.index if dev.index is not None else 0)
+        ncpu = os.cpu_count() or 1
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (ncpu + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
+
+
+def _pin_to_gpu_cpus(dev):
+    """Restrict this process to the GPU's local CPUs; returns the previous set (None if
+    nothing changed)."""
+    cpus = _gpu_cpus(dev)
+    if not cpus:
+        return None
+    before = os.sched_getaffinity(0)
+    if cpus == before:
+        return None
+    os.sched_setaffinity(0, cpus)
+    return before
+
+
 def run_e2e(layer, cfg, dev, world, barrier, args, planes):
     """The step through the public autograd API with every step's inputs copied in
     from pinned host memory and its results (out, dQ, dK, dV) copied back, as a
     training loop with a prefetching loader runs it: step i+1's inputs go up on one
     copy stream and step i-1's results come down on another while step i computes
-    (two device input slots; each copy waits only for what it overwrites or reads)."""
+    (two device input slots; each copy waits only for what it overwrites or reads).  The host
+    side runs on the GPU's local CPUs while its pinned buffers are allocated and used, as a
+    NUMA-aware loader does."""
     B, H, T, D, L, P, dtype, scale = cfg
     # long enough that the pipeline's one-time fill (first inputs up) and drain (last
     # results down) weigh little, as in a training loop; they stay inside the timed region
-    steps = max(4, min(16, 2 * args.steps))
+    steps = max(4, min(24, 3 * args.steps))
     nbytes = B * H * T * D * torch.tensor([], dtype=dtype).element_size()
     # device memory of the pipeline: two input slots of four tensors, four results for each
     # of two steps in flight, the layer's own saved states and workspace (about three more)
@@ -793,6 +823,10 @@ def run_e2e(layer, cfg, dev, world, barrier, args, planes):
         return {"value": None, "unit": "tokens/s", "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
                 "skipped": f"the copy pipeline needs about {need / 2**30:.0f} GiB of device memory, "
                            f"{free / 2**30:.0f} GiB free: this configuration has no end-to-end line on one GPU"}
+    # the host side of the pipeline on the CPUs next to this GPU, so its pinned buffers are
+    # allocated (first touch) on the GPU's own NUMA node; restored afterwards
+    saved_affinity = _pin_to_gpu_cpus(dev)
+    host_cpus = len(os.sched_getaffinity(0))
     host_in = [torch.empty((B, H, T, D), dtype=dtype, pin_memory=True) for _ in range(4)]
     host_out = [torch.empty((B, H, T, D), dtype=dtype, pin_memory=True) for _ in range(4)]
     g = torch.Generator().manual_seed(7)
@@ -855,6 +889,9 @@ def run_e2e(layer, cfg, dev, world, barrier, args, planes):
     e.record(main)
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / steps
+    del host_in, host_out, slots
+    if saved_affinity is not None:
+        os.sched_setaffinity(0, saved_affinity)
     if world > 1:
         import torch.distributed as dist
         t = torch.tensor([ms], device=dev)
@@ -862,6 +899,7 @@ def run_e2e(layer, cfg, dev, world, barrier, args, planes):
         ms = float(t.item())
     return {"value": B * T * world / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": 4 * nbytes,
             "d2h_bytes_per_step": 4 * nbytes, "ms_per_step": ms, "steps": steps,
+            "host_cpus": host_cpus,
             "api": "race_attention_b200.race_causal (autograd) from pinned host tensors; next step's H2D and "
                    "previous step's D2H on copy streams overlap this step's compute (fill and drain timed)"}
 
