@@ -345,14 +345,14 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
         }
         if (leader && ok) {
           tc::tc_fence_after();
-          // G = P1m Pk (needs only this group's Pk) + dO Bst^T once the state tile is in
+          // G = P1m Pk (needs only this group's Pk) + dO Bst^T once the state tile is in (the
+          // load, issued at the previous group's {DA} step, is waited for only here, after
+          // Apref and P1m Pk are queued: waiting for it before {PK} held the next Apref back)
 #pragma unroll
           for (int k0 = 0; k0 < C; k0 += 16)
             tc::mma_bf16(tmem + B3_GD, tc::desc_kmajor(sbase + P.p1m, k0, TILE),
                          tc::desc_mnmajor(sbase + P.pk, k0, 0), id_gm, k0 > 0);
-          // (groups after the first: the Bst tile was waited for at the end of the previous
-          // group's {DA} step, off this critical path)
-          if (g == 0) ok = tc::mbar_wait_sleep(&bars[V3_BST], u & 1, abort);
+          ok = tc::mbar_wait_sleep(&bars[V3_BST], u & 1, abort);
           if (ok) {
             tc::tc_fence_after();
 #pragma unroll
@@ -416,8 +416,6 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
             tc::mma_bf16(m64_addr(tmem, T_GA, g, 16), tc::desc_mnmajor(sbase + P.da, k0, 0),
                          tc::desc_kmajor(sbase + P.ones, k0, 16 * 128), id_cs, true);
           if (g + 1 == NG) tc::mma_commit(&bars[V3_D2]);
-          // the next group's Bst tile, loaded above, while the epilogue works on dpk and Pk
-          if (g + 1 < NG) ok = tc::mbar_wait_sleep(&bars[V3_BST], (u + 1) & 1, abort);
         }
       }
       tc::named_bar_sync(N3_Q2, NT);
