@@ -221,6 +221,7 @@ def run_gpt(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        _nccl_init_log()
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     cfg = GPTConfig()
     B, T = 8, args.tokens or 16384
@@ -503,6 +504,7 @@ def run_ours(args, cfg):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        _nccl_init_log()
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     B, H, T, D, L, P, dtype, scale = cfg
     planes, _ = rb.build_planes_protos(D, P, L, 1, device=dev, seed=0)
@@ -766,6 +768,14 @@ def roofline(kernels, cfg, ms, fwd_ms, bwd_ms):
                  "traffic": _ncu_traffic(k, th), "ms_per_launch": fast[k]["ms_per_launch"],
                  "mma_issued_tflops": mma_tflops, "mma_frac_of_bf16_peak": mma_tflops / tc})
     return roof
+
+
+def _nccl_init_log():
+    """NCCL's own communicator log for multi-GPU runs (unless the caller chose otherwise): its
+    INIT lines state each communicator's rank count, so a run record shows how many ranks the
+    exchange really spanned."""
+    os.environ.setdefault("NCCL_DEBUG", "INFO")
+    os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
 
 
 def _gpu_cpus(dev):
