@@ -238,7 +238,9 @@ int race_state_from_prefill(const void *K, const void *V, int dtype,
 /* One fused decode step for a batch of single tokens with grouped-query
  * sharing: q[Nq,D], k/v[Nkv,D] (Nq = Nkv*group, q head i reads kv stream
  * i/group).  Updates the persistent state A[Nkv,S], B[Nkv,S,D] in place with
- * this token's key, then writes out[Nq,D] = row t of the layer output. */
+ * this token's key, then writes out[Nq,D] = row t of the layer output.
+ * A and B must be 16-byte aligned (the state streams in by 16-byte copies;
+ * otherwise RACE_ERR_ALIGN, nothing launched). */
 int race_decode_step(const void *q, const void *k, const void *v, int dtype,
                      const float *planes_T, float *A, float *B, void *out,
                      int64_t Nq, int64_t Nkv, int64_t D, int64_t L, int64_t P,

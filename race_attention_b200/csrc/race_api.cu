@@ -1370,10 +1370,12 @@ int race_decode_step(const void *q, const void *k, const void *v, int dtype, con
   if (group > race::dec::MAX_GROUP)
     return fail(RACE_ERR_UNSUPPORTED, "query group %lld > %d", (long long)group, race::dec::MAX_GROUP);
   if (D < 1 || D > race::dec::NT) return fail(RACE_ERR_SHAPE, "D=%lld out of range [1,%d]", (long long)D, race::dec::NT);
+  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  // both kernels copy the state rows 16 bytes at a time
+  if (!al16(A) || !al16(B)) return fail(RACE_ERR_ALIGN, "decode state A and B must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   using bf = __nv_bfloat16;
   constexpr int MAXG = race::dec::MAX_GROUP;
-  auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (race::dec::d64_eligible((int)D, (int)L, (int)P, (int)group) && al16(q) && al16(k) && al16(v) && al16(out) &&
       al16(planes_T) && al16(A) && al16(B)) {
     // head_dim 64, 4 planes per table: the compile-time-shaped kernel (one CTA per kv stream)

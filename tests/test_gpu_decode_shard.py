@@ -36,6 +36,44 @@ def test_prefill_then_decode(dtype, tol, Hq, Hkv):
     assert st.tokens == T
 
 
+@pytest.mark.parametrize("L", [8, 16])
+@pytest.mark.parametrize("Hq,Hkv", [(4, 4), (8, 4), (12, 4), (16, 2)])
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
+def test_decode_d64_tables_and_groups(L, Hq, Hkv, dtype, tol):
+    """The compile-time-shaped decode kernel (head_dim 64, 4 planes) at 8 and 16 tables and
+    query groups 1, 2, 3 (a group below the kernel's width) and 8, against the oracle's rows."""
+    import race_attention_b200 as rb
+    B, T0, steps, D, P = 2, 24, 4, 64, 4
+    g = torch.Generator().manual_seed(100 * L + 10 * Hq + Hkv)
+    T = T0 + steps
+    Q = torch.randn(B, Hq, T, D, generator=g).to(dtype)
+    K = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    V = torch.randn(B, Hkv, T, D, generator=g).to(dtype)
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device="cpu", seed=2)
+    grp = Hq // Hkv
+    ref, _, _ = O.race_qkv_fwd(Q, K.repeat_interleave(grp, 1), V.repeat_interleave(grp, 1), planes, L, P)
+    ref = ref.reshape(B, Hq, T, D)
+    _, st = rb.prefill_with_state(Q[:, :, :T0].cuda(), K[:, :, :T0].cuda(), V[:, :, :T0].cuda(), planes.cuda(), L, P)
+    for t in range(T0, T):
+        o = st.step(Q[:, :, t].cuda(), K[:, :, t].cuda(), V[:, :, t].cuda())
+        assert relerr(o, ref[:, :, t]) < tol, (t, relerr(o, ref[:, :, t]))
+
+
+def test_decode_rejects_misaligned_state():
+    """A state buffer that is contiguous but not 16-byte aligned (a view one float into an
+    allocation) is refused on the host before anything is launched."""
+    import race_attention_b200 as rb
+    Nkv, S, D, L, P = 4, 128, 64, 8, 4
+    planes, _ = rb.build_planes_protos(D, P, L, 1, device="cuda", seed=0)
+    A = torch.zeros(Nkv * S + 1, device="cuda")[1:].view(Nkv, S)
+    B = torch.zeros(Nkv, S, D, device="cuda")
+    q = torch.randn(Nkv, D, device="cuda")
+    assert A.is_contiguous() and A.data_ptr() % 16 != 0
+    with pytest.raises(RuntimeError, match="aligned"):
+        rb.ops.decode_step(q, q, q, planes, A, B, L, P)
+    torch.cuda.synchronize()  # the context is still healthy
+
+
 @pytest.mark.parametrize("D,Hq,Hkv,L,P", [(30, 16, 2, 4, 3), (32, 12, 2, 4, 3), (64, 10, 2, 8, 4)])
 def test_decode_generic_shapes(D, Hq, Hkv, L, P):
     """Decode steps for head dims off the float4 path (D % 4 != 0) and query groups above
