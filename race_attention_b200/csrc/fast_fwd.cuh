@@ -655,23 +655,25 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_readout_kernel(const __grid_const
 // A + eps in fp32 and B in bf16, the operands of the backward's reverse walk --
 // and writes no record.
 struct TotSmem {
-  uint32_t k, v, pk, ones, planes, bars, total;  // k, v: 2 stages of TILE bytes each
+  uint32_t k, v, pk, planes, bars, total;  // k: 2 stages of TILE bytes; v: 2 stages of [V | ones]
 };
 
 __host__ __device__ __forceinline__ TotSmem tot_smem_plan(int ngroups, int LP) {
   TotSmem m;
   uint32_t o = 0;
   m.k = o; o += 2 * TILE;
-  m.v = o; o += 2 * TILE;
+  m.v = o; o += 4 * TILE;  // stage st: V tile at v + 2 st TILE, a ones block right after it
   m.pk = o; o += (uint32_t)ngroups * 2 * TILE;
-  m.ones = o; o += TILE;
   m.planes = o; o += (uint32_t)align_up((size_t)LP * 128, 1024);
   m.bars = o; o += 256;
   m.total = o + 1024;
   return m;
 }
 
-// TMEM map of the totals kernel (256 columns): projK 0..63, Bstate g at 64+64g, A at 192 + 16g
+// TMEM map of the totals kernel (256 columns): projK 0..63; group g's sums at 64 + 80 g: Bstate
+// (64 columns) then A (16 identical columns), one N = 80 accumulator: the B operand is the V
+// stage and the ones block after it (MN-major 64-column blocks), so Pk^T [V | 1] gives both
+// sums with one MMA per K step
 enum { TB_FULL0 = 0, TB_FULL1, TB_PROJ, TB_PK, TB_DONE, TB_FINAL, TB_INIT, TB_COUNT };
 
 __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_constant__ CUtensorMap tmK,
@@ -720,11 +722,10 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       for (int c = a.withhold_first_load ? 2 : 0; c < 2 && c < nch; ++c) {
         tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + c], 2 * TILE);
         tc::tma_load_4d(sm + P.k + c * TILE, &tmK, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
-        tc::tma_load_4d(sm + P.v + c * TILE, &tmV, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
+        tc::tma_load_4d(sm + P.v + 2 * c * TILE, &tmV, &bars[TB_FULL0 + c], 0, hn, (c_begin + c) * C, bn);
       }
       const uint32_t id_proj = tc::idesc_bf16(C, a.LP, false, false);
-      const uint32_t id_bupd = tc::idesc_bf16(GB, HD, true, true);
-      const uint32_t id_ones = tc::idesc_bf16(GB, 16, true, true);
+      const uint32_t id_sums = tc::idesc_bf16(GB, HD + 16, true, true);
       auto issue_proj = [&](int st) {
         for (int k0 = 0; k0 < HD; k0 += 16)
           tc::mma_bf16(tmem + 0, tc::desc_kmajor(sbase + P.k + st * TILE, k0, TILE),
@@ -756,9 +757,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           const uint32_t pk = sbase + P.pk + (uint32_t)g * 2 * TILE;
           for (int k0 = 0; k0 < C; k0 += 16) {
             const uint64_t ap = tc::desc_mnmajor(pk, k0, TILE);
-            tc::mma_bf16(tmem + 64 + 64 * g, ap, tc::desc_mnmajor(sbase + P.v + st * TILE, k0, TILE), id_bupd,
-                         states || c > 0 || k0 > 0);
-            tc::mma_bf16(tmem + 192 + 16 * g, ap, tc::desc_mnmajor(sbase + P.ones, k0, TILE), id_ones,
+            tc::mma_bf16(tmem + 64 + 80 * g, ap, tc::desc_mnmajor(sbase + P.v + 2 * st * TILE, k0, TILE), id_sums,
                          states || c > 0 || k0 > 0);
           }
         }
@@ -769,7 +768,7 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
           tc::mbar_arrive_expect_tx(&bars[TB_FULL0 + st], 2 * TILE);
           tc::tma_load_4d(sm + P.k + st * TILE, &tmK, &bars[TB_FULL0 + st], 0, hn, (c_begin + c + 2) * C,
                           bn);
-          tc::tma_load_4d(sm + P.v + st * TILE, &tmV, &bars[TB_FULL0 + st], 0, hn, (c_begin + c + 2) * C,
+          tc::tma_load_4d(sm + P.v + 2 * st * TILE, &tmV, &bars[TB_FULL0 + st], 0, hn, (c_begin + c + 2) * C,
                           bn);
         }
       }
@@ -791,7 +790,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
       for (int ch = 2 * hq; ch < 2 * hq + 2; ++ch) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = (ch * 8 + e) < 16 ? 1.f : 0.f;
-        tc::st_row_chunk(sbase + P.ones, t, ch, v);
+        tc::st_row_chunk(sbase + P.v + TILE, t, ch, v);      // after V stage 0
+        tc::st_row_chunk(sbase + P.v + 3 * TILE, t, ch, v);  // after V stage 1
       }
     }
     if (states) {  // segment-start state into the accumulators (lane t = bucket t of group g)
@@ -801,8 +801,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
         const float *src = st0 + S + (size_t)(g * GB + t) * HD + 16 * hq;
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = src[i];
-        tc::tmem_st16(tmem + lane_off + 64 + 64 * g + 16 * hq, v);
-        if (hq == 0) tc::tmem_st1(tmem + lane_off + 192 + 16 * g, st0[g * GB + t]);
+        tc::tmem_st16(tmem + lane_off + 64 + 80 * g + 16 * hq, v);
+        if (hq == 0) tc::tmem_st1(tmem + lane_off + 128 + 80 * g, st0[g * GB + t]);
       }
       tc::tmem_wait_st();
     }
@@ -823,8 +823,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
         const int cg = c_begin + c;
         for (int g = 0; g < a.ngroups; ++g) {
           float bv[16], av;
-          tc::tmem_ld16(tmem + lane_off + 64 + 64 * g + 16 * hq, bv);
-          tc::tmem_ld1(tmem + lane_off + 192 + 16 * g, av);
+          tc::tmem_ld16(tmem + lane_off + 64 + 80 * g + 16 * hq, bv);
+          tc::tmem_ld1(tmem + lane_off + 128 + 80 * g, av);
           tc::tmem_wait_ld();
           const size_t row = ((size_t)n * a.nchunks + cg) * S + g * GB + t;
 #pragma unroll
@@ -880,8 +880,8 @@ __global__ void __launch_bounds__(NTHR, 1) fwd_totals_kernel(const __grid_consta
     if (ok && !states) {
       for (int g = 0; g < a.ngroups; ++g) {
         float bv[16], av;
-        tc::tmem_ld16(tmem + lane_off + 64 + 64 * g + 16 * hq, bv);
-        tc::tmem_ld1(tmem + lane_off + 192 + 16 * g, av);
+        tc::tmem_ld16(tmem + lane_off + 64 + 80 * g + 16 * hq, bv);
+        tc::tmem_ld1(tmem + lane_off + 128 + 80 * g, av);
         tc::tmem_wait_ld();
         float *dst = rec + S + (size_t)(g * GB + t) * HD + 16 * hq;
 #pragma unroll
