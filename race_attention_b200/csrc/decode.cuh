@@ -243,9 +243,11 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16 *dst, const 
 // instruction issue (about 16 K warp instructions per kv stream, most of them index
 // arithmetic with run-time divisors and per-element reloads); this one keeps to the
 // work itself:
-//   * all global reads at kernel start: planes and A by cp.async (group 0), the
-//     stream's B state by cp.async (group 1, awaited only before the update), the
-//     key / query rows and v through registers;
+//   * all global reads at kernel start: planes and A by cp.async (group 0); the
+//     stream's B state by cp.async, each thread copying exactly the row chunks it
+//     updates, in four groups awaited one by one during the update (the first rows are
+//     updated and stored while the later ones arrive); the key / query rows and v
+//     through registers;
 //   * projections: thread (plane j, dim range) over all 1 + group rows, x read as
 //     float4 broadcasts; partial sums combined in shared memory;
 //   * one pass per bucket s (thread s): pk[s], the queries' corner probabilities,
