@@ -214,15 +214,27 @@ constexpr uint32_t B3_X = 0, B3_R = 128, B3_GD = 192, B3_ST = 256;
 
 // TPW: tables per epilogue thread per 64-bucket group (1: 16 epilogue warps, 2: 8 epilogue warps
 // and twice the registers per thread -- two warps beside the MMA issuer on its SM
-// sub-partition instead of four, and each thread's work twice as wide)
+// sub-partition instead of four, and each thread's work twice as wide).
+// With TPW = 2 the block is three warpgroups: two of epilogue warps and a control warpgroup
+// (the MMA / TMA issuer and three warps that only take the block's first and last barriers).
+// Launched at 168 registers a thread (the limit of 384 threads on one SM), the control
+// warpgroup drops to REV_CTL_REGS and the epilogue warps rise to REV_EPI_REGS:
+// 4 x 128 + 8 x 184 = 1984 <= 12 x 168 = 2016 registers a lane for the block, and on each SM
+// sub-partition (two epilogue warps, one control warp) 2 x 184 + 128 = 496 <= 512.
+constexpr int REV_CTL_REGS = 128, REV_EPI_REGS = 184;
 template <int TPW>
-__global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ? 96 : 224) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
+constexpr int rev_block_threads() { return TPW == 2 ? 32 * (16 / TPW + 4) : 32 * (16 / TPW + 1); }
+static_assert(4 * REV_CTL_REGS + 8 * REV_EPI_REGS <= 12 * 168 && 2 * REV_EPI_REGS + REV_CTL_REGS <= 512,
+              "reverse walk register split exceeds the block's launch registers");
+template <int TPW>
+__global__ void __launch_bounds__(rev_block_threads<TPW>(), 1) __maxnreg__(TPW == 1 ? 96 : 168) bwd_rev_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                                         const __grid_constant__ CUtensorMap tmK,
                                                                         const __grid_constant__ CUtensorMap tmV,
                                                                         const __grid_constant__ CUtensorMap tmO,
                                                                         const __grid_constant__ CUtensorMap tmB,
                                                                         BwdArgs a) {
-  constexpr int NE = 16 / TPW, NT = 32 * (NE + 1), NET = 32 * NE;  // epilogue warps, threads
+  // epilogue warps; threads of the named barriers (epilogue + issuer), of the epilogue
+  constexpr int NE = 16 / TPW, NT = 32 * (NE + 1), NET = 32 * NE;
   extern __shared__ __align__(1024) unsigned char smraw[];
   unsigned char *sm = (unsigned char *)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   const BwdSmem P = bwd_smem_plan(a.LP, a.S);
@@ -253,6 +265,12 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
   tc::tc_fence_after();
   const uint32_t tmem = s_tmem;
   volatile int *abort = s_abort;
+  if constexpr (TPW == 2) {  // whole warpgroups: warps 0-7 epilogue, 8-11 control
+    if (warp < NE)
+      tc::setmaxnreg_inc<REV_EPI_REGS>();
+    else
+      tc::setmaxnreg_dec<REV_CTL_REGS>();
+  }
 
   if (warp == NE) {
     // ===================== control warp: named-barrier steps as a warp, TMA + MMA issue by lane 0
@@ -451,7 +469,7 @@ __global__ void __launch_bounds__(32 * (16 / TPW + 1), 1) __maxnreg__(TPW == 1 ?
       if (!tc::mbar_wait_drain(&bars[V3_FINAL], 0)) atomicExch(a.err, 2);
     }
     __syncwarp();
-  } else {
+  } else if (warp < NE) {
     // ============================== epilogue warps: row t, column slot hq
     // (NE = 16/TPW warps, four per TMEM lane quarter; in a 64-bucket group slot hq owns
     // tables 4g + TPW hq + [0, TPW): buckets and d columns [TB hq, TB hq + TB), TB = 16 TPW;

@@ -629,7 +629,7 @@ int fast_backward(const void *Q, const void *K, const void *V, const void *dO, c
     RACE_TRY(set_smem(fk::bwd_rev_kernel<fk::REV_TPW>, rs.total));
     {
       KernelScope ks(RACE_KT_BWD_REV, s);
-      fk::bwd_rev_kernel<fk::REV_TPW><<<grid, 32 * (16 / fk::REV_TPW + 1), rs.total, s>>>(mQ, mK, mV, mO, mB, b);
+      fk::bwd_rev_kernel<fk::REV_TPW><<<grid, fk::rev_block_threads<fk::REV_TPW>(), rs.total, s>>>(mQ, mK, mV, mO, mB, b);
       ks.stop();
     }
     RACE_TRY(check_launch("fast bwd_rev"));

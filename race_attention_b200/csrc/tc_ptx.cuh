@@ -142,6 +142,21 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Per-thread register limit of a whole warpgroup (all four warps execute the same
+// instruction).  A decrease returns registers to the block's pool, an increase takes them
+// from it and waits until they are there: the increases a block makes must never exceed
+// what it was launched with (threads x registers per thread) less what stays in use.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg: 24..256, a multiple of 8");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  static_assert(N % 8 == 0 && N >= 24 && N <= 256, "setmaxnreg: 24..256, a multiple of 8");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Non-blocking arrival on a named barrier (producer side of a bar.sync).
 // Arrivals count whole warps; the warp must be converged.
 __device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
